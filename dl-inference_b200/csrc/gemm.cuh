@@ -1,0 +1,42 @@
+// Internal GEMM interface shared by linear, matmul and conv2d.
+#pragma once
+
+#include "common.cuh"
+
+namespace dli_sm100 {
+
+// Output mapping of the TN GEMM D[i, j] = sum_k A[i, k] * B[j, k].
+enum GemmEpilogue : int {
+  kEpiRowMajor = 0,   // out[i * ldo + j], bias[j]           (A = activations, B = weights)
+  kEpiTransposed = 1, // out[j * ldo + i], bias[i]           (swap-AB: A = weights, B = activations)
+  kEpiNchw = 2,       // i = img * ohw + pix, j = channel -> out[(img * OC + j) * ohw + pix], bias[j]
+};
+
+struct GemmPlan {
+  int bn = 0;             // tile width along j (tcgen05 N)
+  int stages = 0;
+  int tiles_i = 0, tiles_j = 0;
+  int splits = 1;
+  int kblocks = 0, kblocks_per_split = 0;
+  bool tcgen05 = false;   // false -> SIMT fallback
+  size_t workspace = 0;   // bytes of split-K scratch (partials + tile counters)
+};
+
+// Plans a TN GEMM with rows_a x K and rows_b x K operands.
+GemmPlan plan_tn_gemm(int64_t rows_a, int64_t rows_b, int64_t k, dli_dtype dtype, bool allow_split);
+
+// Runs D = A * B^T on tcgen05 (bf16/f16 only; K % 8 == 0; A/B 16-byte aligned).
+// `ldo` is the output row stride (elements); `ohw` is used by kEpiNchw.
+dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, void* out,
+                               int64_t rows_a, int64_t rows_b, int64_t k, int64_t lda,
+                               int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,
+                               dli_dtype dtype, const GemmPlan& plan, void* workspace,
+                               size_t workspace_bytes, cudaStream_t stream);
+
+// SIMT fallback (any float dtype, any alignment): out[M,N] = A[M,K] . B + bias,
+// with B given as [N,K] (b_kmajor) or [K,N].
+dli_status run_gemm_simt(const void* a, const void* b, const void* bias, void* out, int64_t m,
+                         int64_t n, int64_t k, bool b_kmajor, dli_dtype dtype,
+                         cudaStream_t stream);
+
+}  // namespace dli_sm100

@@ -1,0 +1,802 @@
+// Attention kernels (softmax(q k^T * scale + bottom-right causal mask) v).
+//
+// Semantics follow python/dli_ops/aot/attention/kernel.py:5-62: query row i of a
+// sequence with Sq queries and Sk keys may see key j iff j <= i + (Sk - Sq)
+// (kernel.py:35,49-50); scale defaults to 1/sqrt(D) (build_triton_aot_ops.py:283).
+// GQA: query head h reads KV head h / (Hq / Hkv).
+//
+// All kernels are stride-generic: q/out element (b, h, s, d) lives at
+// b*sb + h*sh + s*ss + d, and K/V rows of (b, kvh) are contiguous D-vectors at
+// b*k_sb + kvh*k_sh + j*D. The key count of sequence b is `kv_len[b]` (a device
+// array, so CUDA-graph replays can advance it) or the dense `seq_k`.
+//
+//  * decode kernel (Sq * group <= 16 query rows per KV head): split-KV flash
+//    decoding. CTA = (split, kv head, batch); the group's query rows form one
+//    16-row MMA tile so each K/V byte fetched from HBM serves every query head
+//    of the group. 4 warps each take 16 keys of every 64-key block
+//    (cp.async 3-stage ring); partial (m, l, O) per split go to the workspace
+//    and a combine kernel merges them.
+//  * prefill kernel: FA2-style, CTA = (64 query rows, head, batch), 4 warps x
+//    16 rows, 64-key blocks double-buffered with cp.async, QK^T and PV on
+//    mma.sync m16n8k16 with fp32 accumulators, online softmax in registers.
+//  * fallback kernel: exact fp32 (CUDA cores), any head_dim; serves fp32
+//    graphs (the reference dtype) and head dims the MMA kernels do not cover.
+#include <algorithm>
+#include <cfloat>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace dli_sm100 {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AttnArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int64_t q_sb, q_sh, q_ss;
+  int64_t o_sb, o_sh, o_ss;
+  int64_t k_sb, k_sh;  // v uses the same strides
+  int batch, hq, hkv, group, seq_q, seq_k, head_dim;
+  const int64_t* positions;  // kv_len[b] = positions[b] + seq_q when non-null
+  float scale_log2;          // scale * log2(e)
+  int causal;                // 0: every key < kv_len is visible
+  // split-KV decode
+  int splits;
+  float* part_o;    // [B, Hkv, splits, 16, D]
+  float* part_ml;   // [B, Hkv, splits, 16, 2]
+};
+
+__device__ __forceinline__ int kv_len_of(const AttnArgs& a, int b) {
+  return a.positions ? static_cast<int>(a.positions[b]) + a.seq_q : a.seq_k;
+}
+
+// ---- MMA / ldmatrix / cp.async helpers ------------------------------------------
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+// Element offset of (row, col) inside a [rows x D] tile whose 16-byte chunks are
+// XOR-swizzled by (row % 8) so ldmatrix row groups hit distinct banks.
+template <int D>
+__device__ __forceinline__ int swz(int row, int col) {
+  return row * D + ((((col >> 3) ^ (row & 7))) << 3) + (col & 7);
+}
+
+// Loads `rows` x D elements (row r of the tile = global row r0 + r, clipped to
+// `limit` with zero fill) into a swizzled smem tile with 16-byte cp.async.
+template <typename T, int D, int ROWS, int THREADS>
+__device__ __forceinline__ void load_tile(T* smem_tile, const T* base, int r0, int limit) {
+  constexpr int CPR = D / 8;  // 16-byte chunks per row
+  const uint32_t s0 = static_cast<uint32_t>(__cvta_generic_to_shared(smem_tile));
+  for (int c = threadIdx.x; c < ROWS * CPR; c += THREADS) {
+    const int r = c / CPR, ch = c - r * CPR;
+    const int gr = r0 + r;
+    const bool valid = gr < limit;
+    const T* src = base + static_cast<int64_t>(valid ? gr : 0) * D + ch * 8;
+    cp_async16(s0 + swz<D>(r, ch * 8) * 2, src, valid);
+  }
+}
+
+// ---- prefill ---------------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(128)
+    attn_prefill_kernel(const AttnArgs a) {
+  constexpr int BM = 64, BN = 64;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  T* sq = reinterpret_cast<T*>(smem_raw);
+  T* sk = sq + BM * D;          // [2][BN*D]
+  T* sv = sk + 2 * BN * D;      // [2][BN*D]
+
+  const int mb = gridDim.x - 1 - blockIdx.x;  // longest causal rows first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / a.group;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int m0 = mb * BM;
+  const int kv_len = kv_len_of(a, b);
+  const int off = kv_len - a.seq_q;  // bottom-right causal offset
+  const T* qbase = static_cast<const T*>(a.q) + b * a.q_sb + h * a.q_sh;
+  const T* kbase = static_cast<const T*>(a.k) + b * a.k_sb + kvh * a.k_sh;
+  const T* vbase = static_cast<const T*>(a.v) + b * a.k_sb + kvh * a.k_sh;
+
+  // Q tile (rows may be strided: token-major layouts have q_ss != D).
+  {
+    constexpr int CPR = D / 8;
+    const uint32_t s0 = static_cast<uint32_t>(__cvta_generic_to_shared(sq));
+    for (int c = threadIdx.x; c < BM * CPR; c += 128) {
+      const int r = c / CPR, ch = c - r * CPR;
+      const int qs = m0 + r;
+      const bool valid = qs < a.seq_q;
+      cp_async16(s0 + swz<D>(r, ch * 8) * 2, qbase + (valid ? qs : 0) * a.q_ss + ch * 8, valid);
+    }
+  }
+  int n_end = a.causal ? min(kv_len, m0 + BM + off) : kv_len;
+  n_end = max(n_end, 0);
+  const int nblocks = (n_end + BN - 1) / BN;
+  if (nblocks > 0) {
+    load_tile<T, D, BN, 128>(sk, kbase, 0, kv_len);
+    load_tile<T, D, BN, 128>(sv, vbase, 0, kv_len);
+  }
+  cp_async_commit();
+
+  uint32_t qf[D / 16][4];
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  const int qrow0 = m0 + warp * 16 + g;  // rows qrow0 and qrow0 + 8
+
+  for (int nb = 0; nb < nblocks; ++nb) {
+    const int buf = nb & 1;
+    if (nb + 1 < nblocks) {
+      load_tile<T, D, BN, 128>(sk + (buf ^ 1) * BN * D, kbase, (nb + 1) * BN, kv_len);
+      load_tile<T, D, BN, 128>(sv + (buf ^ 1) * BN * D, vbase, (nb + 1) * BN, kv_len);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (nb == 0) {
+      const uint32_t s0 = static_cast<uint32_t>(__cvta_generic_to_shared(sq));
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int r = warp * 16 + (lane & 15);
+        const int c = kk * 16 + (lane >> 4) * 8;
+        ldsm_x4(qf[kk], s0 + swz<D>(r, c) * 2);
+      }
+    }
+    const T* kt = sk + buf * BN * D;
+    const T* vt = sv + buf * BN * D;
+    const uint32_t ks = static_cast<uint32_t>(__cvta_generic_to_shared(kt));
+    const uint32_t vs = static_cast<uint32_t>(__cvta_generic_to_shared(vt));
+
+    float s[BN / 8][4];
+#pragma unroll
+    for (int nt = 0; nt < BN / 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < BN / 8; ++nt) {
+#pragma unroll
+      for (int kk = 0; kk < D / 16; kk += 2) {
+        uint32_t bf[4];
+        const int r = nt * 8 + (lane & 7);
+        const int c = kk * 16 + (lane >> 3) * 8;
+        ldsm_x4(bf, ks + swz<D>(r, c) * 2);
+        mma16816<T>(s[nt], qf[kk], bf[0], bf[1]);
+        mma16816<T>(s[nt], qf[kk + 1], bf[2], bf[3]);
+      }
+    }
+    // mask + online softmax
+    const int n0 = nb * BN;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < BN / 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = n0 + nt * 8 + 2 * t + (e & 1);
+        const int qr = qrow0 + (e >> 1) * 8;
+        const bool vis = key < kv_len && (!a.causal || key <= qr + off);
+        const float val = vis ? s[nt][e] * a.scale_log2 : -INFINITY;
+        s[nt][e] = val;
+        mx[e >> 1] = fmaxf(mx[e >> 1], val);
+      }
+    }
+    float alpha[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float mnew = fmaxf(mrow[r], mx[r]);
+      alpha[r] = (mrow[r] == -INFINITY) ? 0.f : exp2f(mrow[r] - mnew);
+      mrow[r] = mnew;
+    }
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < BN / 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float m = mrow[e >> 1];
+        const float p = (m == -INFINITY) ? 0.f : exp2f(s[nt][e] - m);
+        s[nt][e] = p;
+        rs[e >> 1] += p;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) lrow[r] = lrow[r] * alpha[r] + rs[r];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= alpha[0];
+      o[i][1] *= alpha[0];
+      o[i][2] *= alpha[1];
+      o[i][3] *= alpha[1];
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < BN / 16; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack2<T>(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack2<T>(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack2<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack2<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dt = 0; dt < D / 16; ++dt) {
+        uint32_t bf[4];
+        const int r = kk * 16 + (lane & 15);
+        const int c = dt * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(bf, vs + swz<D>(r, c) * 2);
+        mma16816<T>(o[2 * dt], pa, bf[0], bf[1]);
+        mma16816<T>(o[2 * dt + 1], pa, bf[2], bf[3]);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  // finalize
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+    lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+  }
+  T* obase = static_cast<T*>(a.out) + b * a.o_sb + h * a.o_sh;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int qs = qrow0 + r * 8;
+    if (qs >= a.seq_q) continue;
+    const float inv = lrow[r] > 0.f ? 1.f / lrow[r] : 0.f;
+    T* dst = obase + static_cast<int64_t>(qs) * a.o_ss;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      const int d = i * 8 + 2 * t;
+      *reinterpret_cast<uint32_t*>(dst + d) = pack2<T>(o[i][2 * r] * inv, o[i][2 * r + 1] * inv);
+    }
+  }
+}
+
+// ---- decode (split-KV) ---------------------------------------------------------------
+template <typename T, int D>
+__global__ void __launch_bounds__(128)
+    attn_decode_kernel(const AttnArgs a) {
+  constexpr int BN = 64, STAGES = 3;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  T* sk = reinterpret_cast<T*>(smem_raw);           // [STAGES][BN*D]
+  T* sv = sk + STAGES * BN * D;                      // [STAGES][BN*D]
+  float* so = reinterpret_cast<float*>(sv + STAGES * BN * D);  // [16][D] merged O
+  float* sm = so + 16 * D;                           // [4][16] warp maxima
+  float* sl = sm + 64;                               // [4][16] warp sums
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int kv_len = kv_len_of(a, b);
+  const int off = kv_len - a.seq_q;
+  const int rows = a.group * a.seq_q;  // <= 16
+  // key range of this split, in whole 64-key blocks
+  const int total_blocks = (kv_len + BN - 1) / BN;
+  const int per_split = (total_blocks + a.splits - 1) / a.splits;
+  const int blk0 = split * per_split;
+  const int blk1 = min(blk0 + per_split, total_blocks);
+  const int nblocks = max(blk1 - blk0, 0);
+
+  const T* kbase = static_cast<const T*>(a.k) + b * a.k_sb + kvh * a.k_sh;
+  const T* vbase = static_cast<const T*>(a.v) + b * a.k_sb + kvh * a.k_sh;
+
+  // prologue loads
+#pragma unroll
+  for (int st = 0; st < STAGES - 1; ++st) {
+    if (st < nblocks) {
+      load_tile<T, D, BN, 128>(sk + st * BN * D, kbase, (blk0 + st) * BN, kv_len);
+      load_tile<T, D, BN, 128>(sv + st * BN * D, vbase, (blk0 + st) * BN, kv_len);
+    }
+    cp_async_commit();
+  }
+
+  // Q fragments straight from global: row r -> (s = r / group, head = kvh*group + r % group)
+  uint32_t qf[D / 16][4];
+  {
+    const T* qb = static_cast<const T*>(a.q) + b * a.q_sb;
+    auto qptr = [&](int r, int col) -> const T* {
+      const int s = r / a.group, hh = kvh * a.group + (r - s * a.group);
+      return qb + hh * a.q_sh + s * a.q_ss + col;
+    };
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int c0 = kk * 16 + 2 * t;
+      uint32_t z = 0;
+      qf[kk][0] = g < rows ? *reinterpret_cast<const uint32_t*>(qptr(g, c0)) : z;
+      qf[kk][1] = g + 8 < rows ? *reinterpret_cast<const uint32_t*>(qptr(g + 8, c0)) : z;
+      qf[kk][2] = g < rows ? *reinterpret_cast<const uint32_t*>(qptr(g, c0 + 8)) : z;
+      qf[kk][3] = g + 8 < rows ? *reinterpret_cast<const uint32_t*>(qptr(g + 8, c0 + 8)) : z;
+    }
+  }
+  // query token index of each of the thread's two rows (for the causal mask)
+  const int qs0 = g < rows ? g / a.group : 0;
+  const int qs1 = g + 8 < rows ? (g + 8) / a.group : 0;
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+  for (int it = 0; it < nblocks; ++it) {
+    const int pre = it + STAGES - 1;
+    if (pre < nblocks) {
+      const int st = pre % STAGES;
+      load_tile<T, D, BN, 128>(sk + st * BN * D, kbase, (blk0 + pre) * BN, kv_len);
+      load_tile<T, D, BN, 128>(sv + st * BN * D, vbase, (blk0 + pre) * BN, kv_len);
+    }
+    cp_async_commit();
+    cp_async_wait<STAGES - 1>();
+    __syncthreads();
+    const int st = it % STAGES;
+    const uint32_t ks = static_cast<uint32_t>(__cvta_generic_to_shared(sk + st * BN * D));
+    const uint32_t vs = static_cast<uint32_t>(__cvta_generic_to_shared(sv + st * BN * D));
+    const int kw = warp * 16;  // this warp's 16 keys inside the block
+    float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t bf[4];
+      const int r = kw + (lane & 7) + ((lane >> 4) << 3);
+      const int c = kk * 16 + ((lane >> 3) & 1) * 8;
+      ldsm_x4(bf, ks + swz<D>(r, c) * 2);
+      mma16816<T>(s[0], qf[kk], bf[0], bf[1]);
+      mma16816<T>(s[1], qf[kk], bf[2], bf[3]);
+    }
+    const int n0 = (blk0 + it) * BN + kw;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = n0 + nt * 8 + 2 * t + (e & 1);
+        const int qs = (e >> 1) ? qs1 : qs0;
+        const bool vis = key < kv_len && (!a.causal || key <= qs + off);
+        const float val = vis ? s[nt][e] * a.scale_log2 : -INFINITY;
+        s[nt][e] = val;
+        mx[e >> 1] = fmaxf(mx[e >> 1], val);
+      }
+    }
+    float alpha[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float mnew = fmaxf(mrow[r], mx[r]);
+      alpha[r] = (mrow[r] == -INFINITY) ? 0.f : exp2f(mrow[r] - mnew);
+      mrow[r] = mnew;
+    }
+    float rs[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float m = mrow[e >> 1];
+        const float p = (m == -INFINITY) ? 0.f : exp2f(s[nt][e] - m);
+        s[nt][e] = p;
+        rs[e >> 1] += p;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) lrow[r] = lrow[r] * alpha[r] + rs[r];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= alpha[0];
+      o[i][1] *= alpha[0];
+      o[i][2] *= alpha[1];
+      o[i][3] *= alpha[1];
+    }
+    uint32_t pa[4];
+    pa[0] = pack2<T>(s[0][0], s[0][1]);
+    pa[1] = pack2<T>(s[0][2], s[0][3]);
+    pa[2] = pack2<T>(s[1][0], s[1][1]);
+    pa[3] = pack2<T>(s[1][2], s[1][3]);
+#pragma unroll
+    for (int dt = 0; dt < D / 16; ++dt) {
+      uint32_t bf[4];
+      const int r = kw + (lane & 15);
+      const int c = dt * 16 + (lane >> 4) * 8;
+      ldsm_x4_t(bf, vs + swz<D>(r, c) * 2);
+      mma16816<T>(o[2 * dt], pa, bf[0], bf[1]);
+      mma16816<T>(o[2 * dt + 1], pa, bf[2], bf[3]);
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+  // merge the 4 warps' states: row maxima / sums per warp, then scaled O sum
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 1);
+    lrow[r] += __shfl_xor_sync(0xffffffffu, lrow[r], 2);
+  }
+  for (int i = threadIdx.x; i < 16 * D; i += 128) so[i] = 0.f;
+  if (t == 0) {
+    sm[warp * 16 + g] = mrow[0];
+    sm[warp * 16 + g + 8] = mrow[1];
+    sl[warp * 16 + g] = lrow[0];
+    sl[warp * 16 + g + 8] = lrow[1];
+  }
+  __syncthreads();
+  float mtot[2], ltot[2], scale[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = g + 8 * r;
+    float m = -INFINITY;
+    for (int w = 0; w < 4; ++w) m = fmaxf(m, sm[w * 16 + row]);
+    float l = 0.f;
+    for (int w = 0; w < 4; ++w) {
+      const float mw = sm[w * 16 + row];
+      l += (mw == -INFINITY) ? 0.f : sl[w * 16 + row] * exp2f(mw - m);
+    }
+    mtot[r] = m;
+    ltot[r] = l;
+    scale[r] = (mrow[r] == -INFINITY) ? 0.f : exp2f(mrow[r] - m);
+  }
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) {
+    const int d = i * 8 + 2 * t;
+    atomicAdd(&so[g * D + d], o[i][0] * scale[0]);
+    atomicAdd(&so[g * D + d + 1], o[i][1] * scale[0]);
+    atomicAdd(&so[(g + 8) * D + d], o[i][2] * scale[1]);
+    atomicAdd(&so[(g + 8) * D + d + 1], o[i][3] * scale[1]);
+  }
+  __syncthreads();
+  if (a.splits == 1) {
+    // final output
+    for (int i = threadIdx.x; i < rows * D; i += 128) {
+      const int r = i / D, d = i - r * D;
+      const int s = r / a.group, hh = kvh * a.group + (r - s * a.group);
+      // every thread with this row computed identical mtot/ltot; recompute from smem
+      float m = -INFINITY, l = 0.f;
+      for (int w = 0; w < 4; ++w) m = fmaxf(m, sm[w * 16 + r]);
+      for (int w = 0; w < 4; ++w) {
+        const float mw = sm[w * 16 + r];
+        l += (mw == -INFINITY) ? 0.f : sl[w * 16 + r] * exp2f(mw - m);
+      }
+      T* dst = static_cast<T*>(a.out) + b * a.o_sb + hh * a.o_sh + s * a.o_ss + d;
+      *dst = from_f32<T>(l > 0.f ? so[r * D + d] / l : 0.f);
+    }
+  } else {
+    const int64_t slot = ((static_cast<int64_t>(b) * a.hkv + kvh) * a.splits + split);
+    float* po = a.part_o + slot * 16 * D;
+    for (int i = threadIdx.x; i < 16 * D; i += 128) po[i] = so[i];
+    if (t == 0 && warp == 0) {
+      float* pml = a.part_ml + slot * 32;
+      pml[g * 2] = mtot[0];
+      pml[g * 2 + 1] = ltot[0];
+      pml[(g + 8) * 2] = mtot[1];
+      pml[(g + 8) * 2 + 1] = ltot[1];
+    }
+  }
+}
+
+// Merges split partials: out = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M).
+template <typename T>
+__global__ void attn_combine_kernel(const AttnArgs a) {
+  const int kvh = blockIdx.x, b = blockIdx.y;
+  const int rows = a.group * a.seq_q;
+  const int D = a.head_dim;
+  const int64_t slot0 = (static_cast<int64_t>(b) * a.hkv + kvh) * a.splits;
+  for (int i = threadIdx.x; i < rows * D; i += blockDim.x) {
+    const int r = i / D, d = i - r * D;
+    float m = -INFINITY;
+    for (int s = 0; s < a.splits; ++s) m = fmaxf(m, a.part_ml[(slot0 + s) * 32 + r * 2]);
+    float l = 0.f, acc = 0.f;
+    for (int s = 0; s < a.splits; ++s) {
+      const float ms = a.part_ml[(slot0 + s) * 32 + r * 2];
+      if (ms == -INFINITY) continue;
+      const float w = exp2f(ms - m);
+      l += a.part_ml[(slot0 + s) * 32 + r * 2 + 1] * w;
+      acc += a.part_o[(slot0 + s) * 16 * D + r * D + d] * w;
+    }
+    const int sq = r / a.group, hh = kvh * a.group + (r - sq * a.group);
+    T* dst = static_cast<T*>(a.out) + b * a.o_sb + hh * a.o_sh + sq * a.o_ss + d;
+    *dst = from_f32<T>(l > 0.f ? acc / l : 0.f);
+  }
+}
+
+// ---- exact fp32 fallback ---------------------------------------------------------------
+// One warp per query row; lanes split the keys of each 32-key chunk (dot products
+// read q from shared memory), then the chunk's probabilities are broadcast and
+// each lane accumulates its own dims of O. Exact fp32 math with expf.
+template <typename T>
+__global__ void attn_fallback_kernel(const AttnArgs a) {
+  extern __shared__ float sqf[];  // [warps][D]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * nwarps + warp;
+  const int64_t total = static_cast<int64_t>(a.batch) * a.hq * a.seq_q;
+  if (row >= total) return;
+  const int qs = static_cast<int>(row % a.seq_q);
+  const int h = static_cast<int>((row / a.seq_q) % a.hq);
+  const int b = static_cast<int>(row / (static_cast<int64_t>(a.seq_q) * a.hq));
+  const int kvh = h / a.group;
+  const int D = a.head_dim;
+  const int kv_len = kv_len_of(a, b);
+  const int off = kv_len - a.seq_q;
+  const float scale = a.scale_log2 / kLog2e;
+  float* qv = sqf + warp * D;
+  const T* qp = static_cast<const T*>(a.q) + b * a.q_sb + h * a.q_sh + qs * a.q_ss;
+  for (int d = lane; d < D; d += 32) qv[d] = to_f32(qp[d]);
+  __syncwarp();
+  const T* kb = static_cast<const T*>(a.k) + b * a.k_sb + kvh * a.k_sh;
+  const T* vb = static_cast<const T*>(a.v) + b * a.k_sb + kvh * a.k_sh;
+  const int nkeys = a.causal ? max(0, min(kv_len, qs + off + 1)) : kv_len;
+  float m = -INFINITY, l = 0.f;
+  float acc[8];  // dims lane, lane+32, ... (D <= 256)
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int j0 = 0; j0 < nkeys; j0 += 32) {
+    const int j = j0 + lane;
+    float sc = -INFINITY;
+    if (j < nkeys) {
+      float dot = 0.f;
+      for (int d = 0; d < D; ++d) dot = fmaf(qv[d], to_f32(kb[static_cast<int64_t>(j) * D + d]), dot);
+      sc = dot * scale;
+    }
+    const float cm = warp_max(sc);
+    const float mnew = fmaxf(m, cm);
+    const float alpha = (m == -INFINITY) ? 0.f : expf(m - mnew);
+    const float p = (sc == -INFINITY) ? 0.f : expf(sc - mnew);
+    l = l * alpha + warp_sum(p);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] *= alpha;
+    const int cnt = min(32, nkeys - j0);
+    for (int jj = 0; jj < cnt; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, p, jj);
+      const T* vr = vb + static_cast<int64_t>(j0 + jj) * D;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int d = lane + 32 * i;
+        if (d < D) acc[i] = fmaf(pj, to_f32(vr[d]), acc[i]);
+      }
+    }
+    m = mnew;
+  }
+  T* op = static_cast<T*>(a.out) + b * a.o_sb + h * a.o_sh + qs * a.o_ss;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = lane + 32 * i;
+    if (d < D) op[d] = from_f32<T>(l > 0.f ? acc[i] / l : 0.f);
+  }
+}
+
+// ---- host dispatch ----------------------------------------------------------------------
+struct DecodePlan {
+  bool decode = false;
+  int splits = 1;
+  size_t workspace = 0;
+};
+
+DecodePlan plan_decode(int64_t batch, int64_t hkv, int64_t group, int64_t seq_q, int64_t max_kv,
+                       int64_t head_dim) {
+  DecodePlan p;
+  if (group * seq_q > 16) return p;
+  p.decode = true;
+  const int64_t pairs = batch * hkv;
+  const int64_t blocks = std::max<int64_t>(1, ceil_div(max_kv, 64));
+  const int64_t target = 2 * sm_count();
+  int64_t splits = std::max<int64_t>(1, ceil_div(target, pairs));
+  splits = std::min<int64_t>(splits, blocks);
+  splits = std::min<int64_t>(splits, 64);
+  p.splits = static_cast<int>(splits);
+  if (p.splits > 1)
+    p.workspace = static_cast<size_t>(pairs * p.splits) * (16 * head_dim + 32) * sizeof(float);
+  return p;
+}
+
+bool tc_head_dim(int64_t d) { return d == 64 || d == 128; }
+
+template <typename T, int D>
+dli_status launch_tc_attention(const AttnArgs& args, const DecodePlan& plan, cudaStream_t stream) {
+  if (plan.decode) {
+    constexpr int kSmem = 2 * 3 * 64 * D * 2 + 16 * D * 4 + 128 * 4;
+    auto kern = attn_decode_kernel<T, D>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    dim3 grid(plan.splits, args.hkv, args.batch);
+    kern<<<grid, 128, kSmem, stream>>>(args);
+    if (plan.splits > 1) {
+      dim3 cg(args.hkv, args.batch);
+      attn_combine_kernel<T><<<cg, 256, 0, stream>>>(args);
+    }
+    return check_launch("attention decode");
+  }
+  constexpr int kSmem = (64 * D + 4 * 64 * D) * 2;
+  auto kern = attn_prefill_kernel<T, D>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  dim3 grid(static_cast<unsigned>(ceil_div(args.seq_q, 64)), args.hq, args.batch);
+  kern<<<grid, 128, kSmem, stream>>>(args);
+  return check_launch("attention prefill");
+}
+
+dli_status run_attention(AttnArgs& args, dli_dtype dtype, int64_t max_kv, void* workspace,
+                         size_t workspace_bytes, cudaStream_t stream) {
+  const bool tc = (dtype == DLI_DTYPE_BF16 || dtype == DLI_DTYPE_F16) &&
+                  tc_head_dim(args.head_dim) && aligned(args.q, 16) && aligned(args.k, 16) &&
+                  aligned(args.v, 16) && aligned(args.out, 4);
+  if (tc) {
+    const DecodePlan plan = plan_decode(args.batch, args.hkv, args.group, args.seq_q, max_kv, args.head_dim);
+    if (plan.decode && plan.splits > 1) {
+      if (workspace == nullptr || workspace_bytes < plan.workspace)
+        return fail(DLI_ERR_WORKSPACE, "attention: workspace too small (need " +
+                                           std::to_string(plan.workspace) + " bytes)");
+      args.part_o = static_cast<float*>(workspace);
+      args.part_ml = args.part_o + static_cast<int64_t>(args.batch) * args.hkv * plan.splits * 16 * args.head_dim;
+    }
+    args.splits = plan.splits;
+    if (dtype == DLI_DTYPE_BF16)
+      return args.head_dim == 64 ? launch_tc_attention<__nv_bfloat16, 64>(args, plan, stream)
+                                 : launch_tc_attention<__nv_bfloat16, 128>(args, plan, stream);
+    return args.head_dim == 64 ? launch_tc_attention<__half, 64>(args, plan, stream)
+                               : launch_tc_attention<__half, 128>(args, plan, stream);
+  }
+  if (args.head_dim > 256) return fail(DLI_ERR_UNSUPPORTED, "attention: head_dim > 256");
+  const int64_t rows = static_cast<int64_t>(args.batch) * args.hq * args.seq_q;
+  const int warps = 4;
+  const unsigned grid = static_cast<unsigned>(ceil_div(rows, warps));
+  const size_t smem = warps * args.head_dim * sizeof(float);
+  const dli_status st = dispatch_float(dtype, "attention", [&](auto tag) {
+    using T = decltype(tag);
+    attn_fallback_kernel<T><<<grid, warps * 32, smem, stream>>>(args);
+  });
+  if (st != DLI_OK) return st;
+  return check_launch("attention fallback");
+}
+
+size_t attention_ws(int64_t batch, int64_t hq, int64_t hkv, int64_t seq_q, int64_t max_kv,
+                    int64_t head_dim, dli_dtype dtype) {
+  if (batch <= 0 || hq <= 0 || hkv <= 0 || hq % hkv != 0) return 0;
+  const bool tc = (dtype == DLI_DTYPE_BF16 || dtype == DLI_DTYPE_F16) && tc_head_dim(head_dim);
+  if (!tc) return 0;
+  const DecodePlan plan = plan_decode(batch, hkv, hq / hkv, seq_q, max_kv, head_dim);
+  return plan.decode ? plan.workspace : 0;
+}
+
+}  // namespace
+}  // namespace dli_sm100
+
+using namespace dli_sm100;
+
+extern "C" size_t dli_sm100_attention_workspace_size(int64_t batch, int64_t q_heads,
+                                                     int64_t kv_heads, int64_t seq_q,
+                                                     int64_t seq_k, int64_t head_dim,
+                                                     dli_dtype dtype) {
+  return attention_ws(batch, q_heads, kv_heads, seq_q, seq_k, head_dim, dtype);
+}
+
+extern "C" dli_status dli_sm100_attention(const void* q, const void* k, const void* v, void* out,
+                                          int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                          int64_t seq_q, int64_t seq_k, int64_t kv_capacity,
+                                          int64_t head_dim, int causal, float scale,
+                                          dli_dtype dtype, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  if (batch < 0 || q_heads <= 0 || kv_heads <= 0 || seq_q < 0 || seq_k < 0 || head_dim <= 0)
+    return fail(DLI_ERR_INVALID_ARGUMENT, "attention: bad sizes");
+  if (q_heads % kv_heads != 0)
+    return fail(DLI_ERR_INVALID_ARGUMENT, "attention: q heads must be a multiple of kv heads");
+  if (kv_capacity < seq_k) return fail(DLI_ERR_INVALID_ARGUMENT, "attention: kv_capacity < seq_k");
+  if (!is_float_dtype(dtype)) return fail(DLI_ERR_INVALID_ARGUMENT, "attention expects a float dtype");
+  if (batch == 0 || seq_q == 0) return ok();
+  if (seq_k == 0) return fail(DLI_ERR_INVALID_ARGUMENT, "attention: no keys");
+  if (seq_q > (1 << 30) || seq_k > (1 << 30)) return fail(DLI_ERR_UNSUPPORTED, "attention: sequence too long");
+  AttnArgs args{};
+  args.q = q;
+  args.k = k;
+  args.v = v;
+  args.out = out;
+  args.q_sb = q_heads * seq_q * head_dim;
+  args.q_sh = seq_q * head_dim;
+  args.q_ss = head_dim;
+  args.o_sb = args.q_sb;
+  args.o_sh = args.q_sh;
+  args.o_ss = args.q_ss;
+  args.k_sb = kv_heads * kv_capacity * head_dim;
+  args.k_sh = kv_capacity * head_dim;
+  args.batch = static_cast<int>(batch);
+  args.hq = static_cast<int>(q_heads);
+  args.hkv = static_cast<int>(kv_heads);
+  args.group = static_cast<int>(q_heads / kv_heads);
+  args.seq_q = static_cast<int>(seq_q);
+  args.seq_k = static_cast<int>(seq_k);
+  args.head_dim = static_cast<int>(head_dim);
+  args.positions = nullptr;
+  const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(head_dim));
+  args.scale_log2 = sc * kLog2e;
+  args.causal = causal ? 1 : 0;
+  return run_attention(args, dtype, seq_k, workspace, workspace_bytes, as_stream(stream));
+}
+
+extern "C" size_t dli_sm100_attention_kvcache_workspace_size(int64_t batch, int64_t seq,
+                                                             int64_t q_heads, int64_t kv_heads,
+                                                             int64_t capacity, int64_t head_dim,
+                                                             dli_dtype dtype) {
+  return attention_ws(batch, q_heads, kv_heads, seq, capacity, head_dim, dtype);
+}
+
+extern "C" dli_status dli_sm100_attention_kvcache(const void* q, const void* cache_k,
+                                                  const void* cache_v, const int64_t* positions,
+                                                  void* out, int64_t batch, int64_t seq,
+                                                  int64_t q_heads, int64_t kv_heads,
+                                                  int64_t capacity, int64_t head_dim, float scale,
+                                                  dli_dtype dtype, void* workspace,
+                                                  size_t workspace_bytes, void* stream) {
+  if (batch < 0 || seq < 0 || q_heads <= 0 || kv_heads <= 0 || capacity <= 0 || head_dim <= 0)
+    return fail(DLI_ERR_INVALID_ARGUMENT, "attention_kvcache: bad sizes");
+  if (q_heads % kv_heads != 0)
+    return fail(DLI_ERR_INVALID_ARGUMENT, "attention_kvcache: q heads must be a multiple of kv heads");
+  if (positions == nullptr) return fail(DLI_ERR_INVALID_ARGUMENT, "attention_kvcache: positions required");
+  if (!is_float_dtype(dtype)) return fail(DLI_ERR_INVALID_ARGUMENT, "attention_kvcache expects a float dtype");
+  if (batch == 0 || seq == 0) return ok();
+  AttnArgs args{};
+  args.q = q;
+  args.k = cache_k;
+  args.v = cache_v;
+  args.out = out;
+  args.q_sb = seq * q_heads * head_dim;
+  args.q_sh = head_dim;
+  args.q_ss = q_heads * head_dim;
+  args.o_sb = args.q_sb;
+  args.o_sh = args.q_sh;
+  args.o_ss = args.q_ss;
+  args.k_sb = kv_heads * capacity * head_dim;
+  args.k_sh = capacity * head_dim;
+  args.batch = static_cast<int>(batch);
+  args.hq = static_cast<int>(q_heads);
+  args.hkv = static_cast<int>(kv_heads);
+  args.group = static_cast<int>(q_heads / kv_heads);
+  args.seq_q = static_cast<int>(seq);
+  args.seq_k = static_cast<int>(capacity);
+  args.head_dim = static_cast<int>(head_dim);
+  args.positions = positions;
+  const float sc = scale > 0.f ? scale : 1.0f / sqrtf(static_cast<float>(head_dim));
+  args.scale_log2 = sc * kLog2e;
+  args.causal = 1;
+  return run_attention(args, dtype, capacity, workspace, workspace_bytes, as_stream(stream));
+}

@@ -1,0 +1,178 @@
+// conv2d (NCHW, python/dli_ops/aot/conv2d/kernel.py:5-49 semantics: zero padding,
+// stride, optional bias).
+//
+// bf16/f16: implicit GEMM on the tcgen05 path. An im2col kernel writes the
+// patch matrix cols[M = N*OH*OW, Kp] (K = C*KH*KW rounded up to a multiple of 8
+// so TMA row strides stay 16-byte aligned) into the workspace; the weight
+// [OC, C, KH, KW] is already a K-major [OC, K] operand (repacked to Kp columns
+// when K % 8 != 0). The GEMM epilogue scatters D[m, oc] straight to NCHW.
+// f32: direct convolution, one output per thread, fp32 FMA (exact arithmetic).
+#include <algorithm>
+
+#include "gemm.cuh"
+
+namespace dli_sm100 {
+namespace {
+
+struct ConvShape {
+  int64_t n, c, h, w, oc, kh, kw, sh, sw, ph, pw, oh, ow;
+  __host__ __device__ int64_t k() const { return c * kh * kw; }
+  __host__ __device__ int64_t kp() const { return (k() + 7) / 8 * 8; }
+  __host__ __device__ int64_t m() const { return n * oh * ow; }
+};
+
+template <typename T>
+__global__ void im2col_kernel(const T* __restrict__ x, T* __restrict__ cols, ConvShape s) {
+  const int64_t kp = s.kp(), k = s.k();
+  const int64_t total = s.m() * kp;
+  const int64_t ohw = s.oh * s.ow;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t kk = i % kp, m = i / kp;
+    T v = from_f32<T>(0.f);
+    if (kk < k) {
+      const int64_t img = m / ohw, pix = m - img * ohw;
+      const int64_t oy = pix / s.ow, ox = pix - oy * s.ow;
+      const int64_t ch = kk / (s.kh * s.kw), r = kk - ch * s.kh * s.kw;
+      const int64_t ky = r / s.kw, kx = r - ky * s.kw;
+      const int64_t iy = oy * s.sh + ky - s.ph, ix = ox * s.sw + kx - s.pw;
+      if (iy >= 0 && iy < s.h && ix >= 0 && ix < s.w) v = x[((img * s.c + ch) * s.h + iy) * s.w + ix];
+    }
+    cols[i] = v;
+  }
+}
+
+template <typename T>
+__global__ void pad_weight_kernel(const T* __restrict__ w, T* __restrict__ wp, int64_t oc, int64_t k,
+                                  int64_t kp) {
+  const int64_t total = oc * kp;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t kk = i % kp, o = i / kp;
+    wp[i] = kk < k ? w[o * k + kk] : from_f32<T>(0.f);
+  }
+}
+
+template <typename T>
+__global__ void conv_direct_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                   const T* __restrict__ bias, T* __restrict__ out, ConvShape s) {
+  const int64_t total = s.n * s.oc * s.oh * s.ow;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t ox = i % s.ow, oy = (i / s.ow) % s.oh;
+    const int64_t o = (i / (s.ow * s.oh)) % s.oc, img = i / (s.ow * s.oh * s.oc);
+    float acc = bias ? to_f32(bias[o]) : 0.f;
+    for (int64_t ch = 0; ch < s.c; ++ch) {
+      const T* plane = x + (img * s.c + ch) * s.h * s.w;
+      const T* wk = w + (o * s.c + ch) * s.kh * s.kw;
+      for (int64_t ky = 0; ky < s.kh; ++ky) {
+        const int64_t iy = oy * s.sh + ky - s.ph;
+        if (iy < 0 || iy >= s.h) continue;
+        for (int64_t kx = 0; kx < s.kw; ++kx) {
+          const int64_t ix = ox * s.sw + kx - s.pw;
+          if (ix < 0 || ix >= s.w) continue;
+          acc = fmaf(to_f32(plane[iy * s.w + ix]), to_f32(wk[ky * s.kw + kx]), acc);
+        }
+      }
+    }
+    out[i] = from_f32<T>(acc);
+  }
+}
+
+inline unsigned grid_for(int64_t n) {
+  return static_cast<unsigned>(std::min<int64_t>(ceil_div(std::max<int64_t>(n, 1), 256), sm_count() * 16));
+}
+
+inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+struct ConvWorkspace {
+  size_t cols = 0, weight = 0, gemm = 0, total = 0;
+  GemmPlan plan;
+  bool implicit = false;
+};
+
+ConvWorkspace conv_workspace(const ConvShape& s, dli_dtype dtype) {
+  ConvWorkspace ws;
+  if (dtype != DLI_DTYPE_BF16 && dtype != DLI_DTYPE_F16) return ws;
+  ws.plan = plan_tn_gemm(s.m(), s.oc, s.kp(), dtype, true);
+  if (!ws.plan.tcgen05) return ws;
+  ws.implicit = true;
+  ws.cols = align256(static_cast<size_t>(s.m() * s.kp()) * 2);
+  ws.weight = s.kp() != s.k() ? align256(static_cast<size_t>(s.oc * s.kp()) * 2) : 0;
+  ws.gemm = align256(ws.plan.workspace);
+  ws.total = ws.cols + ws.weight + ws.gemm;
+  return ws;
+}
+
+dli_status make_shape(ConvShape& s, int64_t n, int64_t c, int64_t h, int64_t w, int64_t oc,
+                      int64_t kh, int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw) {
+  if (n < 0 || c <= 0 || h <= 0 || w <= 0 || oc <= 0 || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0 ||
+      ph < 0 || pw < 0)
+    return fail(DLI_ERR_INVALID_ARGUMENT, "conv2d: bad sizes");
+  s = ConvShape{n, c, h, w, oc, kh, kw, sh, sw, ph, pw, 0, 0};
+  s.oh = (h + 2 * ph - kh) / sh + 1;
+  s.ow = (w + 2 * pw - kw) / sw + 1;
+  if (s.oh <= 0 || s.ow <= 0) return fail(DLI_ERR_INVALID_ARGUMENT, "conv2d: empty output");
+  return DLI_OK;
+}
+
+}  // namespace
+}  // namespace dli_sm100
+
+using namespace dli_sm100;
+
+extern "C" size_t dli_sm100_conv2d_workspace_size(int64_t n, int64_t c, int64_t h, int64_t w,
+                                                  int64_t oc, int64_t kh, int64_t kw,
+                                                  int64_t stride_h, int64_t stride_w,
+                                                  int64_t pad_h, int64_t pad_w, dli_dtype dtype) {
+  ConvShape s;
+  if (make_shape(s, n, c, h, w, oc, kh, kw, stride_h, stride_w, pad_h, pad_w) != DLI_OK) return 0;
+  if (s.m() == 0) return 0;
+  return conv_workspace(s, dtype).total;
+}
+
+extern "C" dli_status dli_sm100_conv2d(const void* x, const void* weight, const void* bias,
+                                       void* out, int64_t n, int64_t c, int64_t h, int64_t w,
+                                       int64_t oc, int64_t kh, int64_t kw, int64_t stride_h,
+                                       int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                                       dli_dtype dtype, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+  ConvShape s;
+  dli_status st = make_shape(s, n, c, h, w, oc, kh, kw, stride_h, stride_w, pad_h, pad_w);
+  if (st != DLI_OK) return st;
+  if (!is_float_dtype(dtype)) return fail(DLI_ERR_INVALID_ARGUMENT, "conv2d expects a float dtype");
+  if (s.m() == 0) return ok();
+  if (!x || !weight || !out) return fail(DLI_ERR_INVALID_ARGUMENT, "conv2d: null pointer");
+  cudaStream_t cs = as_stream(stream);
+  const ConvWorkspace ws = conv_workspace(s, dtype);
+  if (ws.implicit && s.m() * s.oc < (1ll << 31)) {
+    if (workspace == nullptr || workspace_bytes < ws.total)
+      return fail(DLI_ERR_WORKSPACE, "conv2d: workspace too small (need " + std::to_string(ws.total) + " bytes)");
+    uint8_t* base = static_cast<uint8_t*>(workspace);
+    void* cols = base;
+    const void* wk = weight;
+    st = dispatch_float(dtype, "conv2d", [&](auto tag) {
+      using T = decltype(tag);
+      im2col_kernel<T><<<grid_for(s.m() * s.kp()), 256, 0, cs>>>((const T*)x, (T*)cols, s);
+      if (ws.weight) {
+        pad_weight_kernel<T><<<grid_for(s.oc * s.kp()), 256, 0, cs>>>((const T*)weight,
+                                                                      (T*)(base + ws.cols), s.oc,
+                                                                      s.k(), s.kp());
+        wk = base + ws.cols;
+      }
+    });
+    if (st != DLI_OK) return st;
+    st = check_launch("conv2d im2col");
+    if (st != DLI_OK) return st;
+    return run_tn_gemm_tcgen05(cols, wk, bias, out, s.m(), s.oc, s.kp(), s.kp(), s.kp(), 0,
+                               kEpiNchw, s.oh * s.ow, dtype, ws.plan, base + ws.cols + ws.weight,
+                               ws.gemm, cs);
+  }
+  st = dispatch_float(dtype, "conv2d", [&](auto tag) {
+    using T = decltype(tag);
+    conv_direct_kernel<T><<<grid_for(s.n * s.oc * s.oh * s.ow), 256, 0, cs>>>(
+        (const T*)x, (const T*)weight, (const T*)bias, (T*)out, s);
+  });
+  if (st != DLI_OK) return st;
+  return check_launch("conv2d direct");
+}

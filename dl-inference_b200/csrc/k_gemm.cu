@@ -1,0 +1,544 @@
+// GEMM kernels behind linear, matmul and conv2d.
+//
+// tcgen05 path (bf16/f16 operands, fp32 accumulation) — a warp-specialised TN
+// GEMM  D[i, j] = sum_k A[i, k] * B[j, k]  with both operands K-major (the
+// nn.Linear layout x[M,K], w[N,K]):
+//   warp 0     TMA producer: 128x64 A box + BNx64 B box per stage, 128-byte
+//              swizzle, STAGES-deep mbarrier ring (full/empty);
+//   warp 1     TMEM allocator + single-thread tcgen05.mma issuer (M=128, N=BN,
+//              K=16 per instruction, 4 per stage), tcgen05.commit frees a stage;
+//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time from the warp's TMEM
+//              lane quarter, bias add, convert, store.
+// Decode-sized problems (few activation rows) run swap-AB: A = weights (rows N
+// fill the 128-row MMA), B = activations (BN = rows rounded up to 16), so the
+// weight matrix streams through HBM exactly once; tiles with too little K-work
+// per SM are split along K, each split writing an fp32 partial tile to the
+// workspace and the last-arriving CTA of a tile (atomic ticket) reducing them.
+// Prefill-sized problems run A = activations, B = weights with BN = 128/256 and
+// grouped tile rasterisation for L2 reuse.
+//
+// SIMT path: exact-fp32 FFMA tiles for fp32 tensors (the reference kernel,
+// python/dli_ops/aot/linear/kernel.py:24-38, runs fp32 tl.dot as TF32; the
+// accuracy target here is fp32), and for shapes TMA cannot address.
+#include <algorithm>
+#include <mutex>
+#include <type_traits>
+
+#include "gemm.cuh"
+#include "tcgen05.cuh"
+
+namespace dli_sm100 {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kGemmThreads = 192;
+constexpr int kGroupI = 8;
+
+template <int BN, int STAGES>
+struct TcLayout {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kBytes = kBarOffset + (2 * STAGES + 1) * 8 + 16 + 1024;
+  static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
+  static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KiB alignment");
+};
+
+struct TcParams {
+  int rows_a, rows_b;
+  int tiles_i, tiles_j;
+  int kblocks, kpb, splits;
+  int epilogue;
+  int64_t ldo, ohw;
+  int out_vec;  // output base is 16-byte aligned
+  const void* bias;
+  void* out;
+  float* partials;
+  unsigned* counters;
+  unsigned* err;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_i, int tiles_j, int& ti, int& tj) {
+  const int per_group = kGroupI * tiles_j;
+  const int g = tile / per_group;
+  const int first = g * kGroupI;
+  const int gsize = min(tiles_i - first, kGroupI);
+  const int r = tile - g * per_group;
+  ti = first + r % gsize;
+  tj = r / gsize;
+}
+
+template <typename T>
+__device__ __forceinline__ void store_chunk(const TcParams& p, int64_t gi, int jc, const float* v) {
+  const T* bias = static_cast<const T*>(p.bias);
+  T* out = static_cast<T*>(p.out);
+  if (gi >= p.rows_a) return;
+  if (p.epilogue == kEpiRowMajor) {
+    T* dst = out + gi * p.ldo + jc;
+    if (p.out_vec && jc + 32 <= p.rows_b && (p.ldo % 8) == 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        Vec16<T> pack;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int k = q * 8 + e;
+          const float bv = bias ? to_f32(bias[jc + k]) : 0.f;
+          pack.e[e] = from_f32<T>(v[k] + bv);
+        }
+        store16(dst + q * 8, pack);
+      }
+    } else {
+      for (int k = 0; k < 32 && jc + k < p.rows_b; ++k) {
+        const float bv = bias ? to_f32(bias[jc + k]) : 0.f;
+        dst[k] = from_f32<T>(v[k] + bv);
+      }
+    }
+  } else if (p.epilogue == kEpiTransposed) {
+    const float bv = bias ? to_f32(bias[gi]) : 0.f;
+    for (int k = 0; k < 32 && jc + k < p.rows_b; ++k)
+      out[static_cast<int64_t>(jc + k) * p.ldo + gi] = from_f32<T>(v[k] + bv);
+  } else {  // kEpiNchw
+    const int64_t img = gi / p.ohw, pix = gi - img * p.ohw;
+    for (int k = 0; k < 32 && jc + k < p.rows_b; ++k) {
+      const float bv = bias ? to_f32(bias[jc + k]) : 0.f;
+      out[(img * p.rows_b + jc + k) * p.ohw + pix] = from_f32<T>(v[k] + bv);
+    }
+  }
+}
+
+template <typename T, int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    tcgen05_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                        const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
+  using L = TcLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort, [1] last split
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  int ti, tj;
+  tile_coords(tile, p.tiles_i, p.tiles_j, ti, tj);
+  const int kb0 = split * p.kpb;
+  const int nkb = min(kb0 + p.kpb, p.kblocks) - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    flags[0] = 0;
+    flags[1] = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int it = 0; it < nkb; ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1)) {
+          set_device_error(p.err, kDevErrGemmTimeout);
+          flags[0] = 1;
+          break;
+        }
+        if (flags[0]) break;
+        uint8_t* sa = smem + s * L::kStageBytes;
+        mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+        tma_load_2d(sa, &tmap_a, (kb0 + it) * kBK, ti * kBM, &full[s]);
+        tma_load_2d(sa + L::kABytes, &tmap_b, (kb0 + it) * kBK, tj * BN, &full[s]);
+        issued = it + 1;
+      }
+      // No bulk copy may still be writing shared memory when the CTA exits.
+      for (int it = max(0, issued - STAGES); it < issued; ++it)
+        mbar_wait(&full[it % STAGES], (it / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, BN);
+      for (int it = 0; it < nkb; ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph)) {
+          set_device_error(p.err, kDevErrGemmTimeout);
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
+        const uint64_t adesc = umma_desc_sw128(a_addr);
+        const uint64_t bdesc = umma_desc_sw128(a_addr + L::kABytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          umma_f16(tmem_base, adesc + 2 * kk, bdesc + 2 * kk, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(acc_full);
+    }
+  } else {
+    // Epilogue: warp w may only touch TMEM lanes 32*(w%4) .. 32*(w%4)+31.
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int64_t gi = static_cast<int64_t>(ti) * kBM + row;
+    const int j0 = tj * BN;
+    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    if (!mbar_wait(acc_full, 0)) {
+      set_device_error(p.err, kDevErrGemmTimeout);
+      flags[0] = 1;
+    }
+    tc_fence_after();
+    const bool aborted = flags[0] != 0;
+    if (!aborted && p.splits == 1) {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c, r);
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
+        if (j0 + c < p.rows_b) store_chunk<T>(p, gi, j0 + c, v);
+      }
+    } else if (!aborted) {
+      const int ntiles = p.tiles_i * p.tiles_j;
+      float* mine = p.partials + ((static_cast<size_t>(split) * ntiles + tile) * kBM + row) * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int k = 0; k < 32; k += 4)
+          __stcg(reinterpret_cast<float4*>(mine + c + k),
+                 make_float4(__uint_as_float(r[k]), __uint_as_float(r[k + 1]),
+                             __uint_as_float(r[k + 2]), __uint_as_float(r[k + 3])));
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        const unsigned prev = atomicAdd(&p.counters[tile], 1u);
+        flags[1] = (prev == static_cast<unsigned>(p.splits - 1)) ? 1 : 0;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (flags[1]) {
+        // Sum every split's partial (this CTA's included) in split order so the
+        // result does not depend on which CTA arrived last.
+        __threadfence();
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] = 0.f;
+          for (int s = 0; s < p.splits; ++s) {
+            const float* other =
+                p.partials + ((static_cast<size_t>(s) * ntiles + tile) * kBM + row) * BN + c;
+#pragma unroll
+            for (int k = 0; k < 32; k += 4) {
+              const float4 o = __ldcg(reinterpret_cast<const float4*>(other + k));
+              v[k] += o.x;
+              v[k + 1] += o.y;
+              v[k + 2] += o.z;
+              v[k + 3] += o.w;
+            }
+          }
+          if (j0 + c < p.rows_b) store_chunk<T>(p, gi, j0 + c, v);
+        }
+        if (threadIdx.x == 64) p.counters[tile] = 0;  // ticket ready for the next launch
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// ---- SIMT fallback -----------------------------------------------------------
+constexpr int kSimtTile = 64;
+constexpr int kSimtK = 16;
+
+template <typename T, bool kBKMajor>
+__global__ void __launch_bounds__(256)
+    gemm_simt_kernel(const T* __restrict__ a, const T* __restrict__ b, const T* __restrict__ bias,
+                     T* __restrict__ out, int64_t m, int64_t n, int64_t k) {
+  __shared__ float as[kSimtK][kSimtTile + 4];
+  __shared__ float bs[kSimtK][kSimtTile + 4];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kSimtTile;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kSimtTile;
+  float acc[4][4] = {};
+  for (int64_t k0 = 0; k0 < k; k0 += kSimtK) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int idx = tid + e * 256;
+      const int r = idx >> 4, c = idx & 15;
+      as[c][r] = (m0 + r < m && k0 + c < k) ? to_f32(a[(m0 + r) * k + k0 + c]) : 0.f;
+      if constexpr (kBKMajor) {
+        bs[c][r] = (n0 + r < n && k0 + c < k) ? to_f32(b[(n0 + r) * k + k0 + c]) : 0.f;
+      } else {
+        const int kk = idx >> 6, nn = idx & 63;
+        bs[kk][nn] = (k0 + kk < k && n0 + nn < n) ? to_f32(b[(k0 + kk) * n + n0 + nn]) : 0.f;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < kSimtK; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = as[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = m0 + ty * 4 + i;
+    if (r >= m) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t c = n0 + tx * 4 + j;
+      if (c < n) out[r * n + c] = from_f32<T>(acc[i][j] + (bias ? to_f32(bias[c]) : 0.f));
+    }
+  }
+}
+
+// ---- host helpers ---------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// K-major 2-D map over [rows, k] with row stride `ld` elements, box {64, box_rows}.
+dli_status make_kmajor_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, int64_t ld,
+                           int box_rows, bool bf16) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(DLI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DLI_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
+  return DLI_OK;
+}
+
+int stages_for(int bn) { return bn >= 256 ? 4 : (bn >= 128 ? 6 : 8); }
+
+template <typename T, int BN, int STAGES>
+dli_status launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p, int splits,
+                     cudaStream_t stream) {
+  using L = TcLayout<BN, STAGES>;
+  auto kernel = tcgen05_gemm_kernel<T, BN, STAGES>;
+  static bool configured[64] = {};  // per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return fail(DLI_ERR_CUDA, std::string("gemm smem attribute: ") + cudaGetErrorString(e));
+    configured[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>(p.tiles_i * p.tiles_j), static_cast<unsigned>(splits));
+  kernel<<<grid, kGemmThreads, L::kBytes, stream>>>(ma, mb, p);
+  return check_launch("tcgen05 gemm");
+}
+
+template <typename T>
+dli_status launch_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p,
+                        int splits, cudaStream_t stream) {
+  switch (bn) {
+    case 32: return launch_tc<T, 32, 8>(ma, mb, p, splits, stream);
+    case 64: return launch_tc<T, 64, 8>(ma, mb, p, splits, stream);
+    case 128: return launch_tc<T, 128, 6>(ma, mb, p, splits, stream);
+    case 256: return launch_tc<T, 256, 4>(ma, mb, p, splits, stream);
+  }
+  return fail(DLI_ERR_UNSUPPORTED, "gemm: unsupported tile width");
+}
+
+}  // namespace
+
+GemmPlan plan_tn_gemm(int64_t rows_a, int64_t rows_b, int64_t k, dli_dtype dtype, bool allow_split) {
+  GemmPlan plan;
+  const bool tc_type = dtype == DLI_DTYPE_BF16 || dtype == DLI_DTYPE_F16;
+  if (!tc_type || k % 8 != 0 || k <= 0 || rows_a <= 0 || rows_b <= 0 || rows_a > (1ll << 31) ||
+      rows_b > (1ll << 31))
+    return plan;
+  plan.tcgen05 = true;
+  if (rows_b <= 32) plan.bn = 32;
+  else if (rows_b <= 64) plan.bn = 64;
+  else if (rows_b <= 128) plan.bn = 128;
+  else plan.bn = (rows_b % 256 == 0 || rows_b >= 2048) ? 256 : 128;
+  plan.stages = stages_for(plan.bn);
+  plan.tiles_i = static_cast<int>(ceil_div(rows_a, kBM));
+  plan.tiles_j = static_cast<int>(ceil_div(rows_b, plan.bn));
+  plan.kblocks = static_cast<int>(ceil_div(k, kBK));
+  plan.splits = 1;
+  plan.kblocks_per_split = plan.kblocks;
+  const int64_t tiles = static_cast<int64_t>(plan.tiles_i) * plan.tiles_j;
+  const int sms = sm_count();
+  if (allow_split && tiles < sms && plan.kblocks >= 4) {
+    int splits = static_cast<int>(std::min<int64_t>(sms / tiles, plan.kblocks / 2));
+    splits = std::max(splits, 1);
+    if (splits > 1) {
+      plan.kblocks_per_split = static_cast<int>(ceil_div(plan.kblocks, splits));
+      plan.splits = static_cast<int>(ceil_div(plan.kblocks, plan.kblocks_per_split));
+    }
+  }
+  if (plan.splits > 1) {
+    const size_t counters = ((tiles * sizeof(unsigned)) + 255) / 256 * 256;
+    plan.workspace = counters + static_cast<size_t>(plan.splits) * tiles * kBM * plan.bn * sizeof(float);
+  }
+  return plan;
+}
+
+dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, void* out,
+                               int64_t rows_a, int64_t rows_b, int64_t k, int64_t lda,
+                               int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,
+                               dli_dtype dtype, const GemmPlan& plan, void* workspace,
+                               size_t workspace_bytes, cudaStream_t stream) {
+  if (!plan.tcgen05) return fail(DLI_ERR_UNSUPPORTED, "gemm: shape not served by tcgen05");
+  if (!aligned(a, 16) || !aligned(b, 16) || lda % 8 != 0 || ldb % 8 != 0)
+    return fail(DLI_ERR_UNSUPPORTED, "gemm: TMA needs 16-byte aligned operands and row strides");
+  if (plan.splits > 1 && (workspace == nullptr || workspace_bytes < plan.workspace))
+    return fail(DLI_ERR_WORKSPACE, "gemm: split-K workspace too small (need " +
+                                       std::to_string(plan.workspace) + " bytes)");
+  const bool bf16 = dtype == DLI_DTYPE_BF16;
+  CUtensorMap ma, mb;
+  dli_status st = make_kmajor_map(&ma, a, rows_a, k, lda, kBM, bf16);
+  if (st != DLI_OK) return st;
+  st = make_kmajor_map(&mb, b, rows_b, k, ldb, plan.bn, bf16);
+  if (st != DLI_OK) return st;
+  TcParams p{};
+  p.rows_a = static_cast<int>(rows_a);
+  p.rows_b = static_cast<int>(rows_b);
+  p.tiles_i = plan.tiles_i;
+  p.tiles_j = plan.tiles_j;
+  p.kblocks = plan.kblocks;
+  p.kpb = plan.kblocks_per_split;
+  p.splits = plan.splits;
+  p.epilogue = epilogue;
+  p.ldo = ldo;
+  p.ohw = ohw > 0 ? ohw : 1;
+  p.out_vec = aligned(out, 16) ? 1 : 0;
+  p.bias = bias;
+  p.out = out;
+  p.err = device_error_word();
+  if (plan.splits > 1) {
+    const int64_t tiles = static_cast<int64_t>(plan.tiles_i) * plan.tiles_j;
+    const size_t counters = ((tiles * sizeof(unsigned)) + 255) / 256 * 256;
+    p.counters = static_cast<unsigned*>(workspace);
+    p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
+    const cudaError_t e = cudaMemsetAsync(workspace, 0, tiles * sizeof(unsigned), stream);
+    if (e != cudaSuccess) return fail(DLI_ERR_CUDA, std::string("gemm ticket reset: ") + cudaGetErrorString(e));
+  }
+  if (bf16) return launch_tc_bn<__nv_bfloat16>(plan.bn, ma, mb, p, plan.splits, stream);
+  return launch_tc_bn<__half>(plan.bn, ma, mb, p, plan.splits, stream);
+}
+
+dli_status run_gemm_simt(const void* a, const void* b, const void* bias, void* out, int64_t m,
+                         int64_t n, int64_t k, bool b_kmajor, dli_dtype dtype,
+                         cudaStream_t stream) {
+  if (ceil_div(m, kSimtTile) > 65535) return fail(DLI_ERR_UNSUPPORTED, "gemm: too many rows for SIMT path");
+  dim3 grid(static_cast<unsigned>(ceil_div(n, kSimtTile)), static_cast<unsigned>(ceil_div(m, kSimtTile)));
+  dli_status st = dispatch_float(dtype, "gemm", [&](auto tag) {
+    using T = decltype(tag);
+    if (b_kmajor)
+      gemm_simt_kernel<T, true><<<grid, 256, 0, stream>>>((const T*)a, (const T*)b, (const T*)bias,
+                                                          (T*)out, m, n, k);
+    else
+      gemm_simt_kernel<T, false><<<grid, 256, 0, stream>>>((const T*)a, (const T*)b, (const T*)bias,
+                                                           (T*)out, m, n, k);
+  });
+  if (st != DLI_OK) return st;
+  return check_launch("simt gemm");
+}
+
+}  // namespace dli_sm100
+
+using namespace dli_sm100;
+
+namespace {
+// Activation rows at or below this count run swap-AB (weights on the MMA M side).
+constexpr int64_t kSwapRows = 128;
+}  // namespace
+
+extern "C" size_t dli_sm100_linear_workspace_size(int64_t m, int64_t n, int64_t k, dli_dtype dtype) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  const bool swap = m <= kSwapRows;
+  const GemmPlan plan = swap ? plan_tn_gemm(n, m, k, dtype, true) : plan_tn_gemm(m, n, k, dtype, true);
+  return plan.tcgen05 ? plan.workspace : 0;
+}
+
+extern "C" dli_status dli_sm100_linear(const void* x, const void* w, const void* bias, void* y,
+                                       int64_t m, int64_t n, int64_t k, dli_dtype dtype,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (m < 0 || n <= 0 || k <= 0) return fail(DLI_ERR_INVALID_ARGUMENT, "linear: bad sizes");
+  if (!is_float_dtype(dtype)) return fail(DLI_ERR_INVALID_ARGUMENT, "linear expects a float dtype");
+  if (m == 0) return ok();
+  if (!x || !w || !y) return fail(DLI_ERR_INVALID_ARGUMENT, "linear: null pointer");
+  const bool swap = m <= kSwapRows;
+  const GemmPlan plan = swap ? plan_tn_gemm(n, m, k, dtype, true) : plan_tn_gemm(m, n, k, dtype, true);
+  const bool tma_ok = aligned(x, 16) && aligned(w, 16);
+  if (plan.tcgen05 && tma_ok) {
+    if (swap)
+      return run_tn_gemm_tcgen05(w, x, bias, y, n, m, k, k, k, n, kEpiTransposed, 0, dtype, plan,
+                                 workspace, workspace_bytes, as_stream(stream));
+    return run_tn_gemm_tcgen05(x, w, bias, y, m, n, k, k, k, n, kEpiRowMajor, 0, dtype, plan,
+                               workspace, workspace_bytes, as_stream(stream));
+  }
+  return run_gemm_simt(x, w, bias, y, m, n, k, true, dtype, as_stream(stream));
+}
+
+extern "C" dli_status dli_sm100_matmul(const void* a, const void* b, void* out, int64_t m, int64_t n,
+                                       int64_t k, dli_dtype dtype, void* stream) {
+  if (m < 0 || n <= 0 || k <= 0) return fail(DLI_ERR_INVALID_ARGUMENT, "matmul: bad sizes");
+  if (!is_float_dtype(dtype)) return fail(DLI_ERR_INVALID_ARGUMENT, "matmul expects a float dtype");
+  if (m == 0) return ok();
+  return run_gemm_simt(a, b, nullptr, out, m, n, k, false, dtype, as_stream(stream));
+}

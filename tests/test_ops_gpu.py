@@ -1,0 +1,314 @@
+"""GPU parity of every C-ABI entry point of libdli_sm100.so against the oracle.
+
+Tolerances (written per dtype, checked as a relative Frobenius error plus an
+elementwise bound):
+  float32  rel <= 1e-4   (north-star fp32 bound; the kernels accumulate in fp32)
+  bfloat16 rel <= 1.5e-2 (inputs are rounded to bf16 first, the oracle runs on
+                          the rounded values in fp32/fp64; the bound covers bf16
+                          output rounding and bf16 P in attention)
+  float16  rel <= 5e-3
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from golden_io import all_cases
+from op_cases import capi_outputs, oracle_outputs
+from oracle import ops as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: 1e-4, torch.bfloat16: 1.5e-2, torch.float16: 5e-3}
+
+
+def rel_err(got, ref) -> float:
+    got = torch.as_tensor(got).double().cpu()
+    ref = torch.as_tensor(ref).double().cpu()
+    den = ref.norm().item()
+    return (got - ref).norm().item() / (den if den > 0 else 1.0)
+
+
+def assert_close(got, ref, dtype, what=""):
+    got = torch.as_tensor(got).double().cpu()
+    ref = torch.as_tensor(ref).double().cpu()
+    assert got.shape == ref.shape, f"{what}: shape {tuple(got.shape)} vs {tuple(ref.shape)}"
+    tol = TOL[dtype]
+    err = rel_err(got, ref)
+    assert err <= tol, f"{what}: relative error {err:.3e} > {tol:.1e}"
+    scale = max(ref.abs().max().item(), 1e-6)
+    bad = (got - ref).abs() > (8 * tol * scale + 8 * tol * ref.abs())
+    assert not bad.any(), f"{what}: {int(bad.sum())} elements out of the elementwise bound"
+
+
+def rounded(a: np.ndarray, dtype) -> np.ndarray:
+    """Rounds float inputs through `dtype` so the oracle sees what the kernel sees."""
+    if a.dtype.kind != "f":
+        return a
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dtype).double().numpy()
+
+
+CASES = list(all_cases())
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16],
+                         ids=["f32", "bf16", "f16"])
+@pytest.mark.parametrize("op,idx,case", CASES, ids=[f"{op}-{i}" for op, i, _ in CASES])
+def test_golden_case_through_capi(op, idx, case, dtype):
+    inp = case["inputs"]
+    if op == "rotary_embedding":
+        # cos/sin tables stay fp32 in every dtype (reference tables are fp32, export.py:228-247)
+        rinp = {k: (v if k in ("cos", "sin") else rounded(v, dtype)) for k, v in inp.items()}
+    else:
+        rinp = {k: rounded(v, dtype) for k, v in inp.items()}
+    want = oracle_outputs(op, rinp, case["attrs"])
+    got = capi_outputs(op, inp, case["attrs"], dtype)
+    torch.cuda.synchronize()
+    for name, ref in want.items():
+        assert_close(got[name].float(), ref, dtype, f"{op}[{idx}].{name}")
+    if dtype == torch.float32:
+        # the reference kernel's own output (golden) as well, where its math is sound
+        bad_ref = op == "attention" and not case["attrs"].get("causal", False) and \
+            inp["k"].shape[2] % 32 != 0
+        if not bad_ref:
+            for name, ref in case["outputs"].items():
+                assert_close(got[name].float(), ref, dtype, f"{op}[{idx}].{name} vs reference kernel")
+
+
+# ---- contractions at model scale ------------------------------------------------------
+
+LINEAR_SHAPES = [  # (M, N, K)
+    (1, 896, 896), (8, 1152, 896), (8, 9728, 896), (8, 896, 4864), (32, 4608, 3584),
+    (32, 3584, 18944), (64, 3696, 8192), (100, 200, 96), (128, 896, 896), (129, 1152, 896),
+    (512, 4864, 896), (2048, 3584, 3584), (300, 37888 // 8, 3584), (7, 152064 // 16, 896),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("m,n,k", LINEAR_SHAPES)
+def test_linear_tcgen05_model_shapes(m, n, k, dtype):
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+    x = torch.randn(m, k, device="cuda", generator=g).to(dtype)
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).to(dtype)
+    b = (torch.randn(n, device="cuda", generator=g) * 0.02).to(dtype)
+    y = C.linear(x, w, b)
+    y2 = C.linear(x, w, b)  # second call: split-K tickets must have reset themselves
+    C.check_device_error()
+    ref = x.float() @ w.float().T + b.float()
+    assert_close(y.float(), ref, dtype, f"linear {m}x{n}x{k}")
+    assert torch.equal(y, y2)
+
+
+def test_linear_fp32_config1():
+    """x[64,1024] . W[4096,1024]^T + b in fp32, rel-err <= 1e-4."""
+    import dli_sm100 as C
+
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(64, 1024, generator=g)
+    w = torch.randn(4096, 1024, generator=g) * 0.02
+    b = torch.randn(4096, generator=g) * 0.02
+    y = C.linear(x.cuda(), w.cuda(), b.cuda())
+    ref = O.linear(x.numpy(), w.numpy(), b.numpy())
+    assert rel_err(y, ref) <= 1e-4
+    assert np.abs(y.cpu().double().numpy() - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+def test_matmul_bf16_and_f32():
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    for dtype in (torch.float32, torch.bfloat16):
+        a = torch.randn(70, 130, device="cuda", generator=g).to(dtype)
+        b = torch.randn(130, 50, device="cuda", generator=g).to(dtype)
+        assert_close(C.matmul(a, b).float(), a.float() @ b.float(), dtype, f"matmul {dtype}")
+
+
+ALEXNET_CONVS = [  # (C, H, OC) at k3 s1 p1
+    (3, 32, 64), (64, 16, 192), (192, 8, 384), (384, 8, 256), (256, 8, 256)]
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32], ids=["f16", "bf16", "f32"])
+@pytest.mark.parametrize("c,h,oc", ALEXNET_CONVS)
+def test_conv2d_alexnet_shapes(c, h, oc, dtype):
+    import dli_sm100 as C
+
+    g = torch.Generator().manual_seed(c + h + oc)
+    x = torch.randn(2, c, h, h, generator=g)
+    w = torch.randn(oc, c, 3, 3, generator=g) * 0.02
+    b = torch.randn(oc, generator=g) * 0.02
+    xd, wd, bd = (t.to(dtype) for t in (x, w, b))
+    y = C.conv2d(xd.cuda(), wd.cuda(), bd.cuda(), (1, 1), (1, 1))
+    ref = torch.nn.functional.conv2d(xd.double(), wd.double(), bd.double(), padding=1)
+    assert_close(y.float(), ref, dtype, f"conv {c}->{oc} @{h}")
+
+
+# ---- attention ----------------------------------------------------------------------
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("b,hq,hkv,sq,sk,d,causal", [
+    (2, 14, 2, 300, 300, 64, True), (1, 28, 4, 512, 512, 128, True), (1, 2, 2, 65, 130, 128, False),
+    (1, 8, 1, 5, 77, 128, True), (2, 7, 1, 1, 513, 64, True), (1, 4, 4, 100, 100, 128, False)])
+def test_attention_dense(b, hq, hkv, sq, sk, d, causal, dtype):
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(sq + sk + d)
+    q = torch.randn(b, hq, sq, d, device="cuda", generator=g).to(dtype)
+    k = torch.randn(b, hkv, sk, d, device="cuda", generator=g).to(dtype)
+    v = torch.randn(b, hkv, sk, d, device="cuda", generator=g).to(dtype)
+    out = C.attention(q, k, v, causal=causal)
+    ref = torch.from_numpy(O.attention(q.double().cpu().numpy(), k.double().cpu().numpy(),
+                                       v.double().cpu().numpy(), causal))
+    assert_close(out.float(), ref, dtype, "attention")
+
+
+def _cache_reference(q_bshd, ck, cv, positions):
+    """Oracle over a cache: sequence b sees keys [0, positions[b] + S) bottom-right causal."""
+    outs = []
+    b, s, hq, d = q_bshd.shape
+    for i in range(b):
+        n = int(positions[i]) + s
+        q = q_bshd[i:i + 1].permute(0, 2, 1, 3).double().cpu().numpy()
+        k = ck[i:i + 1, :, :n].double().cpu().numpy()
+        v = cv[i:i + 1, :, :n].double().cpu().numpy()
+        outs.append(torch.from_numpy(O.attention(q, k, v, causal=True)).permute(0, 2, 1, 3))
+    return torch.cat(outs, 0)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16], ids=["bf16"])
+@pytest.mark.parametrize("b,s,hq,hkv,d,cap,positions", [
+    (4, 1, 28, 4, 128, 2560, [100, 513, 2000, 0]),
+    (8, 1, 14, 2, 64, 768, [512, 600, 700, 767 - 1, 3, 64, 65, 128]),
+    (2, 3, 64, 8, 128, 1024, [10, 500]),
+    (2, 77, 14, 2, 64, 512, [0, 40]),
+])
+def test_attention_kvcache(b, s, hq, hkv, d, cap, positions, dtype):
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(b * s + cap)
+    q = torch.randn(b, s, hq, d, device="cuda", generator=g).to(dtype)
+    ck = torch.randn(b, hkv, cap, d, device="cuda", generator=g).to(dtype)
+    cv = torch.randn(b, hkv, cap, d, device="cuda", generator=g).to(dtype)
+    pos = torch.tensor(positions, dtype=torch.int64, device="cuda")
+    out = C.attention_kvcache(q, ck, cv, pos)
+    ref = _cache_reference(q, ck, cv, positions)
+    assert_close(out.float(), ref, dtype, "attention_kvcache")
+
+
+def test_qkv_rotary_cache_matches_oracle():
+    import dli_sm100 as C
+
+    b, s, hq, hkv, d, cap = 2, 5, 4, 2, 64, 32
+    g = torch.Generator().manual_seed(11)
+    qkv = torch.randn(b * s, (hq + 2 * hkv) * d, generator=g).to(torch.bfloat16)
+    ang = torch.randn(64, d // 2, generator=g)
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    positions = torch.tensor([3, 20])
+    ck = torch.zeros(b, hkv, cap, d, dtype=torch.bfloat16, device="cuda")
+    cv = torch.zeros_like(ck)
+    qo = C.qkv_rotary_cache(qkv.cuda(), cos.cuda(), sin.cuda(), positions.cuda(), ck, cv, b, s, hq,
+                            hkv, d)
+    x = qkv.double().view(b, s, hq + 2 * hkv, d)
+    q = x[:, :, :hq].permute(0, 2, 1, 3).numpy()
+    k = x[:, :, hq:hq + hkv].permute(0, 2, 1, 3).numpy()
+    v = x[:, :, hq + hkv:].permute(0, 2, 1, 3).numpy()
+    rq, rk = O.rotary(q, k, cos.numpy(), sin.numpy(), positions=positions.numpy())
+    assert_close(qo.float(), torch.from_numpy(rq).permute(0, 2, 1, 3), torch.bfloat16, "q_out")
+    for i in range(b):
+        p = int(positions[i])
+        assert_close(ck[i, :, p:p + s].float(), rk[i], torch.bfloat16, "cache k")
+        assert_close(cv[i, :, p:p + s].float(), v[i], torch.bfloat16, "cache v")
+    # rows outside [p, p+s) stay untouched
+    assert ck[0, :, :3].abs().sum().item() == 0 and ck[0, :, 8:].abs().sum().item() == 0
+
+
+def test_kv_append_is_a_sequence_concat():
+    import dli_sm100 as C
+
+    g = torch.Generator().manual_seed(5)
+    old = torch.randn(2, 3, 4, 8, generator=g)
+    new = torch.randn(2, 3, 2, 8, generator=g)
+    ck = torch.zeros(2, 3, 10, 8, device="cuda")
+    cv = torch.zeros_like(ck)
+    C.kv_append(ck, cv, old.cuda(), (old * 2).cuda(), 0)
+    C.kv_append(ck, cv, new.cuda(), (new * 2).cuda(), 4)
+    torch.testing.assert_close(ck[:, :, :6].cpu(), torch.cat([old, new], 2), rtol=0, atol=0)
+    torch.testing.assert_close(cv[:, :, :6].cpu(), torch.cat([old, new], 2) * 2, rtol=0, atol=0)
+    with pytest.raises(ValueError):
+        C.kv_append(ck, cv, new.cuda(), new.cuda(), 9)
+
+
+# ---- norms / elementwise --------------------------------------------------------------
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
+@pytest.mark.parametrize("rows,hidden", [(8, 896), (32, 3584), (64, 8192), (5, 100)])
+def test_rms_norm_and_fused_residual(rows, hidden, dtype):
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(rows + hidden)
+    r = torch.randn(rows, hidden, device="cuda", generator=g).to(dtype)
+    dlt = torch.randn(rows, hidden, device="cuda", generator=g).to(dtype)
+    w = (1 + 0.1 * torch.randn(hidden, device="cuda", generator=g)).to(dtype)
+    assert_close(C.rms_norm(r, w).float(), O.rms_norm(r.double().cpu().numpy(), w.double().cpu().numpy()),
+                 dtype, "rms_norm")
+    normed, resid = C.add_rms_norm(r, dlt, w)
+    ref_n, ref_r = O.add_rms_norm(r.double().cpu().numpy(), dlt.double().cpu().numpy(),
+                                  w.double().cpu().numpy())
+    assert_close(resid.float(), ref_r, dtype, "residual")
+    assert_close(normed.float(), ref_n, dtype, "normed")
+    # in-place residual update (residual_out aliases residual)
+    r2 = r.clone()
+    normed2, _ = C.add_rms_norm(r2, dlt, w, residual_out=r2)
+    assert torch.equal(normed2, normed) and torch.equal(r2, resid)
+
+
+def test_silu_mul_embedding_argmax_select_cast():
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(9)
+    gu = torch.randn(6, 2 * 4864, device="cuda", generator=g).to(torch.bfloat16)
+    assert_close(C.silu_mul(gu).float(), O.silu_mul(gu.double().cpu().numpy()), torch.bfloat16, "silu_mul")
+    table = torch.randn(1000, 896, device="cuda", generator=g).to(torch.bfloat16)
+    ids = torch.randint(0, 1000, (3, 7), device="cuda", generator=g)
+    assert torch.equal(C.embedding(ids, table), table[ids])
+    assert torch.equal(C.embedding(ids.int(), table), table[ids])
+    logits = torch.randn(5, 152064, device="cuda", generator=g).to(torch.bfloat16)
+    logits[2, 17] = 100.0
+    logits[2, 18] = 100.0  # tie -> lowest index
+    am = C.argmax(logits)
+    assert am[2].item() == 17
+    assert torch.equal(am, torch.from_numpy(O.argmax(logits.float().cpu().numpy())).cuda())
+    x = torch.randn(4, 9, 33, device="cuda", generator=g)
+    assert torch.equal(C.select_token(x, 8), x[:, 8])
+    assert torch.equal(C.cast(x, torch.bfloat16), x.to(torch.bfloat16))
+    assert torch.equal(C.cast(x.half(), torch.float32), x.half().float())
+
+
+def test_device_error_word_reports_bad_embedding_id_and_clears():
+    import dli_sm100 as C
+
+    table = torch.randn(10, 8, device="cuda")
+    ids = torch.tensor([1, 12, 3], device="cuda")
+    out = C.embedding(ids, table)
+    with pytest.raises(RuntimeError, match="embedding id"):
+        C.check_device_error()
+    assert out[1].abs().sum().item() == 0
+    C.check_device_error()  # cleared
+
+
+def test_invalid_arguments_raise_value_error():
+    import dli_sm100 as C
+
+    x = torch.randn(4, 8, device="cuda")
+    w = torch.randn(3, 8, device="cuda")
+    with pytest.raises(ValueError):
+        C.check(C.lib().dli_sm100_linear(C._ptr(x), C._ptr(w), None, C._ptr(x), 4, -1, 8, 0, None, 0,
+                                         C._stream()))
+    with pytest.raises(ValueError):
+        C.attention(torch.randn(1, 3, 2, 8, device="cuda"), torch.randn(1, 2, 2, 8, device="cuda"),
+                    torch.randn(1, 2, 2, 8, device="cuda"))
+    assert math.isfinite(1.0)
