@@ -1,0 +1,458 @@
+"""Qwen2 serving benchmark of the sm_100a plugin (BASELINE config: Qwen2-7B shape).
+
+One "step" = one generation request batch: a causal prefill of B x S prompt
+tokens followed by D greedy decode steps over the KV cache, all through the
+dli.Engine running the exported dli.graph.v1 graph with the sm_100a plugin
+(decode replayed from a captured CUDA graph). Weights are random-init
+N(0, 0.02) of the named architecture (no checkpoints: synthetic data).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--model 7b|0.5b|72b]
+  python bench.py --impl reference ...     # the reference's CPU path (PyTorch eager)
+
+Multi-GPU (launched by torchrun, one rank per GPU): tensor parallelism over
+tp = min(N, max TP the head counts allow, 4 for 7B) with an NCCL all_reduce
+after o_proj and down_proj; N / tp data-parallel groups split the batch
+(strong scaling: total work fixed). Times are CUDA events on each rank, max
+over ranks.
+
+Printed JSON (rank 0): value = decode tok/s of the whole job; prefill tok/s,
+e2e (decode through the public API with host ids in and out every token),
+roofline of the dominant decode kernel (gate/up GEMM, HBM-bound) and of the
+dominant prefill kernel (tensor-bound), clocks sampled during the timed region,
+CPU baseline, and the number of this library's kernels launched.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "dl-inference_b200"
+sys.path.insert(0, str(PKG / "python"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Qwen2 decode tok/s + prefill tok/s at 1/2/4/8 B200; % of HBM/tensor roofline"
+
+MODELS = {
+    # name: (shape, batch, prompt, decode steps, max tp)
+    "7b": ("QWEN2_7B", 32, 2048, 512, 4),
+    "0.5b": ("QWEN2_0_5B", 8, 512, 256, 2),
+    "72b": ("QWEN2_72B", 64, 4096, 512, 8),
+}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("sm100", "reference"), default="sm100")
+    ap.add_argument("--model", choices=sorted(MODELS), default="7b")
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--prompt", type=int, default=None)
+    ap.add_argument("--decode", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled every 200 ms while active."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------
+# CPU baseline: the reference's CPU path (PyTorch-eager forward of the exported model)
+# ---------------------------------------------------------------------------------
+
+def cpu_baseline(shape, batch: int, prompt: int, seconds: float = 20.0) -> dict:
+    """Times transformers' Qwen2 (eager, bf16) on the host cores on a slice of the
+    workload: ONE decoder layer of the named shape, decode steps of the full batch
+    over a `prompt`-token cache, scaled to the full model (layers x per-layer time +
+    the LM head)."""
+    import torch
+    from transformers import Qwen2Config
+    from transformers.models.qwen2.modeling_qwen2 import Qwen2DecoderLayer, Qwen2RotaryEmbedding
+    from transformers.cache_utils import DynamicCache
+
+    threads = torch.get_num_threads()
+    cfg = Qwen2Config(vocab_size=shape.vocab, hidden_size=shape.hidden,
+                      intermediate_size=shape.intermediate, num_hidden_layers=1,
+                      num_attention_heads=shape.q_heads, num_key_value_heads=shape.kv_heads,
+                      max_position_embeddings=prompt + 64, rms_norm_eps=shape.rms_eps,
+                      rope_theta=shape.rope_theta, attn_implementation="eager")
+    torch.manual_seed(0)
+    with torch.no_grad():
+        layer = Qwen2DecoderLayer(cfg, 0).to(torch.bfloat16).eval()
+        for p in layer.parameters():
+            p.normal_(0, 0.02)
+        rot = Qwen2RotaryEmbedding(cfg)
+        lm = torch.randn(shape.vocab, shape.hidden, dtype=torch.bfloat16) * 0.02
+        # KV cache of `prompt` tokens for the full batch (filled directly)
+        cache = DynamicCache()
+        kv = torch.randn(batch, shape.kv_heads, prompt, shape.head_dim, dtype=torch.bfloat16)
+        cache.update(kv, kv.clone(), 0)
+        x = torch.randn(batch, 1, shape.hidden, dtype=torch.bfloat16)
+        steps, t_layer = 0, 0.0
+        start = time.perf_counter()
+        while time.perf_counter() - start < seconds * 0.8 or steps < 2:
+            pos = torch.full((batch, 1), prompt + steps, dtype=torch.int64)
+            emb = rot(x, pos)
+            t0 = time.perf_counter()
+            layer(x, attention_mask=None, position_ids=pos, past_key_values=cache,
+                  use_cache=True, position_embeddings=emb)
+            t_layer += time.perf_counter() - t0
+            steps += 1
+        t0 = time.perf_counter()
+        reps = 0
+        while reps < 2 or time.perf_counter() - t0 < seconds * 0.1:
+            torch.nn.functional.linear(x[:, 0], lm)
+            reps += 1
+        t_head = (time.perf_counter() - t0) / reps
+    step_s = shape.layers * (t_layer / steps) + t_head
+    return {"value": batch / step_s, "unit": "tok/s (decode)", "cores": threads, "kind": "reference",
+            "sample": (f"transformers Qwen2 eager bf16 on {threads} host threads: {steps} decode steps "
+                       f"of 1 of {shape.layers} decoder layers (batch {batch}, {prompt}-token cache) "
+                       f"+ LM head, scaled x{shape.layers} layers"),
+            "ms_per_step": step_s * 1e3}
+
+
+def run_reference_arm(args, world: int, rank: int):
+    from dli_export import qwen2 as Q
+
+    name, batch, prompt, dsteps, _ = MODELS[args.model]
+    if rank != 0:
+        return 0
+    shape = getattr(Q, name)
+    batch = args.batch or batch
+    prompt = args.prompt or prompt
+    vals = []
+    per = max(3.0, 60.0 / max(1, args.steps + args.warmup))
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline(shape, batch, prompt, seconds=per)
+        if i >= args.warmup:
+            vals.append(r)
+    value = statistics.median(v["value"] for v in vals)
+    line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tok/s (decode)",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": statistics.median(v["ms_per_step"] for v in vals),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init N(0,0.02) weights, seeded)",
+            "config": {"workload": f"qwen2-{args.model} decode, batch {batch}, {prompt}-token context"},
+            "cpu_baseline": {k: vals[-1][k] for k in ("kind", "cores", "sample")} | {"value": value,
+                                                                                     "unit": "tok/s (decode)"},
+            "e2e": {"value": value, "unit": "tok/s (decode)", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------------------------
+# sm_100a arm
+# ---------------------------------------------------------------------------------
+
+def main() -> int:
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, world, rank)
+
+    import torch
+    import torch.distributed as dist
+
+    import dli
+    import dli_sm100
+    from dli.qwen2 import Qwen2Runner
+    from dli_export import qwen2 as Q
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    name, batch, prompt, dsteps, max_tp = MODELS[args.model]
+    shape = getattr(Q, name)
+    batch = args.batch or batch
+    prompt = args.prompt or prompt
+    dsteps = args.decode or dsteps
+    tp = 1
+    while tp * 2 <= min(world, max_tp) and world % (tp * 2) == 0:
+        tp *= 2
+    dp = world // tp
+    group, tp_rank = rank // tp, rank % tp
+    if batch % dp:
+        raise SystemExit(f"batch {batch} not divisible by {dp} data-parallel groups")
+    b_local = batch // dp
+    capacity = (prompt + dsteps + 63) // 64 * 64
+
+    # --- communicator: one NCCL comm per tensor-parallel group, built by the plugin
+    comm = 0
+    plugin = dli_sm100.lib()  # noqa: F841  (kernel library loaded before the plugin)
+    if tp > 1:
+        import ctypes
+
+        P = ctypes.CDLL(dli.PLUGIN_PATH)
+        P.dli_sm100_nccl_comm_init.restype = ctypes.c_void_p
+        P.dli_sm100_nccl_comm_init.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        ids = [None] * dp
+        if rank == 0:
+            for g in range(dp):
+                buf = ctypes.create_string_buffer(256)
+                n = P.dli_sm100_nccl_unique_id(buf, 256)
+                if n <= 0:
+                    raise SystemExit("plugin built without NCCL")
+                ids[g] = buf.raw[:n]
+        dist.broadcast_object_list(ids, src=0)
+        idb = ctypes.create_string_buffer(ids[group], len(ids[group]))
+        comm = P.dli_sm100_nccl_comm_init(idb, tp, tp_rank, local)
+        if not comm:
+            raise SystemExit("ncclCommInitRank failed")
+
+    # --- weights: random N(0, 0.02), generated on the device layer by layer, sharded
+    weights = {}
+    for i in range(shape.layers):
+        st = Q.random_state(shape, device=dev, dtype=torch.bfloat16, seed=1000 + i,
+                            layers=range(i, i + 1), embeddings=False)
+        weights.update(Q.transform_weights(st, shape, tp, tp_rank, torch.bfloat16, layers=range(i, i + 1)))
+        del st, part
+    g = torch.Generator(device=dev).manual_seed(7)
+    weights["embed"] = (torch.randn(shape.vocab, shape.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    weights["lm_head"] = weights["embed"] if shape.tie_embeddings else \
+        (torch.randn(shape.vocab, shape.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    weights["norm"] = torch.ones(shape.hidden, device=dev, dtype=torch.bfloat16)
+    cos, sin = Q.rotary_tables(shape, capacity)
+    weights["rotary_cos"], weights["rotary_sin"] = cos.to(dev), sin.to(dev)
+    torch.cuda.synchronize()
+
+    runner = Qwen2Runner(shape, weights, capacity, tp_size=tp, tp_rank=tp_rank, communicator=comm or 0)
+    gen = torch.Generator(device=dev).manual_seed(100 + group)
+    prompts = torch.randint(0, shape.vocab, (b_local, prompt), device=dev, generator=gen)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # capture the decode graph once (counts the launches of one decode step)
+    n0 = dli_sm100.launch_count()
+    runner.decode_graph(b_local)
+    launches_decode = (dli_sm100.launch_count() - n0) // 3  # 2 warm runs + the captured run
+    n0 = dli_sm100.launch_count()
+    runner.prefill(prompts)
+    launches_prefill = dli_sm100.launch_count() - n0
+    torch.cuda.synchronize()
+
+    g_, ids_buf, pos_buf, _, next_buf = runner.decode_graph(b_local)
+    stream = torch.cuda.current_stream(dev)
+
+    def one_step():
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record(stream)
+        _, nxt = runner.prefill(prompts)
+        ids_buf.copy_(nxt.view(-1, 1))
+        pos_buf.fill_(prompt)
+        ev[1].record(stream)
+        for _ in range(dsteps):
+            g_.replay()
+        ev[2].record(stream)
+        return ev
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        events = [one_step() for _ in range(args.steps)]
+        torch.cuda.synchronize()
+    barrier()
+    pre_ms = sum(e[0].elapsed_time(e[1]) for e in events)
+    dec_ms = sum(e[1].elapsed_time(e[2]) for e in events)
+    t = torch.tensor([pre_ms, dec_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    pre_ms, dec_ms = t.tolist()
+    total_seqs = b_local * dp
+    decode_tok_s = total_seqs * dsteps * args.steps / (dec_ms / 1e3)
+    prefill_tok_s = total_seqs * prompt * args.steps / (pre_ms / 1e3)
+    clock = clocks.summary()
+
+    # --- e2e: decode through the public API, ids from pinned host memory each token,
+    #     next ids read back to host each token (same metric, host buffers included)
+    host_ids = torch.empty(b_local, 1, dtype=torch.int64, pin_memory=True)
+    host_out = torch.empty(b_local, dtype=torch.int64, pin_memory=True)
+    host_ids.copy_(prompts[:, -1:].cpu())
+    e2e_steps = min(dsteps, 128)
+    _, nxt = runner.prefill(prompts)
+    pos_buf.fill_(prompt)
+    torch.cuda.synchronize()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    wall0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        ids_buf.copy_(host_ids, non_blocking=True)
+        g_.replay()
+        host_out.copy_(next_buf, non_blocking=True)
+        stream.synchronize()
+        host_ids[:, 0] = host_out
+    t1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([max(t0.elapsed_time(t1), (time.perf_counter() - wall0) * 1e3)], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_tok_s = total_seqs * e2e_steps / (e2e_ms.item() / 1e3)
+
+    # --- roofline of the dominant kernels, timed live with CUDA events
+    pk = peaks()
+    inter_local = shape.intermediate // tp
+    n_gu, k_gu = 2 * inter_local, shape.hidden
+    x_dec = torch.randn(b_local, k_gu, device=dev).to(torch.bfloat16)
+    w_gu = weights["layers.0.wgu"]
+    reps = 20
+    for _ in range(3):
+        dli_sm100.linear(x_dec, w_gu)
+    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ea.record(stream)
+    for _ in range(reps):
+        dli_sm100.linear(x_dec, w_gu)
+    eb.record(stream)
+    torch.cuda.synchronize()
+    gemm_ms = ea.elapsed_time(eb) / reps
+    gemm_bytes = (n_gu * k_gu + b_local * (n_gu + k_gu)) * 2
+    achieved = gemm_bytes / (gemm_ms / 1e3) / 1e9
+    traffic = None
+    prof = ROOT / "profiles" / "traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get(f"decode_gate_up_{args.model}_tp{tp}_b{b_local}")
+    # prefill: gate/up GEMM at M = b_local * prompt (capped for memory)
+    m_pre = min(b_local * prompt, 16384)
+    x_pre = torch.randn(m_pre, k_gu, device=dev).to(torch.bfloat16)
+    dli_sm100.linear(x_pre, w_gu)
+    ea.record(stream)
+    for _ in range(5):
+        dli_sm100.linear(x_pre, w_gu)
+    eb.record(stream)
+    torch.cuda.synchronize()
+    pre_gemm_ms = ea.elapsed_time(eb) / 5
+    pre_tflops = 2.0 * m_pre * n_gu * k_gu / (pre_gemm_ms / 1e3) / 1e12
+    step_bytes = Q.decode_bytes_per_step(shape, b_local, prompt + dsteps // 2) / tp
+    step_ms = dec_ms / (args.steps * dsteps)
+    launches = args.steps * (launches_prefill + dsteps * launches_decode)
+
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_baseline(shape, total_seqs, prompt, seconds=20.0)
+            cpu.pop("ms_per_step", None)
+        except Exception as exc:  # report, do not fail the GPU measurement
+            cpu = {"value": None, "unit": "tok/s (decode)", "cores": os.cpu_count(), "kind": "reference",
+                   "sample": f"failed: {exc!r}"[:200]}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": decode_tok_s, "unit": "tok/s (decode)", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": (pre_ms + dec_ms) / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init N(0,0.02) weights of the named architecture, uniform token ids; seeded)",
+            "config": {"workload": f"qwen2-{args.model}: prefill {batch}x{prompt} + {dsteps} greedy decode steps",
+                       "model": f"Qwen2-{args.model.upper()}-shape", "global_batch": batch,
+                       "seq_len": prompt, "decode_steps": dsteps, "parallelism": f"tp{tp}" + (f"xdp{dp}" if dp > 1 else ""),
+                       "l2": "inputs larger than L2 (weights stream from HBM every step)",
+                       "kv_capacity": capacity},
+            "prefill": {"value": prefill_tok_s, "unit": "tok/s (prefill)", "ms_per_step": pre_ms / args.steps},
+            "decode_ms_per_token_step": step_ms,
+            "e2e": {"value": e2e_tok_s, "unit": "tok/s (decode)", "h2d_bytes_per_step": 8 * b_local,
+                    "d2h_bytes_per_step": 8 * b_local, "steps": e2e_steps,
+                    "path": "Qwen2Runner decode graph fed from pinned host ids, next ids read to host every token"},
+            "roofline": {"bound": "hbm", "kernel": f"tcgen05 swap-AB GEMM gate_up [{b_local}x{k_gu}]x[{n_gu}x{k_gu}]^T",
+                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
+                         "algorithmic_bytes": gemm_bytes, "ms": gemm_ms, "peak_source": pk["source"]},
+            "roofline_decode_step": {"bound": "hbm", "bytes": step_bytes, "ms": step_ms,
+                                     "achieved": step_bytes / (step_ms / 1e3) / 1e9, "peak": pk["hbm_gbs"],
+                                     "unit": "GB/s", "frac": step_bytes / (step_ms / 1e3) / 1e9 / pk["hbm_gbs"]},
+            "roofline_prefill": {"bound": "tensor", "kernel": f"tcgen05 GEMM gate_up [{m_pre}x{k_gu}]x[{n_gu}x{k_gu}]^T",
+                                 "achieved": pre_tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                                 "frac": pre_tflops / pk["bf16_tflops"]},
+            "clocks": clock,
+            "cpu_baseline": cpu,
+            "gpu_launches": launches,
+            "launches_per_decode_step": launches_decode,
+        }
+        print(json.dumps(line))
+    del runner
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

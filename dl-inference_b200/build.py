@@ -107,17 +107,20 @@ def build_core(workers: int) -> Path:
     src = PKG / "core" / "src"
     out = BUILD / "core"
     out.mkdir(parents=True, exist_ok=True)
-    headers = list((PKG / "core" / "include" / "dli").glob("*.h"))
+    headers = list((PKG / "core" / "include" / "dli").glob("*.h")) + list(src.glob("*.h")) + [
+        ROOT / "include" / "dli_sm100.h"]
     flags = [f for f in _cxx_flags(tinc) if not f.startswith("-D_GLIBCXX")] + [_torch_abi_flag()]
     jobs = []
     for cc in sorted(src.glob("*.cc")):
         jobs.append((["g++", *flags, "-c", str(cc)], out / (cc.stem + ".o"), [cc, *headers]))
     objs = _compile_all(jobs, workers)
     so = LIB / "libdli_core.so"
-    if not so.exists() or so.stat().st_mtime < _newest(objs):
-        _run(["g++", "-shared", "-o", str(so), *map(str, objs), f"-L{tlib}", "-lc10", "-lc10_cuda",
-              "-ltorch_cpu", "-ltorch_cuda", f"-L{CUDA_HOME / 'lib64'}", "-lcudart",
-              f"-Wl,-rpath,{tlib}", f"-Wl,-rpath,{CUDA_HOME / 'lib64'}", "-ldl"])
+    deps = objs + [LIB / "libdli_sm100.so"]
+    if not so.exists() or so.stat().st_mtime < _newest(deps):
+        _run(["g++", "-shared", "-o", str(so), *map(str, objs), f"-L{LIB}", "-ldli_sm100",
+              f"-L{tlib}", "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch_cuda",
+              f"-L{CUDA_HOME / 'lib64'}", "-lcudart", "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{tlib}",
+              f"-Wl,-rpath,{CUDA_HOME / 'lib64'}", "-ldl"])
     return so
 
 

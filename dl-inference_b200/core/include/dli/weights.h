@@ -1,0 +1,17 @@
+// dli.weights.v1 loader: a JSON manifest {"format", "data", "tensors": {name:
+// {dtype, shape, offset, nbytes}}} plus one binary payload, the format the
+// reference exporter writes (python/dli_export/weights.py:21-65) and reads
+// (src/weights.cc:242-272 of yncxcw/dl-inference). The payload is memory-mapped
+// and each tensor is copied once to its destination device. Dtype strings:
+// float32, int64 (reference) and bfloat16, float16, int32 (additive).
+#pragma once
+
+#include <string>
+
+#include "dli/engine.h"
+
+namespace dli {
+
+TensorMap loadWeights(const std::string& manifest_path, DeviceType device, int device_id = 0);
+
+}  // namespace dli

@@ -21,8 +21,9 @@ namespace dli_sm100 {
 dli_status fail(dli_status status, const std::string& msg);
 // Clears the last error and returns DLI_OK.
 dli_status ok();
-// Maps the last launch error (cudaGetLastError) to a status naming `what`.
-dli_status check_launch(const char* what);
+// Maps the last launch error (cudaGetLastError) to a status naming `what`; on
+// success adds `launches` kernels to the library's launch counter.
+dli_status check_launch(const char* what, int launches = 1);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
@@ -46,6 +47,9 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
+
+// Raises a kernel's dynamic shared-memory limit to `bytes` once per device.
+dli_status ensure_smem(const void* kernel, int bytes, const char* what);
 
 // Dispatches a functor templated on the element type of a float dtype.
 template <typename F>

@@ -639,18 +639,20 @@ dli_status launch_tc_attention(const AttnArgs& args, const DecodePlan& plan, cud
   if (plan.decode) {
     constexpr int kSmem = 2 * 3 * 64 * D * 2 + 16 * D * 4 + 128 * 4;
     auto kern = attn_decode_kernel<T, D>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    const dli_status st = ensure_smem(reinterpret_cast<const void*>(kern), kSmem, "attention decode");
+    if (st != DLI_OK) return st;
     dim3 grid(plan.splits, args.hkv, args.batch);
     kern<<<grid, 128, kSmem, stream>>>(args);
     if (plan.splits > 1) {
       dim3 cg(args.hkv, args.batch);
       attn_combine_kernel<T><<<cg, 256, 0, stream>>>(args);
     }
-    return check_launch("attention decode");
+    return check_launch("attention decode", plan.splits > 1 ? 2 : 1);
   }
   constexpr int kSmem = (64 * D + 4 * 64 * D) * 2;
   auto kern = attn_prefill_kernel<T, D>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  const dli_status st = ensure_smem(reinterpret_cast<const void*>(kern), kSmem, "attention prefill");
+  if (st != DLI_OK) return st;
   dim3 grid(static_cast<unsigned>(ceil_div(args.seq_q, 64)), args.hq, args.batch);
   kern<<<grid, 128, kSmem, stream>>>(args);
   return check_launch("attention prefill");

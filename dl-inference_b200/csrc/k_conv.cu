@@ -162,7 +162,7 @@ extern "C" dli_status dli_sm100_conv2d(const void* x, const void* weight, const 
       }
     });
     if (st != DLI_OK) return st;
-    st = check_launch("conv2d im2col");
+    st = check_launch("conv2d im2col", ws.weight ? 2 : 1);
     if (st != DLI_OK) return st;
     return run_tn_gemm_tcgen05(cols, wk, bias, out, s.m(), s.oc, s.kp(), s.kp(), s.kp(), 0,
                                kEpiNchw, s.oh * s.ow, dtype, ws.plan, base + ws.cols + ws.weight,

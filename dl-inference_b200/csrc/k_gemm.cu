@@ -376,14 +376,8 @@ dli_status launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcParam
                      cudaStream_t stream) {
   using L = TcLayout<BN, STAGES>;
   auto kernel = tcgen05_gemm_kernel<T, BN, STAGES>;
-  static bool configured[64] = {};  // per device
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    if (e != cudaSuccess) return fail(DLI_ERR_CUDA, std::string("gemm smem attribute: ") + cudaGetErrorString(e));
-    configured[dev] = true;
-  }
+  const dli_status st = ensure_smem(reinterpret_cast<const void*>(kernel), L::kBytes, "tcgen05 gemm");
+  if (st != DLI_OK) return st;
   dim3 grid(static_cast<unsigned>(p.tiles_i * p.tiles_j), static_cast<unsigned>(splits));
   kernel<<<grid, kGemmThreads, L::kBytes, stream>>>(ma, mb, p);
   return check_launch("tcgen05 gemm");

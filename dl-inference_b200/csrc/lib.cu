@@ -1,7 +1,10 @@
 // Library-wide state of libdli_sm100.so: last-error text, device error word,
 // device properties.
+#include <atomic>
 #include <mutex>
+#include <set>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -35,11 +38,14 @@ dli_status ok() {
   return DLI_OK;
 }
 
-dli_status check_launch(const char* what) {
+std::atomic<uint64_t> g_launches{0};
+
+dli_status check_launch(const char* what, int launches) {
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) {
     return fail(DLI_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
   }
+  g_launches.fetch_add(static_cast<uint64_t>(launches), std::memory_order_relaxed);
   return ok();
 }
 
@@ -56,6 +62,20 @@ unsigned* device_error_word() {
     words[dev] = static_cast<unsigned*>(p);
   }
   return words[dev];
+}
+
+dli_status ensure_smem(const void* kernel, int bytes, const char* what) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(DLI_ERR_CUDA, std::string(what) + ": no device");
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({dev, kernel})) return DLI_OK;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    return fail(DLI_ERR_CUDA, std::string(what) + " shared-memory attribute: " + cudaGetErrorString(e));
+  done.insert({dev, kernel});
+  return DLI_OK;
 }
 
 int sm_count() {
@@ -79,6 +99,8 @@ int sm_count() {
 using namespace dli_sm100;
 
 extern "C" int dli_sm100_abi_version(void) { return DLI_SM100_ABI_VERSION; }
+
+extern "C" uint64_t dli_sm100_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" const char* dli_sm100_last_error(void) { return t_last_error.c_str(); }
 

@@ -1,0 +1,692 @@
+// libdli_sm100_ops.so — the operator plugin.
+//
+// Exports `extern "C" bool dli_register_operators(dli::OperatorRegistry*)`, the
+// entry point the runtime resolves after dlopen (src/operator_registry.cc:23-41
+// of yncxcw/dl-inference), and registers the reference's 16 operator strings
+// (linear, matmul, conv2d, rms_norm, rotary_embedding, attention, embedding,
+// add, mul, silu, relu, softmax, max_pool2d, batch_norm2d, reshape, transpose)
+// plus additive fused operators for the batched Qwen2 graphs (add_rms_norm,
+// silu_mul, qkv_rotary_cache, attention_kvcache, last_token, argmax, cast,
+// all_reduce).
+//
+// Every operator validates arity/dtype/shape on the host and throws
+// std::invalid_argument like the reference templates
+// (python/dli_ops/aot/<op>/template.cc), allocates outputs and workspace from
+// the ATen caching allocator, and launches through the C ABI of libdli_sm100.so
+// on the run's stream (ExecutionContext::cuda_stream). There is no fallback:
+// every tensor op runs a kernel of this project.
+#include <ATen/ATen.h>
+
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "dli/operator.h"
+#include "dli/utils.h"
+#include "dli_sm100.h"
+
+#ifdef DLI_WITH_NCCL
+#include <nccl.h>
+#endif
+
+namespace {
+
+using dli::Attributes;
+using dli::DType;
+using dli::ExecutionContext;
+using dli::Tensor;
+using Inputs = std::vector<const Tensor*>;
+using Outputs = std::vector<Tensor*>;
+
+dli_dtype cdt(DType d) {
+  switch (d) {
+    case DType::Float32: return DLI_DTYPE_F32;
+    case DType::Int64: return DLI_DTYPE_I64;
+    case DType::BFloat16: return DLI_DTYPE_BF16;
+    case DType::Float16: return DLI_DTYPE_F16;
+    case DType::Int32: return DLI_DTYPE_I32;
+  }
+  throw std::invalid_argument("unknown dtype");
+}
+
+void check(dli_status st, const std::string& op) {
+  if (st == DLI_OK) return;
+  const std::string msg = op + ": " + dli_sm100_last_error();
+  if (st == DLI_ERR_INVALID_ARGUMENT) throw std::invalid_argument(msg);
+  throw std::runtime_error(msg);
+}
+
+void arity(const Inputs& in, const Outputs& out, std::size_t min_in, std::size_t max_in,
+           std::size_t n_out, const std::string& op) {
+  if (in.size() < min_in || in.size() > max_in || out.size() != n_out)
+    throw std::invalid_argument(op + " arity");
+}
+
+at::Tensor workspace(std::size_t bytes, int device) {
+  if (bytes == 0) return at::Tensor();
+  return at::empty({static_cast<std::int64_t>(bytes)},
+                   at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device));
+}
+void* wsPtr(const at::Tensor& t) { return t.defined() ? t.data_ptr() : nullptr; }
+std::size_t wsBytes(const at::Tensor& t) { return t.defined() ? static_cast<std::size_t>(t.numel()) : 0; }
+
+void floatInputs(const Inputs& in, std::size_t n, const std::string& op) {
+  dli::requireCudaInputs(in, op);
+  for (std::size_t i = 0; i < n && i < in.size(); ++i) {
+    dli::requireFloat(*in[i], op);
+    if (i) dli::requireSameDtype(*in[0], *in[i], op);
+  }
+}
+
+template <typename Op>
+void reg(dli::OperatorRegistry* r, const char* name) {
+  r->registerFactory(name, [] { return std::make_unique<Op>(); });
+}
+
+// ---------------------------------------------------------------------------
+// Reference operators
+// ---------------------------------------------------------------------------
+
+// linear: y = x . W^T (+ b); python/dli_ops/aot/linear/template.cc:14-34.
+class LinearOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "linear"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
+    arity(in, out, 2, 3, 1, type());
+    floatInputs(in, in.size(), type());
+    const Tensor& x = *in[0];
+    const Tensor& w = *in[1];
+    if (w.rank() != 2) throw std::invalid_argument("linear weight must be 2-D");
+    const std::int64_t k = x.shape().back(), n = w.dim(0);
+    if (w.dim(1) != k) throw std::invalid_argument("linear weight K mismatch: " + dli::formatShape(w.shape()));
+    if (in.size() == 3 && static_cast<std::int64_t>(in[2]->numel()) != n)
+      throw std::invalid_argument("linear bias size mismatch");
+    const std::int64_t m = dli::product(x.shape(), 0, x.rank() - 1);
+    auto shape = x.shape();
+    shape.back() = n;
+    *out[0] = Tensor::cuda(x.dtype(), shape, x.deviceId());
+    const dli_dtype dt = cdt(x.dtype());
+    at::Tensor ws = workspace(dli_sm100_linear_workspace_size(m, n, k, dt), x.deviceId());
+    check(dli_sm100_linear(dli::ptr(x), dli::ptr(w), in.size() == 3 ? dli::ptr(*in[2]) : nullptr,
+                           out[0]->deviceData(), m, n, k, dt, wsPtr(ws), wsBytes(ws), ctx.cuda_stream),
+          type());
+  }
+};
+
+// matmul: out[M,N] = a[M,K] . b[K,N]; python/dli_ops/aot/matmul/template.cc:14-30.
+class MatmulOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "matmul"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
+    arity(in, out, 2, 2, 1, type());
+    floatInputs(in, 2, type());
+    const Tensor& a = *in[0];
+    const Tensor& b = *in[1];
+    if (a.rank() != 2 || b.rank() != 2 || a.dim(1) != b.dim(0))
+      throw std::invalid_argument("matmul expects [M,K] x [K,N]");
+    *out[0] = Tensor::cuda(a.dtype(), {a.dim(0), b.dim(1)}, a.deviceId());
+    check(dli_sm100_matmul(dli::ptr(a), dli::ptr(b), out[0]->deviceData(), a.dim(0), b.dim(1), a.dim(1),
+                           cdt(a.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
+// conv2d (NCHW); python/dli_ops/aot/conv2d/template.cc:1-37.
+class Conv2dOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "conv2d"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 2, 3, 1, type());
+    floatInputs(in, in.size(), type());
+    const Tensor& x = *in[0];
+    const Tensor& w = *in[1];
+    if (x.rank() != 4 || w.rank() != 4 || w.dim(1) != x.dim(1))
+      throw std::invalid_argument("conv2d expects NCHW input and [OC,C,KH,KW] weight");
+    const auto stride = dli::attrInts(attrs, "stride", {1, 1});
+    const auto pad = dli::attrInts(attrs, "padding", {0, 0});
+    if (stride.size() != 2 || pad.size() != 2) throw std::invalid_argument("conv2d stride/padding must have 2 entries");
+    const std::int64_t n = x.dim(0), c = x.dim(1), h = x.dim(2), wd = x.dim(3);
+    const std::int64_t oc = w.dim(0), kh = w.dim(2), kw = w.dim(3);
+    const std::int64_t oh = (h + 2 * pad[0] - kh) / stride[0] + 1;
+    const std::int64_t ow = (wd + 2 * pad[1] - kw) / stride[1] + 1;
+    *out[0] = Tensor::cuda(x.dtype(), {n, oc, oh, ow}, x.deviceId());
+    const dli_dtype dt = cdt(x.dtype());
+    at::Tensor ws = workspace(
+        dli_sm100_conv2d_workspace_size(n, c, h, wd, oc, kh, kw, stride[0], stride[1], pad[0], pad[1], dt),
+        x.deviceId());
+    check(dli_sm100_conv2d(dli::ptr(x), dli::ptr(w), in.size() == 3 ? dli::ptr(*in[2]) : nullptr,
+                           out[0]->deviceData(), n, c, h, wd, oc, kh, kw, stride[0], stride[1], pad[0],
+                           pad[1], dt, wsPtr(ws), wsBytes(ws), ctx.cuda_stream),
+          type());
+  }
+};
+
+// rms_norm; python/dli_ops/aot/rms_norm/template.cc:12-28 (eps default 1e-6).
+class RmsNormOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "rms_norm"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 2, 2, 1, type());
+    floatInputs(in, 2, type());
+    const Tensor& x = *in[0];
+    const std::int64_t hidden = x.shape().back();
+    if (static_cast<std::int64_t>(in[1]->numel()) != hidden) throw std::invalid_argument("rms_norm weight size mismatch");
+    const float eps = static_cast<float>(dli::attrDouble(attrs, "eps", 1e-6));
+    *out[0] = Tensor::cuda(x.dtype(), x.shape(), x.deviceId());
+    check(dli_sm100_rms_norm(dli::ptr(x), dli::ptr(*in[1]), out[0]->deviceData(),
+                             static_cast<std::int64_t>(x.numel()) / hidden, hidden, eps, cdt(x.dtype()),
+                             ctx.cuda_stream),
+          type());
+  }
+};
+
+// rotary_embedding: (q, k, cos, sin[, positions]) -> (q', k'); interleaved pairs;
+// python/dli_ops/aot/rotary/template.cc:1-28 (the reserved 5th input carries
+// int64 positions: [B] start per sequence or [B,S] per token).
+class RotaryOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "rotary_embedding"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 4, 5, 2, type());
+    dli::requireCudaInputs(in, type());
+    const Tensor& q = *in[0];
+    const Tensor& k = *in[1];
+    dli::requireFloat(q, type());
+    dli::requireSameDtype(q, k, type());
+    if (q.rank() != 4 || k.rank() != 4) throw std::invalid_argument("rotary_embedding expects [B,H,S,D] q and k");
+    if (q.dim(0) != k.dim(0) || q.dim(2) != k.dim(2) || q.dim(3) != k.dim(3))
+      throw std::invalid_argument("rotary_embedding q/k shape mismatch");
+    const Tensor& cos = *in[2];
+    const Tensor& sin = *in[3];
+    if (cos.dtype() != DType::Float32 || sin.dtype() != DType::Float32 || cos.rank() != 2 ||
+        cos.shape() != sin.shape())
+      throw std::invalid_argument("rotary_embedding expects float32 cos/sin tables [max_pos, pairs]");
+    const Tensor* pos = in.size() == 5 ? in[4] : nullptr;
+    if (pos && pos->dtype() != DType::Int64) throw std::invalid_argument("rotary_embedding positions must be int64");
+    const std::int64_t start = attrs.value_or<std::int64_t>("start_pos", 0);
+    *out[0] = Tensor::cuda(q.dtype(), q.shape(), q.deviceId());
+    *out[1] = Tensor::cuda(k.dtype(), k.shape(), k.deviceId());
+    check(dli_sm100_rotary_embedding(dli::ptr(q), dli::ptr(k), static_cast<const float*>(dli::ptr(cos)),
+                                     static_cast<const float*>(dli::ptr(sin)), out[0]->deviceData(),
+                                     out[1]->deviceData(), q.dim(0), q.dim(1), k.dim(1), q.dim(2), q.dim(3),
+                                     cos.dim(1), cos.dim(0), start,
+                                     pos ? static_cast<const std::int64_t*>(dli::ptr(*pos)) : nullptr,
+                                     pos ? static_cast<std::int64_t>(pos->numel()) : 0, cdt(q.dtype()),
+                                     ctx.cuda_stream),
+          type());
+  }
+};
+
+// attention: (q[B,Hq,Sq,D], k[B,Hkv,Sk,D], v) -> out; attrs causal, kv_cache, scale.
+// python/dli_ops/aot/attention/template.cc:1-49: with a non-empty kv_cache name
+// the new k/v are appended to the named cache entry first and q attends to all
+// cached rows.
+class AttentionOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "attention"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 3, 3, 1, type());
+    floatInputs(in, 3, type());
+    const Tensor& q = *in[0];
+    const Tensor* k = in[1];
+    const Tensor* v = in[2];
+    if (q.rank() != 4 || k->rank() != 4 || v->rank() != 4 || k->shape() != v->shape())
+      throw std::invalid_argument("attention expects [B,H,S,D] q/k/v");
+    std::int64_t seq_k = k->dim(2), capacity = k->dim(2);
+    if (attrs.contains("kv_cache")) {
+      const auto& name = attrs.require<std::string>("kv_cache");
+      if (!name.empty()) {
+        if (ctx.kv_cache == nullptr) throw std::invalid_argument("attention missing KV cache");
+        ctx.kv_cache->append(name, *in[1], *in[2], ctx.cuda_stream);
+        const dli::KVCacheEntry* e = ctx.kv_cache->get(name);
+        k = &e->key;
+        v = &e->value;
+        seq_k = e->length;
+        capacity = e->capacity();
+      }
+    }
+    if (q.dim(0) != k->dim(0) || q.dim(3) != k->dim(3) || q.dim(1) % k->dim(1) != 0)
+      throw std::invalid_argument("attention q/k shape mismatch");
+    const bool causal = attrs.value_or<bool>("causal", false);
+    const float scale = static_cast<float>(dli::attrDouble(attrs, "scale", 0.0));
+    *out[0] = Tensor::cuda(q.dtype(), q.shape(), q.deviceId());
+    const dli_dtype dt = cdt(q.dtype());
+    at::Tensor ws = workspace(
+        dli_sm100_attention_workspace_size(q.dim(0), q.dim(1), k->dim(1), q.dim(2), seq_k, q.dim(3), dt),
+        q.deviceId());
+    check(dli_sm100_attention(dli::ptr(q), dli::ptr(*k), dli::ptr(*v), out[0]->deviceData(), q.dim(0), q.dim(1),
+                              k->dim(1), q.dim(2), seq_k, capacity, q.dim(3), causal ? 1 : 0, scale, dt,
+                              wsPtr(ws), wsBytes(ws), ctx.cuda_stream),
+          type());
+  }
+};
+
+// embedding: out[..., :] = table[ids[...]]; python/dli_ops/aot/embedding/template.cc:12-31.
+class EmbeddingOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "embedding"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
+    arity(in, out, 2, 2, 1, type());
+    dli::requireCudaInputs(in, type());
+    const Tensor& ids = *in[0];
+    const Tensor& table = *in[1];
+    if (ids.dtype() != DType::Int64 && ids.dtype() != DType::Int32)
+      throw std::invalid_argument("embedding ids must be int64");
+    dli::requireFloat(table, type());
+    if (table.rank() != 2) throw std::invalid_argument("embedding table must be 2-D");
+    auto shape = ids.shape();
+    shape.push_back(table.dim(1));
+    *out[0] = Tensor::cuda(table.dtype(), shape, ids.deviceId());
+    check(dli_sm100_embedding(dli::ptr(ids), cdt(ids.dtype()), dli::ptr(table), out[0]->deviceData(),
+                              static_cast<std::int64_t>(ids.numel()), table.dim(1), table.dim(0),
+                              cdt(table.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
+// add / mul: out[i] = a[i] op b[i mod numel(b)]; python/dli_ops/aot/{add,mul}/template.cc.
+template <int kMul>
+class BinaryOp final : public dli::Operator {
+ public:
+  std::string type() const override { return kMul ? "mul" : "add"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
+    arity(in, out, 2, 2, 1, type());
+    floatInputs(in, 2, type());
+    const Tensor& a = *in[0];
+    const Tensor& b = *in[1];
+    if (b.numel() == 0 || a.numel() % b.numel() != 0)
+      throw std::invalid_argument(type() + " broadcast requires numel(a) to be a multiple of numel(b)");
+    *out[0] = Tensor::cuda(a.dtype(), a.shape(), a.deviceId());
+    const auto fn = kMul ? dli_sm100_mul : dli_sm100_add;
+    check(fn(dli::ptr(a), dli::ptr(b), out[0]->deviceData(), static_cast<std::int64_t>(a.numel()),
+             static_cast<std::int64_t>(b.numel()), cdt(a.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
+// silu / relu; python/dli_ops/aot/{silu,relu}/template.cc.
+template <int kRelu>
+class UnaryOp final : public dli::Operator {
+ public:
+  std::string type() const override { return kRelu ? "relu" : "silu"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
+    arity(in, out, 1, 1, 1, type());
+    floatInputs(in, 1, type());
+    const Tensor& x = *in[0];
+    *out[0] = Tensor::cuda(x.dtype(), x.shape(), x.deviceId());
+    const auto fn = kRelu ? dli_sm100_relu : dli_sm100_silu;
+    check(fn(dli::ptr(x), out[0]->deviceData(), static_cast<std::int64_t>(x.numel()), cdt(x.dtype()),
+             ctx.cuda_stream),
+          type());
+  }
+};
+
+// softmax over the last dim; python/dli_ops/aot/softmax/template.cc:20-37 (any width here).
+class SoftmaxOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "softmax"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
+    arity(in, out, 1, 1, 1, type());
+    floatInputs(in, 1, type());
+    const Tensor& x = *in[0];
+    const std::int64_t width = x.shape().back();
+    *out[0] = Tensor::cuda(x.dtype(), x.shape(), x.deviceId());
+    check(dli_sm100_softmax(dli::ptr(x), out[0]->deviceData(), static_cast<std::int64_t>(x.numel()) / width,
+                            width, cdt(x.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
+// max_pool2d; python/dli_ops/aot/max_pool2d/template.cc:1-30 (stride defaults to kernel_size).
+class MaxPool2dOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "max_pool2d"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 1, 1, 1, type());
+    floatInputs(in, 1, type());
+    const Tensor& x = *in[0];
+    if (x.rank() != 4) throw std::invalid_argument("max_pool2d expects NCHW input");
+    const auto ks = dli::attrInts(attrs, "kernel_size", {2, 2});
+    const auto st = dli::attrInts(attrs, "stride", ks);
+    const auto pad = dli::attrInts(attrs, "padding", {0, 0});
+    if (ks.size() != 2 || st.size() != 2 || pad.size() != 2)
+      throw std::invalid_argument("max_pool2d kernel_size/stride/padding must have 2 entries");
+    const std::int64_t oh = (x.dim(2) + 2 * pad[0] - ks[0]) / st[0] + 1;
+    const std::int64_t ow = (x.dim(3) + 2 * pad[1] - ks[1]) / st[1] + 1;
+    *out[0] = Tensor::cuda(x.dtype(), {x.dim(0), x.dim(1), oh, ow}, x.deviceId());
+    check(dli_sm100_max_pool2d(dli::ptr(x), out[0]->deviceData(), x.dim(0), x.dim(1), x.dim(2), x.dim(3), ks[0],
+                               ks[1], st[0], st[1], pad[0], pad[1], cdt(x.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
+// batch_norm2d (inference); python/dli_ops/aot/batch_norm2d/template.cc:1-33 (eps default 1e-5).
+class BatchNorm2dOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "batch_norm2d"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 5, 5, 1, type());
+    floatInputs(in, 5, type());
+    const Tensor& x = *in[0];
+    if (x.rank() != 4) throw std::invalid_argument("batch_norm2d expects NCHW input");
+    for (std::size_t i = 1; i < 5; ++i)
+      if (static_cast<std::int64_t>(in[i]->numel()) != x.dim(1))
+        throw std::invalid_argument("batch_norm2d parameter size must match input channels");
+    const float eps = static_cast<float>(dli::attrDouble(attrs, "eps", 1e-5));
+    *out[0] = Tensor::cuda(x.dtype(), x.shape(), x.deviceId());
+    check(dli_sm100_batch_norm2d(dli::ptr(x), dli::ptr(*in[1]), dli::ptr(*in[2]), dli::ptr(*in[3]),
+                                 dli::ptr(*in[4]), out[0]->deviceData(), static_cast<std::int64_t>(x.numel()),
+                                 x.dim(1), x.dim(2) * x.dim(3), eps, cdt(x.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
+// reshape: a view; python/dli_ops/aot/reshape/template.cc:1-11.
+class ReshapeOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "reshape"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext&) const override {
+    arity(in, out, 1, 1, 1, type());
+    dli::requireCudaInputs(in, type());
+    *out[0] = in[0]->withShape(dli::reshapeShape(in[0]->shape(), attrs.require<std::vector<std::int64_t>>("shape")));
+  }
+};
+
+// transpose: 2-D, perm [1,0]; python/dli_ops/aot/transpose/template.cc:1-20.
+class TransposeOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "transpose"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 1, 1, 1, type());
+    floatInputs(in, 1, type());
+    const auto perm = attrs.require<std::vector<std::int64_t>>("perm");
+    const Tensor& x = *in[0];
+    if (x.rank() != 2 || perm != std::vector<std::int64_t>({1, 0}))
+      throw std::invalid_argument("transpose supports 2D perm [1,0]");
+    *out[0] = Tensor::cuda(x.dtype(), {x.dim(1), x.dim(0)}, x.deviceId());
+    check(dli_sm100_transpose2d(dli::ptr(x), out[0]->deviceData(), x.dim(0), x.dim(1), cdt(x.dtype()),
+                                ctx.cuda_stream),
+          type());
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Additive fused operators (batched Qwen2 graphs)
+// ---------------------------------------------------------------------------
+
+// add_rms_norm: (residual, delta, weight) -> (normed, residual + delta).
+class AddRmsNormOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "add_rms_norm"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 3, 3, 2, type());
+    floatInputs(in, 3, type());
+    const Tensor& r = *in[0];
+    if (in[1]->shape() != r.shape()) throw std::invalid_argument("add_rms_norm residual/delta shape mismatch");
+    const std::int64_t hidden = r.shape().back();
+    if (static_cast<std::int64_t>(in[2]->numel()) != hidden) throw std::invalid_argument("add_rms_norm weight size mismatch");
+    const float eps = static_cast<float>(dli::attrDouble(attrs, "eps", 1e-6));
+    *out[0] = Tensor::cuda(r.dtype(), r.shape(), r.deviceId());
+    *out[1] = Tensor::cuda(r.dtype(), r.shape(), r.deviceId());
+    check(dli_sm100_add_rms_norm(dli::ptr(r), dli::ptr(*in[1]), dli::ptr(*in[2]), out[0]->deviceData(),
+                                 out[1]->deviceData(), static_cast<std::int64_t>(r.numel()) / hidden, hidden, eps,
+                                 cdt(r.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
+// silu_mul: gate_up [.., 2I] -> silu(gate) * up [.., I].
+class SiluMulOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "silu_mul"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
+    arity(in, out, 1, 1, 1, type());
+    floatInputs(in, 1, type());
+    const Tensor& x = *in[0];
+    const std::int64_t w2 = x.shape().back();
+    if (w2 % 2) throw std::invalid_argument("silu_mul expects an even last dimension");
+    auto shape = x.shape();
+    shape.back() = w2 / 2;
+    *out[0] = Tensor::cuda(x.dtype(), shape, x.deviceId());
+    check(dli_sm100_silu_mul(dli::ptr(x), out[0]->deviceData(), static_cast<std::int64_t>(x.numel()) / w2, w2 / 2,
+                             cdt(x.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
+int64_t requireIntAttr(const Attributes& attrs, const std::string& name, const std::string& op) {
+  if (!attrs.contains(name)) throw std::invalid_argument(op + " missing attribute " + name);
+  return attrs.require<std::int64_t>(name);
+}
+
+// qkv_rotary_cache: (qkv [B,S,(Hq+2Hkv)D], cos, sin, positions[B] int64) -> q [B,S,Hq,D].
+// Rotated k and raw v go to rows positions[b]+s of the kv_cache entry (reserved
+// with `capacity` rows on first use).
+class QkvRotaryCacheOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "qkv_rotary_cache"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 4, 4, 1, type());
+    dli::requireCudaInputs(in, type());
+    const Tensor& qkv = *in[0];
+    dli::requireFloat(qkv, type());
+    const Tensor& cos = *in[1];
+    const Tensor& sin = *in[2];
+    const Tensor& pos = *in[3];
+    if (cos.dtype() != DType::Float32 || sin.dtype() != DType::Float32 || cos.shape() != sin.shape() || cos.rank() != 2)
+      throw std::invalid_argument("qkv_rotary_cache expects float32 cos/sin [max_pos, pairs]");
+    if (pos.dtype() != DType::Int64) throw std::invalid_argument("qkv_rotary_cache positions must be int64");
+    const std::int64_t hq = requireIntAttr(attrs, "q_heads", type());
+    const std::int64_t hkv = requireIntAttr(attrs, "kv_heads", type());
+    const std::int64_t d = requireIntAttr(attrs, "head_dim", type());
+    const std::int64_t cap = requireIntAttr(attrs, "capacity", type());
+    const std::string& name = attrs.require<std::string>("kv_cache");
+    if (qkv.rank() != 3 || qkv.shape().back() != (hq + 2 * hkv) * d)
+      throw std::invalid_argument("qkv_rotary_cache expects qkv [B,S,(Hq+2Hkv)*D]");
+    const std::int64_t b = qkv.dim(0), s = qkv.dim(1);
+    if (static_cast<std::int64_t>(pos.numel()) != b) throw std::invalid_argument("qkv_rotary_cache positions must be [B]");
+    if (ctx.kv_cache == nullptr) throw std::invalid_argument("qkv_rotary_cache missing KV cache");
+    dli::KVCacheEntry& e = ctx.kv_cache->reserve(name, b, hkv, cap, d, qkv.dtype(), qkv.deviceId());
+    *out[0] = Tensor::cuda(qkv.dtype(), {b, s, hq, d}, qkv.deviceId());
+    check(dli_sm100_qkv_rotary_cache(dli::ptr(qkv), static_cast<const float*>(dli::ptr(cos)),
+                                     static_cast<const float*>(dli::ptr(sin)),
+                                     static_cast<const std::int64_t*>(dli::ptr(pos)), out[0]->deviceData(),
+                                     e.key.deviceData(), e.value.deviceData(), b, s, hq, hkv, d, cos.dim(1),
+                                     cos.dim(0), e.capacity(), cdt(qkv.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
+// attention_kvcache: (q [B,S,Hq,D], positions[B]) -> out [B,S,Hq*D] over the
+// kv_cache entry's rows [0, positions[b] + S), bottom-right causal.
+class AttentionKvCacheOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "attention_kvcache"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 2, 2, 1, type());
+    dli::requireCudaInputs(in, type());
+    const Tensor& q = *in[0];
+    const Tensor& pos = *in[1];
+    dli::requireFloat(q, type());
+    if (pos.dtype() != DType::Int64) throw std::invalid_argument("attention_kvcache positions must be int64");
+    if (q.rank() != 4) throw std::invalid_argument("attention_kvcache expects q [B,S,Hq,D]");
+    if (ctx.kv_cache == nullptr) throw std::invalid_argument("attention_kvcache missing KV cache");
+    const dli::KVCacheEntry* e = ctx.kv_cache->get(attrs.require<std::string>("kv_cache"));
+    if (e == nullptr) throw std::invalid_argument("attention_kvcache: unknown cache entry");
+    const std::int64_t b = q.dim(0), s = q.dim(1), hq = q.dim(2), d = q.dim(3);
+    const std::int64_t hkv = e->key.dim(1), cap = e->capacity();
+    if (e->key.dim(0) != b || e->key.dim(3) != d || hq % hkv != 0)
+      throw std::invalid_argument("attention_kvcache q/cache shape mismatch");
+    const float scale = static_cast<float>(dli::attrDouble(attrs, "scale", 0.0));
+    *out[0] = Tensor::cuda(q.dtype(), {b, s, hq * d}, q.deviceId());
+    const dli_dtype dt = cdt(q.dtype());
+    at::Tensor ws = workspace(dli_sm100_attention_kvcache_workspace_size(b, s, hq, hkv, cap, d, dt), q.deviceId());
+    check(dli_sm100_attention_kvcache(dli::ptr(q), e->key.deviceData(), e->value.deviceData(),
+                                      static_cast<const std::int64_t*>(dli::ptr(pos)), out[0]->deviceData(), b, s,
+                                      hq, hkv, cap, d, scale, dt, wsPtr(ws), wsBytes(ws), ctx.cuda_stream),
+          type());
+  }
+};
+
+// last_token: x [B,S,W] -> x[:, index] (default S-1) as [B,W].
+class LastTokenOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "last_token"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 1, 1, 1, type());
+    floatInputs(in, 1, type());
+    const Tensor& x = *in[0];
+    if (x.rank() != 3) throw std::invalid_argument("last_token expects [B,S,W]");
+    const std::int64_t index = attrs.value_or<std::int64_t>("index", x.dim(1) - 1);
+    *out[0] = Tensor::cuda(x.dtype(), {x.dim(0), x.dim(2)}, x.deviceId());
+    check(dli_sm100_select_token(dli::ptr(x), out[0]->deviceData(), x.dim(0), x.dim(1), x.dim(2), index,
+                                 cdt(x.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
+// argmax over the last dim -> int64 ids (greedy decoding).
+class ArgmaxOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "argmax"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
+    arity(in, out, 1, 1, 1, type());
+    floatInputs(in, 1, type());
+    const Tensor& x = *in[0];
+    const std::int64_t width = x.shape().back();
+    auto shape = x.shape();
+    shape.pop_back();
+    if (shape.empty()) shape.push_back(1);
+    *out[0] = Tensor::cuda(DType::Int64, shape, x.deviceId());
+    check(dli_sm100_argmax(dli::ptr(x), static_cast<std::int64_t*>(out[0]->deviceData()),
+                           static_cast<std::int64_t>(x.numel()) / width, width, cdt(x.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
+// cast: float dtype conversion, attr dtype = "float32" | "bfloat16" | "float16".
+class CastOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "cast"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 1, 1, 1, type());
+    floatInputs(in, 1, type());
+    const Tensor& x = *in[0];
+    const DType to = dli::dtypeFromString(attrs.require<std::string>("dtype"));
+    if (!dli::isFloating(to)) throw std::invalid_argument("cast target must be a float dtype");
+    *out[0] = Tensor::cuda(to, x.shape(), x.deviceId());
+    check(dli_sm100_cast(dli::ptr(x), cdt(x.dtype()), out[0]->deviceData(), cdt(to),
+                         static_cast<std::int64_t>(x.numel()), ctx.cuda_stream),
+          type());
+  }
+};
+
+// all_reduce: sum over the tensor-parallel group (identity when tp_size == 1).
+class AllReduceOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "all_reduce"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
+    arity(in, out, 1, 1, 1, type());
+    floatInputs(in, 1, type());
+    const Tensor& x = *in[0];
+    if (ctx.tp_size <= 1 || ctx.communicator == nullptr) {
+      if (ctx.tp_size > 1) throw std::invalid_argument("all_reduce: no communicator for tp_size > 1");
+      *out[0] = x;  // single rank: the sum is the input
+      return;
+    }
+#ifdef DLI_WITH_NCCL
+    *out[0] = Tensor::cuda(x.dtype(), x.shape(), x.deviceId());
+    ncclDataType_t t = x.dtype() == DType::Float32 ? ncclFloat32
+                       : x.dtype() == DType::BFloat16 ? ncclBfloat16 : ncclFloat16;
+    const ncclResult_t r = ncclAllReduce(dli::ptr(x), out[0]->deviceData(), x.numel(), t, ncclSum,
+                                         static_cast<ncclComm_t>(ctx.communicator),
+                                         static_cast<cudaStream_t>(ctx.cuda_stream));
+    if (r != ncclSuccess) throw std::runtime_error(std::string("all_reduce: ") + ncclGetErrorString(r));
+#else
+    throw std::runtime_error("all_reduce: plugin built without NCCL");
+#endif
+  }
+};
+
+}  // namespace
+
+extern "C" bool dli_register_operators(dli::OperatorRegistry* registry) {
+  if (registry == nullptr) return false;
+  if (dli_sm100_abi_version() != DLI_SM100_ABI_VERSION) return false;
+  reg<LinearOp>(registry, "linear");
+  reg<MatmulOp>(registry, "matmul");
+  reg<Conv2dOp>(registry, "conv2d");
+  reg<RmsNormOp>(registry, "rms_norm");
+  reg<RotaryOp>(registry, "rotary_embedding");
+  reg<AttentionOp>(registry, "attention");
+  reg<EmbeddingOp>(registry, "embedding");
+  reg<BinaryOp<0>>(registry, "add");
+  reg<BinaryOp<1>>(registry, "mul");
+  reg<UnaryOp<0>>(registry, "silu");
+  reg<UnaryOp<1>>(registry, "relu");
+  reg<SoftmaxOp>(registry, "softmax");
+  reg<MaxPool2dOp>(registry, "max_pool2d");
+  reg<BatchNorm2dOp>(registry, "batch_norm2d");
+  reg<ReshapeOp>(registry, "reshape");
+  reg<TransposeOp>(registry, "transpose");
+  reg<AddRmsNormOp>(registry, "add_rms_norm");
+  reg<SiluMulOp>(registry, "silu_mul");
+  reg<QkvRotaryCacheOp>(registry, "qkv_rotary_cache");
+  reg<AttentionKvCacheOp>(registry, "attention_kvcache");
+  reg<LastTokenOp>(registry, "last_token");
+  reg<ArgmaxOp>(registry, "argmax");
+  reg<CastOp>(registry, "cast");
+  reg<AllReduceOp>(registry, "all_reduce");
+  return true;
+}
+
+// ---- tensor-parallel communicator helpers (called from Python via ctypes) ----
+extern "C" int dli_sm100_plugin_has_nccl(void) {
+#ifdef DLI_WITH_NCCL
+  return 1;
+#else
+  return 0;
+#endif
+}
+
+extern "C" int dli_sm100_nccl_unique_id(void* out, int out_bytes) {
+#ifdef DLI_WITH_NCCL
+  if (out == nullptr || out_bytes < static_cast<int>(sizeof(ncclUniqueId))) return -1;
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return -2;
+  std::memcpy(out, &id, sizeof(id));
+  return static_cast<int>(sizeof(id));
+#else
+  (void)out;
+  (void)out_bytes;
+  return -3;
+#endif
+}
+
+extern "C" void* dli_sm100_nccl_comm_init(const void* id_bytes, int world, int rank, int device) {
+#ifdef DLI_WITH_NCCL
+  if (id_bytes == nullptr) return nullptr;
+  if (cudaSetDevice(device) != cudaSuccess) return nullptr;
+  ncclUniqueId id;
+  std::memcpy(&id, id_bytes, sizeof(id));
+  ncclComm_t comm = nullptr;
+  if (ncclCommInitRank(&comm, world, id, rank) != ncclSuccess) return nullptr;
+  return comm;
+#else
+  (void)id_bytes;
+  (void)world;
+  (void)rank;
+  (void)device;
+  return nullptr;
+#endif
+}
+
+extern "C" void dli_sm100_nccl_comm_destroy(void* comm) {
+#ifdef DLI_WITH_NCCL
+  if (comm) ncclCommDestroy(static_cast<ncclComm_t>(comm));
+#else
+  (void)comm;
+#endif
+}

@@ -35,6 +35,7 @@ P, I, F, D, Z, N = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_in
 # name -> (restype, argtypes); mirrors include/dli_sm100.h
 SIGNATURES = {
     "dli_sm100_abi_version": (ctypes.c_int, []),
+    "dli_sm100_launch_count": (ctypes.c_uint64, []),
     "dli_sm100_last_error": (ctypes.c_char_p, []),
     "dli_sm100_check_device_error": (N, [P]),
     "dli_sm100_linear_workspace_size": (Z, [I, I, I, D]),
@@ -82,6 +83,11 @@ def lib() -> ctypes.CDLL:
             fn.argtypes = args
         _lib = handle
     return _lib
+
+
+def launch_count() -> int:
+    """Kernels launched (or captured) by libdli_sm100.so in this process so far."""
+    return int(lib().dli_sm100_launch_count())
 
 
 def last_error() -> str:

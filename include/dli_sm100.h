@@ -50,6 +50,9 @@ typedef enum dli_status {
 /* ---- library ---------------------------------------------------------- */
 
 int dli_sm100_abi_version(void);
+/* Number of kernels this library has launched (or recorded into a CUDA graph
+ * under capture) since load; the reference has no counterpart (bookkeeping). */
+uint64_t dli_sm100_launch_count(void);
 /* Message of the last failing call on this thread ("" if none). */
 const char* dli_sm100_last_error(void);
 /* Reads and clears the device error word of the current device (synchronises
