@@ -279,7 +279,7 @@ def main() -> int:
         st = Q.random_state(shape, device=dev, dtype=torch.bfloat16, seed=1000 + i,
                             layers=range(i, i + 1), embeddings=False)
         weights.update(Q.transform_weights(st, shape, tp, tp_rank, torch.bfloat16, layers=range(i, i + 1)))
-        del st, part
+        del st
     g = torch.Generator(device=dev).manual_seed(7)
     weights["embed"] = (torch.randn(shape.vocab, shape.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
     weights["lm_head"] = weights["embed"] if shape.tie_embeddings else \

@@ -2,6 +2,7 @@
 
 #include <c10/cuda/CUDAStream.h>
 
+#include <algorithm>
 #include <stdexcept>
 #include <unordered_map>
 
@@ -13,6 +14,7 @@ struct Engine::Plan {
     const Node* node = nullptr;
     std::vector<int> in;
     std::vector<int> out;
+    std::vector<int> release;  // slots whose last reader is this step (freed after it)
   };
   std::vector<Node> nodes;  // private copy: steps point into it
   std::vector<Step> steps;
@@ -76,6 +78,21 @@ Engine::Plan& Engine::planFor(const Graph& graph) {
     plan->steps.push_back(std::move(s));
   }
   for (const auto& name : graph.outputs) plan->output_slots.push_back(plan->slot(name));
+  // Liveness: a slot is released after its last reader unless the graph returns it
+  // (when the graph lists no outputs every tensor is returned, so nothing is freed).
+  if (!graph.outputs.empty()) {
+    std::vector<int> last(plan->slot_names.size(), -1);
+    for (std::size_t i = 0; i < plan->steps.size(); ++i)
+      for (const int s : plan->steps[i].in) last[s] = static_cast<int>(i);
+    std::vector<bool> keep(plan->slot_names.size(), false);
+    for (const int s : plan->output_slots) keep[s] = true;
+    for (std::size_t s = 0; s < last.size(); ++s) {
+      if (last[s] < 0 || keep[s]) continue;
+      Plan::Step& st = plan->steps[last[s]];
+      if (std::find(st.out.begin(), st.out.end(), static_cast<int>(s)) != st.out.end()) continue;
+      st.release.push_back(static_cast<int>(s));
+    }
+  }
   for (const auto& [name, tensor] : constants_) {
     const auto s = plan->slot_of.find(name);
     if (s != plan->slot_of.end()) plan->constant_slots.emplace_back(s->second, &tensor);
@@ -132,6 +149,7 @@ TensorMap Engine::run(const Graph& graph, TensorMap inputs) {
     for (auto& t : out_storage) out.push_back(&t);
     step.op->compute(in, out, step.node->attributes, ctx);
     for (std::size_t i = 0; i < step.out.size(); ++i) slots[step.out[i]] = std::move(out_storage[i]);
+    for (const int s : step.release) slots[s] = Tensor();
   }
 
   TensorMap result;

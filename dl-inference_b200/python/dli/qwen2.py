@@ -49,8 +49,10 @@ class Qwen2Runner:
 
     # -- CUDA-graph decode ----------------------------------------------------------
     def _capture(self, batch: int):
+        # Warm-up and capture write one cache row per sequence; the last row is only
+        # read after a later step has rewritten it, so live sequences are not disturbed.
         ids = torch.zeros(batch, 1, dtype=torch.int64, device=self.device)
-        pos = torch.zeros(batch, dtype=torch.int64, device=self.device)
+        pos = torch.full((batch,), self.capacity - 1, dtype=torch.int64, device=self.device)
         stream = torch.cuda.Stream(self.device)
         stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(stream):
