@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "dli_sm100.h"
 
@@ -51,6 +52,14 @@ int sm_count();
 // Raises a kernel's dynamic shared-memory limit to `bytes` once per device.
 dli_status ensure_smem(const void* kernel, int bytes, const char* what);
 
+// Integer tuning knob read once from the environment (DLI_SM100_<name>),
+// `fallback` when unset. Knobs change launch shapes only, never the result.
+int tuning_knob(const char* name, int fallback);
+inline bool pdl_enabled() {
+  static const bool on = tuning_knob("PDL", 1) != 0;
+  return on;
+}
+
 // Dispatches a functor templated on the element type of a float dtype.
 template <typename F>
 dli_status dispatch_float(dli_dtype dtype, const char* what, F&& f) {
@@ -81,6 +90,65 @@ unsigned* device_error_word();
 
 __device__ __forceinline__ void set_device_error(unsigned* word, unsigned code) {
   if (word != nullptr) atomicCAS(word, 0u, code);
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch. Every kernel of this library is launched with
+// the programmatic-stream-serialization attribute, so it may be scheduled while
+// the previous kernel of the stream is still running. Before its first global
+// read of data a previous kernel produces and before its first global write, a
+// kernel calls pdl_wait() (griddepcontrol.wait: returns once the preceding grid
+// has completed and its memory is visible; a no-op without a programmatic
+// dependency). Only reads of operands no kernel writes (weights) may precede
+// it. pdl_trigger() lets the next kernel's CTAs be scheduled early; correctness
+// never depends on it because the next kernel's pdl_wait() still waits for this
+// grid to finish.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Entry of a kernel whose every global access may depend on the previous kernel.
+#define DLI_PDL_ENTRY()          \
+  do {                           \
+    ::dli_sm100::pdl_wait();     \
+    ::dli_sm100::pdl_trigger();  \
+  } while (0)
+
+// Launches `kernel` on `stream` with programmatic dependent launch enabled and,
+// when cluster_y > 1, thread-block clusters of (1, cluster_y, 1) CTAs.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t stream, unsigned cluster_y, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_y > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = cluster_y;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  return launch_pdl_cluster(kernel, grid, block, smem, stream, 1u, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------

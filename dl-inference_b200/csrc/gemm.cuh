@@ -17,7 +17,7 @@ struct GemmPlan {
   int stages = 0;
   int tiles_i = 0, tiles_j = 0;
   int splits = 1;
-  int kblocks = 0, kblocks_per_split = 0;
+  int kblocks = 0;
   bool tcgen05 = false;   // false -> SIMT fallback
   size_t workspace = 0;   // bytes of split-K scratch (partials + tile counters)
 };
@@ -27,11 +27,16 @@ GemmPlan plan_tn_gemm(int64_t rows_a, int64_t rows_b, int64_t k, dli_dtype dtype
 
 // Runs D = A * B^T on tcgen05 (bf16/f16 only; K % 8 == 0; A/B 16-byte aligned).
 // `ldo` is the output row stride (elements); `ohw` is used by kEpiNchw.
+// `const_a` / `const_b` mark an operand that no kernel writes (weights): its
+// first tiles are fetched before the kernel waits on the previous kernel.
+// Split-K plans need a workspace whose ticket words are zero on entry (the
+// kernel leaves them zero).
 dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, void* out,
                                int64_t rows_a, int64_t rows_b, int64_t k, int64_t lda,
                                int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,
                                dli_dtype dtype, const GemmPlan& plan, void* workspace,
-                               size_t workspace_bytes, cudaStream_t stream);
+                               size_t workspace_bytes, cudaStream_t stream, bool const_a,
+                               bool const_b);
 
 // SIMT fallback (any float dtype, any alignment): out[M,N] = A[M,K] . B + bias,
 // with B given as [N,K] (b_kmajor) or [K,N].

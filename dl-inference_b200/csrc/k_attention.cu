@@ -31,6 +31,9 @@ namespace dli_sm100 {
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMaxSplits = 16;  // split-KV partials merged per (sequence, KV head)
+// K/V stages per decode CTA: 2 (3 CTAs per SM) or 3 (2 CTAs per SM).
+static const int kDecodeStages = tuning_knob("ATTN_STAGES", 3) == 2 ? 2 : 3;
 
 struct AttnArgs {
   const void* q;
@@ -131,6 +134,7 @@ __device__ __forceinline__ void load_tile(T* smem_tile, const T* base, int r0, i
 template <typename T, int D>
 __global__ void __launch_bounds__(128)
     attn_prefill_kernel(const AttnArgs a) {
+  DLI_PDL_ENTRY();
   constexpr int BM = 64, BN = 64;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   T* sq = reinterpret_cast<T*>(smem_raw);
@@ -301,10 +305,11 @@ __global__ void __launch_bounds__(128)
 }
 
 // ---- decode (split-KV) ---------------------------------------------------------------
-template <typename T, int D>
-__global__ void __launch_bounds__(128)
+template <typename T, int D, int STAGES>
+__global__ void __launch_bounds__(128, STAGES == 2 ? 3 : 2)
     attn_decode_kernel(const AttnArgs a) {
-  constexpr int BN = 64, STAGES = 3;
+  DLI_PDL_ENTRY();
+  constexpr int BN = 64;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   T* sk = reinterpret_cast<T*>(smem_raw);           // [STAGES][BN*D]
   T* sv = sk + STAGES * BN * D;                      // [STAGES][BN*D]
@@ -520,25 +525,44 @@ __global__ void __launch_bounds__(128)
 // Merges split partials: out = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M).
 template <typename T>
 __global__ void attn_combine_kernel(const AttnArgs a) {
+  DLI_PDL_ENTRY();
+  // One thread per (query row, 4 dims); every split's (m, l) and O quad are
+  // fetched with independent loads (splits <= kMaxSplits, unrolled) so the
+  // merge costs two memory round trips.
   const int kvh = blockIdx.x, b = blockIdx.y;
   const int rows = a.group * a.seq_q;
   const int D = a.head_dim;
+  const int quads = D / 4;
   const int64_t slot0 = (static_cast<int64_t>(b) * a.hkv + kvh) * a.splits;
-  for (int i = threadIdx.x; i < rows * D; i += blockDim.x) {
-    const int r = i / D, d = i - r * D;
+  for (int i = threadIdx.x; i < rows * quads; i += blockDim.x) {
+    const int r = i / quads, d = (i - r * quads) * 4;
+    float ms[kMaxSplits];
     float m = -INFINITY;
-    for (int s = 0; s < a.splits; ++s) m = fmaxf(m, a.part_ml[(slot0 + s) * 32 + r * 2]);
-    float l = 0.f, acc = 0.f;
-    for (int s = 0; s < a.splits; ++s) {
-      const float ms = a.part_ml[(slot0 + s) * 32 + r * 2];
-      if (ms == -INFINITY) continue;
-      const float w = exp2f(ms - m);
-      l += a.part_ml[(slot0 + s) * 32 + r * 2 + 1] * w;
-      acc += a.part_o[(slot0 + s) * 16 * D + r * D + d] * w;
+#pragma unroll
+    for (int s = 0; s < kMaxSplits; ++s) {
+      ms[s] = s < a.splits ? a.part_ml[(slot0 + s) * 32 + r * 2] : -INFINITY;
+      m = fmaxf(m, ms[s]);
     }
+    float l = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < kMaxSplits; ++s) {
+      if (s >= a.splits || ms[s] == -INFINITY) continue;
+      const float w = exp2f(ms[s] - m);
+      l += a.part_ml[(slot0 + s) * 32 + r * 2 + 1] * w;
+      const float4 o = *reinterpret_cast<const float4*>(a.part_o + (slot0 + s) * 16 * D + r * D + d);
+      acc.x += o.x * w;
+      acc.y += o.y * w;
+      acc.z += o.z * w;
+      acc.w += o.w * w;
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
     const int sq = r / a.group, hh = kvh * a.group + (r - sq * a.group);
     T* dst = static_cast<T*>(a.out) + b * a.o_sb + hh * a.o_sh + sq * a.o_ss + d;
-    *dst = from_f32<T>(l > 0.f ? acc / l : 0.f);
+    dst[0] = from_f32<T>(acc.x * inv);
+    dst[1] = from_f32<T>(acc.y * inv);
+    dst[2] = from_f32<T>(acc.z * inv);
+    dst[3] = from_f32<T>(acc.w * inv);
   }
 }
 
@@ -548,6 +572,7 @@ __global__ void attn_combine_kernel(const AttnArgs a) {
 // each lane accumulates its own dims of O. Exact fp32 math with expf.
 template <typename T>
 __global__ void attn_fallback_kernel(const AttnArgs a) {
+  DLI_PDL_ENTRY();
   extern __shared__ float sqf[];  // [warps][D]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
@@ -620,12 +645,18 @@ DecodePlan plan_decode(int64_t batch, int64_t hkv, int64_t group, int64_t seq_q,
   DecodePlan p;
   if (group * seq_q > 16) return p;
   p.decode = true;
+  // Enough CTAs for ~4 waves at 3 resident CTAs per SM (short tails), with at
+  // least two 64-key blocks per split so each CTA amortises its prologue.
   const int64_t pairs = batch * hkv;
   const int64_t blocks = std::max<int64_t>(1, ceil_div(max_kv, 64));
-  const int64_t target = 2 * sm_count();
+  // Few, long splits measure best: each split pays a pipeline fill, a 4-warp
+  // merge and a partial round trip, so splits only need to fill the SMs once.
+  static const int kWaves = tuning_knob("ATTN_WAVES", 1);
+  static const int kMinBlocks = std::max(1, tuning_knob("ATTN_MIN_BLOCKS", 1));
+  const int64_t target = static_cast<int64_t>(kWaves) * (kDecodeStages == 2 ? 3 : 2) * sm_count();
   int64_t splits = std::max<int64_t>(1, ceil_div(target, pairs));
-  splits = std::min<int64_t>(splits, blocks);
-  splits = std::min<int64_t>(splits, 64);
+  splits = std::min<int64_t>(splits, std::max<int64_t>(1, blocks / kMinBlocks));
+  splits = std::min<int64_t>(splits, kMaxSplits);
   p.splits = static_cast<int>(splits);
   if (p.splits > 1)
     p.workspace = static_cast<size_t>(pairs * p.splits) * (16 * head_dim + 32) * sizeof(float);
@@ -634,18 +665,26 @@ DecodePlan plan_decode(int64_t batch, int64_t hkv, int64_t group, int64_t seq_q,
 
 bool tc_head_dim(int64_t d) { return d == 64 || d == 128; }
 
+template <typename T, int D, int STAGES>
+dli_status launch_decode(const AttnArgs& args, const DecodePlan& plan, cudaStream_t stream) {
+  constexpr int kSmem = 2 * STAGES * 64 * D * 2 + 16 * D * 4 + 128 * 4;
+  auto kern = attn_decode_kernel<T, D, STAGES>;
+  const dli_status st = ensure_smem(reinterpret_cast<const void*>(kern), kSmem, "attention decode");
+  if (st != DLI_OK) return st;
+  dim3 grid(plan.splits, args.hkv, args.batch);
+  launch_pdl(kern, grid, dim3(128), kSmem, stream, args);
+  return DLI_OK;
+}
+
 template <typename T, int D>
 dli_status launch_tc_attention(const AttnArgs& args, const DecodePlan& plan, cudaStream_t stream) {
   if (plan.decode) {
-    constexpr int kSmem = 2 * 3 * 64 * D * 2 + 16 * D * 4 + 128 * 4;
-    auto kern = attn_decode_kernel<T, D>;
-    const dli_status st = ensure_smem(reinterpret_cast<const void*>(kern), kSmem, "attention decode");
+    const dli_status st = kDecodeStages == 3 ? launch_decode<T, D, 3>(args, plan, stream)
+                                             : launch_decode<T, D, 2>(args, plan, stream);
     if (st != DLI_OK) return st;
-    dim3 grid(plan.splits, args.hkv, args.batch);
-    kern<<<grid, 128, kSmem, stream>>>(args);
     if (plan.splits > 1) {
       dim3 cg(args.hkv, args.batch);
-      attn_combine_kernel<T><<<cg, 256, 0, stream>>>(args);
+      launch_pdl(attn_combine_kernel<T>, cg, dim3(256), 0, stream, args);
     }
     return check_launch("attention decode", plan.splits > 1 ? 2 : 1);
   }
@@ -654,7 +693,7 @@ dli_status launch_tc_attention(const AttnArgs& args, const DecodePlan& plan, cud
   const dli_status st = ensure_smem(reinterpret_cast<const void*>(kern), kSmem, "attention prefill");
   if (st != DLI_OK) return st;
   dim3 grid(static_cast<unsigned>(ceil_div(args.seq_q, 64)), args.hq, args.batch);
-  kern<<<grid, 128, kSmem, stream>>>(args);
+  launch_pdl(kern, grid, dim3(128), kSmem, stream, args);
   return check_launch("attention prefill");
 }
 
@@ -686,7 +725,7 @@ dli_status run_attention(AttnArgs& args, dli_dtype dtype, int64_t max_kv, void* 
   const size_t smem = warps * args.head_dim * sizeof(float);
   const dli_status st = dispatch_float(dtype, "attention", [&](auto tag) {
     using T = decltype(tag);
-    attn_fallback_kernel<T><<<grid, warps * 32, smem, stream>>>(args);
+    launch_pdl(attn_fallback_kernel<T>, dim3(grid), dim3(warps * 32), smem, stream, args);
   });
   if (st != DLI_OK) return st;
   return check_launch("attention fallback");

@@ -23,6 +23,7 @@ struct ConvShape {
 
 template <typename T>
 __global__ void im2col_kernel(const T* __restrict__ x, T* __restrict__ cols, ConvShape s) {
+  DLI_PDL_ENTRY();
   const int64_t kp = s.kp(), k = s.k();
   const int64_t total = s.m() * kp;
   const int64_t ohw = s.oh * s.ow;
@@ -45,6 +46,7 @@ __global__ void im2col_kernel(const T* __restrict__ x, T* __restrict__ cols, Con
 template <typename T>
 __global__ void pad_weight_kernel(const T* __restrict__ w, T* __restrict__ wp, int64_t oc, int64_t k,
                                   int64_t kp) {
+  DLI_PDL_ENTRY();
   const int64_t total = oc * kp;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -56,6 +58,7 @@ __global__ void pad_weight_kernel(const T* __restrict__ w, T* __restrict__ wp, i
 template <typename T>
 __global__ void conv_direct_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                    const T* __restrict__ bias, T* __restrict__ out, ConvShape s) {
+  DLI_PDL_ENTRY();
   const int64_t total = s.n * s.oc * s.oh * s.ow;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -153,11 +156,10 @@ extern "C" dli_status dli_sm100_conv2d(const void* x, const void* weight, const 
     const void* wk = weight;
     st = dispatch_float(dtype, "conv2d", [&](auto tag) {
       using T = decltype(tag);
-      im2col_kernel<T><<<grid_for(s.m() * s.kp()), 256, 0, cs>>>((const T*)x, (T*)cols, s);
+      launch_pdl(im2col_kernel<T>, grid_for(s.m() * s.kp()), 256, 0, cs, (const T*)x, (T*)cols, s);
       if (ws.weight) {
-        pad_weight_kernel<T><<<grid_for(s.oc * s.kp()), 256, 0, cs>>>((const T*)weight,
-                                                                      (T*)(base + ws.cols), s.oc,
-                                                                      s.k(), s.kp());
+        launch_pdl(pad_weight_kernel<T>, grid_for(s.oc * s.kp()), 256, 0, cs, (const T*)weight,
+                   (T*)(base + ws.cols), s.oc, s.k(), s.kp());
         wk = base + ws.cols;
       }
     });
@@ -166,12 +168,12 @@ extern "C" dli_status dli_sm100_conv2d(const void* x, const void* weight, const 
     if (st != DLI_OK) return st;
     return run_tn_gemm_tcgen05(cols, wk, bias, out, s.m(), s.oc, s.kp(), s.kp(), s.kp(), 0,
                                kEpiNchw, s.oh * s.ow, dtype, ws.plan, base + ws.cols + ws.weight,
-                               ws.gemm, cs);
+                               ws.gemm, cs, false, ws.weight == 0);
   }
   st = dispatch_float(dtype, "conv2d", [&](auto tag) {
     using T = decltype(tag);
-    conv_direct_kernel<T><<<grid_for(s.n * s.oc * s.oh * s.ow), 256, 0, cs>>>(
-        (const T*)x, (const T*)weight, (const T*)bias, (T*)out, s);
+    launch_pdl(conv_direct_kernel<T>, grid_for(s.n * s.oc * s.oh * s.ow), 256, 0, cs, (const T*)x,
+               (const T*)weight, (const T*)bias, (T*)out, s);
   });
   if (st != DLI_OK) return st;
   return check_launch("conv2d direct");

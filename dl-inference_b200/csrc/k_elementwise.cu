@@ -1,7 +1,8 @@
 // Bandwidth kernels: broadcast add/mul, activations, SwiGLU, embedding gather,
 // transpose, pooling, batch norm, softmax, argmax, token select, casts and the
 // KV-cache append. All use 16-byte vector accesses where shape and alignment
-// allow, fp32 arithmetic, and grid-stride loops sized to the SM count.
+// allow, fp32 arithmetic, grid-stride loops sized to the SM count, and
+// programmatic dependent launch (pdl_wait before the first global access).
 #include <algorithm>
 #include <cfloat>
 
@@ -20,7 +21,7 @@ inline unsigned grid_for(int64_t work_items, int threads = kThreads) {
 
 // ---- broadcast binary ------------------------------------------------------
 // out[i] = op(a[i], b[i mod width])  (python/dli_ops/aot/add/kernel.py:8-11)
-template <typename T, int OP>
+template <int OP>
 __device__ __forceinline__ float binop(float x, float y) {
   return OP == 0 ? x + y : x * y;
 }
@@ -28,6 +29,7 @@ __device__ __forceinline__ float binop(float x, float y) {
 template <typename T, int OP>
 __global__ void broadcast_vec_kernel(const T* __restrict__ a, const T* __restrict__ b,
                                      T* __restrict__ out, int64_t nvec, int64_t width) {
+  DLI_PDL_ENTRY();
   constexpr int V = Vec16<T>::N;
   for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
        v += (int64_t)gridDim.x * blockDim.x) {
@@ -36,7 +38,7 @@ __global__ void broadcast_vec_kernel(const T* __restrict__ a, const T* __restric
     Vec16<T> y = load16(b + (i % width));
     Vec16<T> r;
 #pragma unroll
-    for (int j = 0; j < V; ++j) r.e[j] = from_f32<T>(binop<T, OP>(to_f32(x.e[j]), to_f32(y.e[j])));
+    for (int j = 0; j < V; ++j) r.e[j] = from_f32<T>(binop<OP>(to_f32(x.e[j]), to_f32(y.e[j])));
     store16(out + i, r);
   }
 }
@@ -44,9 +46,10 @@ __global__ void broadcast_vec_kernel(const T* __restrict__ a, const T* __restric
 template <typename T, int OP>
 __global__ void broadcast_scalar_kernel(const T* __restrict__ a, const T* __restrict__ b,
                                         T* __restrict__ out, int64_t total, int64_t width) {
+  DLI_PDL_ENTRY();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    out[i] = from_f32<T>(binop<T, OP>(to_f32(a[i]), to_f32(b[i % width])));
+    out[i] = from_f32<T>(binop<OP>(to_f32(a[i]), to_f32(b[i % width])));
   }
 }
 
@@ -62,11 +65,11 @@ dli_status broadcast(const void* a, const void* b, void* out, int64_t total, int
     const bool vec = total % V == 0 && width % V == 0 && aligned(a, 16) && aligned(b, 16) && aligned(out, 16);
     if (vec) {
       const int64_t nvec = total / V;
-      broadcast_vec_kernel<T, OP><<<grid_for(nvec), kThreads, 0, as_stream(stream)>>>(
-          (const T*)a, (const T*)b, (T*)out, nvec, width);
+      launch_pdl(broadcast_vec_kernel<T, OP>, grid_for(nvec), kThreads, 0, as_stream(stream),
+                 (const T*)a, (const T*)b, (T*)out, nvec, width);
     } else {
-      broadcast_scalar_kernel<T, OP><<<grid_for(total), kThreads, 0, as_stream(stream)>>>(
-          (const T*)a, (const T*)b, (T*)out, total, width);
+      launch_pdl(broadcast_scalar_kernel<T, OP>, grid_for(total), kThreads, 0, as_stream(stream),
+                 (const T*)a, (const T*)b, (T*)out, total, width);
     }
   });
   if (st != DLI_OK) return st;
@@ -82,6 +85,7 @@ __device__ __forceinline__ float act(float x) {
 
 template <typename T, int ACT>
 __global__ void unary_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t total) {
+  DLI_PDL_ENTRY();
   constexpr int V = Vec16<T>::N;
   const int64_t nvec = total / V;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -97,6 +101,7 @@ __global__ void unary_kernel(const T* __restrict__ x, T* __restrict__ out, int64
 
 template <typename T, int ACT>
 __global__ void unary_scalar_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t total) {
+  DLI_PDL_ENTRY();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x)
     out[i] = from_f32<T>(act<ACT>(to_f32(x[i])));
@@ -111,11 +116,11 @@ dli_status unary(const void* x, void* out, int64_t total, dli_dtype dtype, void*
   dli_status st = dispatch_float(dtype, name, [&](auto tag) {
     using T = decltype(tag);
     if (aligned(x, 16) && aligned(out, 16))
-      unary_kernel<T, ACT><<<grid_for(ceil_div(total, Vec16<T>::N)), kThreads, 0, as_stream(stream)>>>(
-          (const T*)x, (T*)out, total);
+      launch_pdl(unary_kernel<T, ACT>, grid_for(ceil_div(total, Vec16<T>::N)), kThreads, 0,
+                 as_stream(stream), (const T*)x, (T*)out, total);
     else
-      unary_scalar_kernel<T, ACT><<<grid_for(total), kThreads, 0, as_stream(stream)>>>(
-          (const T*)x, (T*)out, total);
+      launch_pdl(unary_scalar_kernel<T, ACT>, grid_for(total), kThreads, 0, as_stream(stream),
+                 (const T*)x, (T*)out, total);
   });
   if (st != DLI_OK) return st;
   return check_launch(name);
@@ -128,6 +133,7 @@ dli_status unary(const void* x, void* out, int64_t total, dli_dtype dtype, void*
 template <typename T>
 __global__ void silu_mul_vec_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t rows,
                                     int64_t width) {
+  DLI_PDL_ENTRY();
   constexpr int V = Vec16<T>::N;
   const int64_t per_row = width / V;
   const int64_t total = rows * per_row;
@@ -149,6 +155,7 @@ __global__ void silu_mul_vec_kernel(const T* __restrict__ gu, T* __restrict__ ou
 template <typename T>
 __global__ void silu_mul_scalar_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t rows,
                                        int64_t width) {
+  DLI_PDL_ENTRY();
   const int64_t total = rows * width;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -164,6 +171,7 @@ template <typename T, typename I>
 __global__ void embedding_kernel(const I* __restrict__ ids, const T* __restrict__ table,
                                  T* __restrict__ out, int64_t total, int64_t hidden, int64_t vocab,
                                  bool vec, unsigned* err) {
+  DLI_PDL_ENTRY();
   constexpr int V = Vec16<T>::N;
   for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
     const int64_t id = static_cast<int64_t>(ids[t]);
@@ -189,6 +197,7 @@ __global__ void embedding_kernel(const I* __restrict__ ids, const T* __restrict_
 template <typename T>
 __global__ void transpose_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t rows,
                                  int64_t cols) {
+  DLI_PDL_ENTRY();
   __shared__ T tile[32][33];
   const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -206,8 +215,9 @@ __global__ void transpose_kernel(const T* __restrict__ x, T* __restrict__ out, i
 // python/dli_ops/aot/max_pool2d/kernel.py:24-41: out-of-range taps read -inf.
 template <typename T>
 __global__ void max_pool2d_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t total,
-                                  int c, int h, int w, int oh, int ow, int kh, int kw, int sh,
-                                  int sw, int ph, int pw) {
+                                  int h, int w, int oh, int ow, int kh, int kw, int sh, int sw,
+                                  int ph, int pw) {
+  DLI_PDL_ENTRY();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int ox = static_cast<int>(i % ow);
@@ -226,7 +236,6 @@ __global__ void max_pool2d_kernel(const T* __restrict__ x, T* __restrict__ out, 
     }
     out[i] = from_f32<T>(acc);
   }
-  (void)c;
 }
 
 // ---- batch norm (inference) -----------------------------------------------------
@@ -236,6 +245,7 @@ __global__ void batch_norm2d_kernel(const T* __restrict__ x, const T* __restrict
                                     const T* __restrict__ bias, const T* __restrict__ mean,
                                     const T* __restrict__ var, T* __restrict__ out, int64_t total,
                                     int64_t channels, int64_t spatial, float eps) {
+  DLI_PDL_ENTRY();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t ch = (i / spatial) % channels;
@@ -250,6 +260,7 @@ __global__ void batch_norm2d_kernel(const T* __restrict__ x, const T* __restrict
 template <typename T>
 __global__ void softmax_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t rows,
                                int64_t width) {
+  DLI_PDL_ENTRY();
   __shared__ float scratch[32];
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const T* row = x + r * width;
@@ -269,13 +280,42 @@ __global__ void softmax_kernel(const T* __restrict__ x, T* __restrict__ out, int
 template <typename T>
 __global__ void argmax_kernel(const T* __restrict__ x, int64_t* __restrict__ out, int64_t rows,
                               int64_t width) {
+  DLI_PDL_ENTRY();
   __shared__ float sval[32];
   __shared__ int64_t sidx[32];
+  constexpr int V = Vec16<T>::N;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const T* row = x + r * width;
     float best = -INFINITY;
     int64_t best_i = width;  // sentinel larger than any index
-    for (int64_t c = threadIdx.x; c < width; c += blockDim.x) {
+    // 16-byte loads, 4 in flight per thread; the scalar loop takes the tail and
+    // rows whose start is not 16-byte aligned.
+    const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+    const int64_t nvec = vec ? width / V : 0;
+    int64_t v0 = threadIdx.x;
+    for (; v0 + 3 * (int64_t)blockDim.x < nvec; v0 += 4 * (int64_t)blockDim.x) {
+      Vec16<T> pk[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) pk[u] = load16(row + (v0 + u * (int64_t)blockDim.x) * V);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+          const float v = to_f32(pk[u].e[j]);
+          const int64_t c = (v0 + u * (int64_t)blockDim.x) * V + j;
+          if (v > best || (v == best && c < best_i)) { best = v; best_i = c; }
+        }
+    }
+    for (; v0 < nvec; v0 += blockDim.x) {
+      const Vec16<T> pk = load16(row + v0 * V);
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        const float v = to_f32(pk.e[j]);
+        const int64_t c = v0 * V + j;
+        if (v > best || (v == best && c < best_i)) { best = v; best_i = c; }
+      }
+    }
+    for (int64_t c = nvec * V + threadIdx.x; c < width; c += blockDim.x) {
       const float v = to_f32(row[c]);
       if (v > best || (v == best && c < best_i)) { best = v; best_i = c; }
     }
@@ -307,6 +347,7 @@ __global__ void argmax_kernel(const T* __restrict__ x, int64_t* __restrict__ out
 template <typename T>
 __global__ void select_token_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t batch,
                                     int64_t seq, int64_t width, int64_t index) {
+  DLI_PDL_ENTRY();
   for (int64_t b = blockIdx.x; b < batch; b += gridDim.x) {
     const T* src = x + (b * seq + index) * width;
     for (int64_t c = threadIdx.x; c < width; c += blockDim.x) out[b * width + c] = src[c];
@@ -316,6 +357,7 @@ __global__ void select_token_kernel(const T* __restrict__ x, T* __restrict__ out
 // ---- cast -------------------------------------------------------------------------------
 template <typename S, typename D>
 __global__ void cast_kernel(const S* __restrict__ x, D* __restrict__ out, int64_t n) {
+  DLI_PDL_ENTRY();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     out[i] = from_f32<D>(to_f32(x[i]));
@@ -327,6 +369,7 @@ template <typename T>
 __global__ void kv_append_kernel(T* __restrict__ ck, T* __restrict__ cv, const T* __restrict__ k,
                                  const T* __restrict__ v, int64_t bh, int64_t cap, int64_t old_len,
                                  int64_t new_len, int64_t d) {
+  DLI_PDL_ENTRY();
   const int64_t total = bh * new_len * d;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -373,11 +416,11 @@ extern "C" dli_status dli_sm100_silu_mul(const void* gate_up, void* out, int64_t
     using T = decltype(tag);
     constexpr int V = Vec16<T>::N;
     if (width % V == 0 && aligned(gate_up, 16) && aligned(out, 16))
-      silu_mul_vec_kernel<T><<<grid_for(rows * width / V), kThreads, 0, as_stream(stream)>>>(
-          (const T*)gate_up, (T*)out, rows, width);
+      launch_pdl(silu_mul_vec_kernel<T>, grid_for(rows * width / V), kThreads, 0, as_stream(stream),
+                 (const T*)gate_up, (T*)out, rows, width);
     else
-      silu_mul_scalar_kernel<T><<<grid_for(rows * width), kThreads, 0, as_stream(stream)>>>(
-          (const T*)gate_up, (T*)out, rows, width);
+      launch_pdl(silu_mul_scalar_kernel<T>, grid_for(rows * width), kThreads, 0, as_stream(stream),
+                 (const T*)gate_up, (T*)out, rows, width);
   });
   if (st != DLI_OK) return st;
   return check_launch("silu_mul");
@@ -399,11 +442,11 @@ extern "C" dli_status dli_sm100_embedding(const void* ids, dli_dtype ids_dtype, 
     const bool vec = hidden % Vec16<T>::N == 0 && aligned(table, 16) && aligned(out, 16);
     const int threads = hidden >= 1024 ? 256 : 128;
     if (ids_dtype == DLI_DTYPE_I64)
-      embedding_kernel<T, int64_t><<<grid, threads, 0, as_stream(stream)>>>(
-          (const int64_t*)ids, (const T*)table, (T*)out, total, hidden, vocab, vec, err);
+      launch_pdl(embedding_kernel<T, int64_t>, grid, threads, 0, as_stream(stream),
+                 (const int64_t*)ids, (const T*)table, (T*)out, total, hidden, vocab, vec, err);
     else
-      embedding_kernel<T, int32_t><<<grid, threads, 0, as_stream(stream)>>>(
-          (const int32_t*)ids, (const T*)table, (T*)out, total, hidden, vocab, vec, err);
+      launch_pdl(embedding_kernel<T, int32_t>, grid, threads, 0, as_stream(stream),
+                 (const int32_t*)ids, (const T*)table, (T*)out, total, hidden, vocab, vec, err);
   });
   if (st != DLI_OK) return st;
   return check_launch("embedding");
@@ -418,7 +461,7 @@ extern "C" dli_status dli_sm100_transpose2d(const void* x, void* out, int64_t ro
   dim3 block(32, 8);
   dli_status st = dispatch_float(dtype, "transpose", [&](auto tag) {
     using T = decltype(tag);
-    transpose_kernel<T><<<grid, block, 0, as_stream(stream)>>>((const T*)x, (T*)out, rows, cols);
+    launch_pdl(transpose_kernel<T>, grid, block, 0, as_stream(stream), (const T*)x, (T*)out, rows, cols);
   });
   if (st != DLI_OK) return st;
   return check_launch("transpose");
@@ -438,9 +481,9 @@ extern "C" dli_status dli_sm100_max_pool2d(const void* x, void* out, int64_t n, 
   if (total == 0) return ok();
   dli_status st = dispatch_float(dtype, "max_pool2d", [&](auto tag) {
     using T = decltype(tag);
-    max_pool2d_kernel<T><<<grid_for(total), kThreads, 0, as_stream(stream)>>>(
-        (const T*)x, (T*)out, total, (int)c, (int)h, (int)w, (int)oh, (int)ow, (int)kh, (int)kw,
-        (int)stride_h, (int)stride_w, (int)pad_h, (int)pad_w);
+    launch_pdl(max_pool2d_kernel<T>, grid_for(total), kThreads, 0, as_stream(stream), (const T*)x,
+               (T*)out, total, (int)h, (int)w, (int)oh, (int)ow, (int)kh, (int)kw, (int)stride_h,
+               (int)stride_w, (int)pad_h, (int)pad_w);
   });
   if (st != DLI_OK) return st;
   return check_launch("max_pool2d");
@@ -456,9 +499,9 @@ extern "C" dli_status dli_sm100_batch_norm2d(const void* x, const void* weight, 
   if (total == 0) return ok();
   dli_status st = dispatch_float(dtype, "batch_norm2d", [&](auto tag) {
     using T = decltype(tag);
-    batch_norm2d_kernel<T><<<grid_for(total), kThreads, 0, as_stream(stream)>>>(
-        (const T*)x, (const T*)weight, (const T*)bias, (const T*)running_mean,
-        (const T*)running_var, (T*)out, total, channels, spatial, eps);
+    launch_pdl(batch_norm2d_kernel<T>, grid_for(total), kThreads, 0, as_stream(stream), (const T*)x,
+               (const T*)weight, (const T*)bias, (const T*)running_mean, (const T*)running_var,
+               (T*)out, total, channels, spatial, eps);
   });
   if (st != DLI_OK) return st;
   return check_launch("batch_norm2d");
@@ -472,7 +515,7 @@ extern "C" dli_status dli_sm100_softmax(const void* x, void* out, int64_t rows, 
   const int threads = width >= 1024 ? 256 : (width >= 128 ? 128 : 32);
   dli_status st = dispatch_float(dtype, "softmax", [&](auto tag) {
     using T = decltype(tag);
-    softmax_kernel<T><<<grid, threads, 0, as_stream(stream)>>>((const T*)x, (T*)out, rows, width);
+    launch_pdl(softmax_kernel<T>, grid, threads, 0, as_stream(stream), (const T*)x, (T*)out, rows, width);
   });
   if (st != DLI_OK) return st;
   return check_launch("softmax");
@@ -485,7 +528,7 @@ extern "C" dli_status dli_sm100_argmax(const void* x, int64_t* out_ids, int64_t 
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, sm_count() * 16));
   dli_status st = dispatch_float(dtype, "argmax", [&](auto tag) {
     using T = decltype(tag);
-    argmax_kernel<T><<<grid, 1024, 0, as_stream(stream)>>>((const T*)x, out_ids, rows, width);
+    launch_pdl(argmax_kernel<T>, grid, 1024, 0, as_stream(stream), (const T*)x, out_ids, rows, width);
   });
   if (st != DLI_OK) return st;
   return check_launch("argmax");
@@ -500,8 +543,8 @@ extern "C" dli_status dli_sm100_select_token(const void* x, void* out, int64_t b
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(batch, 65535));
   dli_status st = dispatch_float(dtype, "select_token", [&](auto tag) {
     using T = decltype(tag);
-    select_token_kernel<T><<<grid, 256, 0, as_stream(stream)>>>((const T*)x, (T*)out, batch, seq,
-                                                                 width, index);
+    launch_pdl(select_token_kernel<T>, grid, 256, 0, as_stream(stream), (const T*)x, (T*)out, batch,
+               seq, width, index);
   });
   if (st != DLI_OK) return st;
   return check_launch("select_token");
@@ -516,7 +559,7 @@ extern "C" dli_status dli_sm100_cast(const void* x, dli_dtype x_dtype, void* out
     using S = decltype(stag);
     inner = dispatch_float(out_dtype, "cast", [&](auto dtag) {
       using D = decltype(dtag);
-      cast_kernel<S, D><<<grid_for(n), kThreads, 0, as_stream(stream)>>>((const S*)x, (D*)out, n);
+      launch_pdl(cast_kernel<S, D>, grid_for(n), kThreads, 0, as_stream(stream), (const S*)x, (D*)out, n);
     });
   });
   if (st != DLI_OK) return st;
@@ -536,9 +579,9 @@ extern "C" dli_status dli_sm100_kv_append(void* cache_k, void* cache_v, const vo
   if (total == 0) return ok();
   dli_status st = dispatch_float(dtype, "kv_append", [&](auto tag) {
     using T = decltype(tag);
-    kv_append_kernel<T><<<grid_for(total), kThreads, 0, as_stream(stream)>>>(
-        (T*)cache_k, (T*)cache_v, (const T*)k, (const T*)v, batch * heads, capacity, old_len,
-        new_len, head_dim);
+    launch_pdl(kv_append_kernel<T>, grid_for(total), kThreads, 0, as_stream(stream), (T*)cache_k,
+               (T*)cache_v, (const T*)k, (const T*)v, batch * heads, capacity, old_len, new_len,
+               head_dim);
   });
   if (st != DLI_OK) return st;
   return check_launch("kv_append");

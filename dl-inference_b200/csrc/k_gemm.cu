@@ -44,19 +44,21 @@ struct TcLayout {
   static constexpr int kBytes = kBarOffset + (2 * STAGES + 1) * 8 + 16 + 1024;
   static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KiB alignment");
+  // the split-K partial tile [128][BN + 4] fp32 is staged in the idle operand ring
+  static_assert(kBM * (BN + 4) * 4 <= kBarOffset, "split-K staging must fit the operand ring");
 };
 
 struct TcParams {
   int rows_a, rows_b;
   int tiles_i, tiles_j;
-  int kblocks, kpb, splits;
+  int kblocks, splits;  // splits > 1: the grid's y CTAs of a tile form one cluster
   int epilogue;
   int64_t ldo, ohw;
   int out_vec;  // output base is 16-byte aligned
+  int const_a;  // operand A is read-only weights: its first tiles load before pdl_wait
+  int const_b;  // same for operand B
   const void* bias;
   void* out;
-  float* partials;
-  unsigned* counters;
   unsigned* err;
 };
 
@@ -70,14 +72,17 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_i, int tiles_j, 
   tj = r / gsize;
 }
 
+// Writes n (<= 32) accumulator values of D row `gi`, columns jc.. through the
+// epilogue mapping, adding the bias.
 template <typename T>
-__device__ __forceinline__ void store_chunk(const TcParams& p, int64_t gi, int jc, const float* v) {
+__device__ __forceinline__ void store_vals(const TcParams& p, int64_t gi, int jc, const float* v,
+                                           int n) {
   const T* bias = static_cast<const T*>(p.bias);
   T* out = static_cast<T*>(p.out);
   if (gi >= p.rows_a) return;
   if (p.epilogue == kEpiRowMajor) {
     T* dst = out + gi * p.ldo + jc;
-    if (p.out_vec && jc + 32 <= p.rows_b && (p.ldo % 8) == 0) {
+    if (n == 32 && p.out_vec && jc + 32 <= p.rows_b && (p.ldo % 8) == 0) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         Vec16<T> pack;
@@ -90,18 +95,18 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int64_t gi, int j
         store16(dst + q * 8, pack);
       }
     } else {
-      for (int k = 0; k < 32 && jc + k < p.rows_b; ++k) {
+      for (int k = 0; k < n && jc + k < p.rows_b; ++k) {
         const float bv = bias ? to_f32(bias[jc + k]) : 0.f;
         dst[k] = from_f32<T>(v[k] + bv);
       }
     }
   } else if (p.epilogue == kEpiTransposed) {
     const float bv = bias ? to_f32(bias[gi]) : 0.f;
-    for (int k = 0; k < 32 && jc + k < p.rows_b; ++k)
+    for (int k = 0; k < n && jc + k < p.rows_b; ++k)
       out[static_cast<int64_t>(jc + k) * p.ldo + gi] = from_f32<T>(v[k] + bv);
   } else {  // kEpiNchw
     const int64_t img = gi / p.ohw, pix = gi - img * p.ohw;
-    for (int k = 0; k < 32 && jc + k < p.rows_b; ++k) {
+    for (int k = 0; k < n && jc + k < p.rows_b; ++k) {
       const float bv = bias ? to_f32(bias[jc + k]) : 0.f;
       out[(img * p.rows_b + jc + k) * p.ohw + pix] = from_f32<T>(v[k] + bv);
     }
@@ -126,8 +131,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int tile = blockIdx.x, split = blockIdx.y;
   int ti, tj;
   tile_coords(tile, p.tiles_i, p.tiles_j, ti, tj);
-  const int kb0 = split * p.kpb;
-  const int nkb = min(kb0 + p.kpb, p.kblocks) - kb0;
+  // K blocks are spread evenly over the splits (the plan keeps >= 1 per split).
+  const int kb0 = static_cast<int>(static_cast<int64_t>(split) * p.kblocks / p.splits);
+  const int nkb = static_cast<int>(static_cast<int64_t>(split + 1) * p.kblocks / p.splits) - kb0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -136,7 +142,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     mbar_init(acc_full, 1);
     flags[0] = 0;
-    flags[1] = 0;
     mbar_fence_init();
   }
   if (warp == 0 && lane == 0) {
@@ -154,17 +159,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
+      // Weight tiles of the first stages do not depend on the previous kernel:
+      // stream them while that kernel finishes, then wait for its outputs.
+      const int pre = (p.const_a || p.const_b) ? min(STAGES, nkb) : 0;
+      for (int it = 0; it < pre; ++it) {
+        uint8_t* sa = smem + it * L::kStageBytes;
+        mbar_arrive_expect_tx(&full[it], L::kStageBytes);
+        if (p.const_a) tma_load_2d(sa, &tmap_a, (kb0 + it) * kBK, ti * kBM, &full[it]);
+        else tma_load_2d(sa + L::kABytes, &tmap_b, (kb0 + it) * kBK, tj * BN, &full[it]);
+      }
+      pdl_wait();
+      pdl_trigger();
+      int issued = pre;
       for (int it = 0; it < nkb; ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
+        uint8_t* sa = smem + s * L::kStageBytes;
+        if (it < pre) {  // stage armed above: add the dependent operand
+          if (p.const_a) tma_load_2d(sa + L::kABytes, &tmap_b, (kb0 + it) * kBK, tj * BN, &full[s]);
+          else tma_load_2d(sa, &tmap_a, (kb0 + it) * kBK, ti * kBM, &full[s]);
+          continue;
+        }
         if (!mbar_wait(&empty[s], ph ^ 1)) {
           set_device_error(p.err, kDevErrGemmTimeout);
           flags[0] = 1;
           break;
         }
         if (flags[0]) break;
-        uint8_t* sa = smem + s * L::kStageBytes;
         mbar_arrive_expect_tx(&full[s], L::kStageBytes);
         tma_load_2d(sa, &tmap_a, (kb0 + it) * kBK, ti * kBM, &full[s]);
         tma_load_2d(sa + L::kABytes, &tmap_b, (kb0 + it) * kBK, tj * BN, &full[s]);
@@ -218,11 +239,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         float v[32];
 #pragma unroll
         for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
-        if (j0 + c < p.rows_b) store_chunk<T>(p, gi, j0 + c, v);
+        if (j0 + c < p.rows_b) store_vals<T>(p, gi, j0 + c, v, 32);
       }
-    } else if (!aborted) {
-      const int ntiles = p.tiles_i * p.tiles_j;
-      float* mine = p.partials + ((static_cast<size_t>(split) * ntiles + tile) * kBM + row) * BN;
+    } else if (p.splits > 1) {
+      // Split-K: stage this CTA's fp32 partial tile in its own shared memory
+      // (the operand ring is idle: every load was consumed before acc_full).
+      float* red = reinterpret_cast<float*>(smem);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
@@ -230,46 +252,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tmem_ld_wait();
 #pragma unroll
         for (int k = 0; k < 32; k += 4)
-          __stcg(reinterpret_cast<float4*>(mine + c + k),
-                 make_float4(__uint_as_float(r[k]), __uint_as_float(r[k + 1]),
-                             __uint_as_float(r[k + 2]), __uint_as_float(r[k + 3])));
-      }
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (threadIdx.x == 64) {
-        const unsigned prev = atomicAdd(&p.counters[tile], 1u);
-        flags[1] = (prev == static_cast<unsigned>(p.splits - 1)) ? 1 : 0;
-      }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (flags[1]) {
-        // Sum every split's partial (this CTA's included) in split order so the
-        // result does not depend on which CTA arrived last.
-        __threadfence();
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          float v[32];
-#pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = 0.f;
-          for (int s = 0; s < p.splits; ++s) {
-            const float* other =
-                p.partials + ((static_cast<size_t>(s) * ntiles + tile) * kBM + row) * BN + c;
-#pragma unroll
-            for (int k = 0; k < 32; k += 4) {
-              const float4 o = __ldcg(reinterpret_cast<const float4*>(other + k));
-              v[k] += o.x;
-              v[k + 1] += o.y;
-              v[k + 2] += o.z;
-              v[k + 3] += o.w;
-            }
-          }
-          if (j0 + c < p.rows_b) store_chunk<T>(p, gi, j0 + c, v);
-        }
-        if (threadIdx.x == 64) p.counters[tile] = 0;  // ticket ready for the next launch
+          *reinterpret_cast<float4*>(red + row * (BN + 4) + c + k) =
+              make_float4(aborted ? 0.f : __uint_as_float(r[k]), aborted ? 0.f : __uint_as_float(r[k + 1]),
+                          aborted ? 0.f : __uint_as_float(r[k + 2]), aborted ? 0.f : __uint_as_float(r[k + 3]));
       }
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (p.splits > 1) {
+    // The K-splits of this tile form one thread-block cluster (ranks 0..S-1 along
+    // y). After the cluster barrier every partial is visible through distributed
+    // shared memory; CTA `split` sums rows [split*R, (split+1)*R) of all S
+    // partials in rank order (deterministic) and writes them. The second barrier
+    // keeps every CTA's shared memory alive until all ranks finished reading.
+    cluster_sync();
+    const int S = p.splits;
+    const int R = kBM / S;
+    const int quads = R * (BN / 4);
+    const uint32_t red_local = smem_u32(smem);
+    for (int q = threadIdx.x; q < quads; q += kGemmThreads) {
+      const int rr = split * R + q % R;  // consecutive threads: consecutive rows
+      const int cq = (q / R) * 4;
+      const uint32_t off = static_cast<uint32_t>((rr * (BN + 4) + cq) * 4);
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int s = 0; s < S; ++s) {
+        const float4 o = ld_dsmem_f4(mapa_shared(red_local + off, s));
+        v[0] += o.x;
+        v[1] += o.y;
+        v[2] += o.z;
+        v[3] += o.w;
+      }
+      const int64_t gi = static_cast<int64_t>(ti) * kBM + rr;
+      if (tj * BN + cq < p.rows_b) store_vals<T>(p, gi, tj * BN + cq, v, 4);
+    }
+    cluster_sync();
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -285,6 +303,7 @@ template <typename T, bool kBKMajor>
 __global__ void __launch_bounds__(256)
     gemm_simt_kernel(const T* __restrict__ a, const T* __restrict__ b, const T* __restrict__ bias,
                      T* __restrict__ out, int64_t m, int64_t n, int64_t k) {
+  DLI_PDL_ENTRY();
   __shared__ float as[kSimtK][kSimtTile + 4];
   __shared__ float bs[kSimtK][kSimtTile + 4];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -369,7 +388,16 @@ dli_status make_kmajor_map(CUtensorMap* map, const void* base, int64_t rows, int
   return DLI_OK;
 }
 
-int stages_for(int bn) { return bn >= 256 ? 4 : (bn >= 128 ? 6 : 8); }
+// Pipeline depth per tile width. Narrow (decode, swap-AB) tiles keep two CTAs
+// resident per SM (<= ~113 KB shared memory each) so one CTA's prologue and
+// split-K epilogue overlap the other's weight streaming.
+int stages_for(int bn) { return bn >= 256 ? 4 : (bn >= 128 ? 6 : (bn >= 64 ? 4 : 5)); }
+// DLI_SM100_GEMM_NARROW_DEEP=1 selects one CTA per SM with 8 stages instead.
+bool narrow_deep() {
+  static const bool deep = tuning_knob("GEMM_NARROW_DEEP", 0) != 0;
+  return deep;
+}
+int ctas_per_sm(int bn) { return bn <= 64 && !narrow_deep() ? 2 : 1; }
 
 template <typename T, int BN, int STAGES>
 dli_status launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p, int splits,
@@ -379,16 +407,19 @@ dli_status launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcParam
   const dli_status st = ensure_smem(reinterpret_cast<const void*>(kernel), L::kBytes, "tcgen05 gemm");
   if (st != DLI_OK) return st;
   dim3 grid(static_cast<unsigned>(p.tiles_i * p.tiles_j), static_cast<unsigned>(splits));
-  kernel<<<grid, kGemmThreads, L::kBytes, stream>>>(ma, mb, p);
+  launch_pdl_cluster(kernel, grid, dim3(kGemmThreads), L::kBytes, stream,
+                     static_cast<unsigned>(splits), ma, mb, p);
   return check_launch("tcgen05 gemm");
 }
 
 template <typename T>
-dli_status launch_tc_bn(int bn, const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p,
-                        int splits, cudaStream_t stream) {
+dli_status launch_tc_bn(int bn, int stages, const CUtensorMap& ma, const CUtensorMap& mb,
+                        const TcParams& p, int splits, cudaStream_t stream) {
   switch (bn) {
-    case 32: return launch_tc<T, 32, 8>(ma, mb, p, splits, stream);
-    case 64: return launch_tc<T, 64, 8>(ma, mb, p, splits, stream);
+    case 32: return stages == 8 ? launch_tc<T, 32, 8>(ma, mb, p, splits, stream)
+                                : launch_tc<T, 32, 5>(ma, mb, p, splits, stream);
+    case 64: return stages == 8 ? launch_tc<T, 64, 8>(ma, mb, p, splits, stream)
+                                : launch_tc<T, 64, 4>(ma, mb, p, splits, stream);
     case 128: return launch_tc<T, 128, 6>(ma, mb, p, splits, stream);
     case 256: return launch_tc<T, 256, 4>(ma, mb, p, splits, stream);
   }
@@ -413,21 +444,24 @@ GemmPlan plan_tn_gemm(int64_t rows_a, int64_t rows_b, int64_t k, dli_dtype dtype
   plan.tiles_j = static_cast<int>(ceil_div(rows_b, plan.bn));
   plan.kblocks = static_cast<int>(ceil_div(k, kBK));
   plan.splits = 1;
-  plan.kblocks_per_split = plan.kblocks;
   const int64_t tiles = static_cast<int64_t>(plan.tiles_i) * plan.tiles_j;
-  const int sms = sm_count();
-  if (allow_split && tiles < sms && plan.kblocks >= 4) {
-    int splits = static_cast<int>(std::min<int64_t>(sms / tiles, plan.kblocks / 2));
-    splits = std::max(splits, 1);
-    if (splits > 1) {
-      plan.kblocks_per_split = static_cast<int>(ceil_div(plan.kblocks, splits));
-      plan.splits = static_cast<int>(ceil_div(plan.kblocks, plan.kblocks_per_split));
+  if (plan.bn <= 64 && narrow_deep()) plan.stages = 8;
+  static const int kSplitSlots = tuning_knob("GEMM_SPLIT_SLOTS", 0);  // CTAs per SM to fill
+  const int per_sm = plan.stages == 8 ? 1 : ctas_per_sm(plan.bn);
+  const int slots = sm_count() * (kSplitSlots > 0 ? kSplitSlots : per_sm);
+  // When the tiles alone cannot fill the SMs, split K over a thread-block cluster
+  // of S in {8, 4, 2} CTAs per tile (reduced through distributed shared memory,
+  // so splits cost no global traffic); each split keeps >= 2 K blocks.
+  if (allow_split && tiles < slots) {
+    for (const int s : {8, 4, 2}) {
+      if (tiles * s <= slots && plan.kblocks >= 2 * s) {
+        plan.splits = s;
+        break;
+      }
     }
+    if (plan.splits == 1 && plan.kblocks >= 4) plan.splits = 2;
   }
-  if (plan.splits > 1) {
-    const size_t counters = ((tiles * sizeof(unsigned)) + 255) / 256 * 256;
-    plan.workspace = counters + static_cast<size_t>(plan.splits) * tiles * kBM * plan.bn * sizeof(float);
-  }
+  plan.workspace = 0;
   return plan;
 }
 
@@ -435,13 +469,13 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
                                int64_t rows_a, int64_t rows_b, int64_t k, int64_t lda,
                                int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,
                                dli_dtype dtype, const GemmPlan& plan, void* workspace,
-                               size_t workspace_bytes, cudaStream_t stream) {
+                               size_t workspace_bytes, cudaStream_t stream, bool const_a,
+                               bool const_b) {
   if (!plan.tcgen05) return fail(DLI_ERR_UNSUPPORTED, "gemm: shape not served by tcgen05");
   if (!aligned(a, 16) || !aligned(b, 16) || lda % 8 != 0 || ldb % 8 != 0)
     return fail(DLI_ERR_UNSUPPORTED, "gemm: TMA needs 16-byte aligned operands and row strides");
-  if (plan.splits > 1 && (workspace == nullptr || workspace_bytes < plan.workspace))
-    return fail(DLI_ERR_WORKSPACE, "gemm: split-K workspace too small (need " +
-                                       std::to_string(plan.workspace) + " bytes)");
+  (void)workspace;
+  (void)workspace_bytes;
   const bool bf16 = dtype == DLI_DTYPE_BF16;
   CUtensorMap ma, mb;
   dli_status st = make_kmajor_map(&ma, a, rows_a, k, lda, kBM, bf16);
@@ -454,7 +488,6 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
   p.tiles_i = plan.tiles_i;
   p.tiles_j = plan.tiles_j;
   p.kblocks = plan.kblocks;
-  p.kpb = plan.kblocks_per_split;
   p.splits = plan.splits;
   p.epilogue = epilogue;
   p.ldo = ldo;
@@ -463,16 +496,10 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
   p.bias = bias;
   p.out = out;
   p.err = device_error_word();
-  if (plan.splits > 1) {
-    const int64_t tiles = static_cast<int64_t>(plan.tiles_i) * plan.tiles_j;
-    const size_t counters = ((tiles * sizeof(unsigned)) + 255) / 256 * 256;
-    p.counters = static_cast<unsigned*>(workspace);
-    p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
-    const cudaError_t e = cudaMemsetAsync(workspace, 0, tiles * sizeof(unsigned), stream);
-    if (e != cudaSuccess) return fail(DLI_ERR_CUDA, std::string("gemm ticket reset: ") + cudaGetErrorString(e));
-  }
-  if (bf16) return launch_tc_bn<__nv_bfloat16>(plan.bn, ma, mb, p, plan.splits, stream);
-  return launch_tc_bn<__half>(plan.bn, ma, mb, p, plan.splits, stream);
+  p.const_a = const_a ? 1 : 0;
+  p.const_b = const_b ? 1 : 0;
+  if (bf16) return launch_tc_bn<__nv_bfloat16>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
+  return launch_tc_bn<__half>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
 }
 
 dli_status run_gemm_simt(const void* a, const void* b, const void* bias, void* out, int64_t m,
@@ -483,11 +510,11 @@ dli_status run_gemm_simt(const void* a, const void* b, const void* bias, void* o
   dli_status st = dispatch_float(dtype, "gemm", [&](auto tag) {
     using T = decltype(tag);
     if (b_kmajor)
-      gemm_simt_kernel<T, true><<<grid, 256, 0, stream>>>((const T*)a, (const T*)b, (const T*)bias,
-                                                          (T*)out, m, n, k);
+      launch_pdl(gemm_simt_kernel<T, true>, grid, dim3(256), 0, stream, (const T*)a, (const T*)b,
+                 (const T*)bias, (T*)out, m, n, k);
     else
-      gemm_simt_kernel<T, false><<<grid, 256, 0, stream>>>((const T*)a, (const T*)b, (const T*)bias,
-                                                           (T*)out, m, n, k);
+      launch_pdl(gemm_simt_kernel<T, false>, grid, dim3(256), 0, stream, (const T*)a, (const T*)b,
+                 (const T*)bias, (T*)out, m, n, k);
   });
   if (st != DLI_OK) return st;
   return check_launch("simt gemm");
@@ -522,9 +549,9 @@ extern "C" dli_status dli_sm100_linear(const void* x, const void* w, const void*
   if (plan.tcgen05 && tma_ok) {
     if (swap)
       return run_tn_gemm_tcgen05(w, x, bias, y, n, m, k, k, k, n, kEpiTransposed, 0, dtype, plan,
-                                 workspace, workspace_bytes, as_stream(stream));
+                                 workspace, workspace_bytes, as_stream(stream), true, false);
     return run_tn_gemm_tcgen05(x, w, bias, y, m, n, k, k, k, n, kEpiRowMajor, 0, dtype, plan,
-                               workspace, workspace_bytes, as_stream(stream));
+                               workspace, workspace_bytes, as_stream(stream), false, true);
   }
   return run_gemm_simt(x, w, bias, y, m, n, k, true, dtype, as_stream(stream));
 }

@@ -21,6 +21,7 @@ __global__ void rms_norm_kernel(const T* x /* may alias residual_out */,
                                 const T* __restrict__ delta, const T* __restrict__ w,
                                 T* __restrict__ out, T* residual_out, int64_t rows, int64_t hidden,
                                 float eps, bool vec) {
+  DLI_PDL_ENTRY();
   __shared__ float scratch[32];
   constexpr int V = Vec16<T>::N;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -90,8 +91,8 @@ dli_status launch(const void* x, const void* delta, const void* w, void* out, vo
     if (kFused) vec = vec && aligned(delta, 16) && aligned(residual_out, 16);
     const int64_t lanes = vec ? hidden / V : hidden;
     const int threads = lanes >= 512 ? 512 : (lanes >= 256 ? 256 : (lanes >= 128 ? 128 : 32));
-    rms_norm_kernel<T, kFused><<<grid, threads, 0, as_stream(stream)>>>(
-        (const T*)x, (const T*)delta, (const T*)w, (T*)out, (T*)residual_out, rows, hidden, eps, vec);
+    launch_pdl(rms_norm_kernel<T, kFused>, grid, threads, 0, as_stream(stream), (const T*)x,
+               (const T*)delta, (const T*)w, (T*)out, (T*)residual_out, rows, hidden, eps, vec);
   });
   if (st != DLI_OK) return st;
   return check_launch(name);

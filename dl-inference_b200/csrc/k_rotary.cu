@@ -56,6 +56,7 @@ __global__ void rotary_kernel(const T* __restrict__ q, const T* __restrict__ k,
                               int64_t table_rows, int64_t start_pos,
                               const int64_t* __restrict__ positions, int64_t positions_numel,
                               unsigned* err) {
+  DLI_PDL_ENTRY();
   const int64_t q_pairs = batch * hq * seq * half_d;
   const int64_t total = q_pairs + batch * hk * seq * half_d;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -94,6 +95,7 @@ __global__ void qkv_rotary_cache_kernel(const T* __restrict__ qkv, const float* 
                                         T* __restrict__ cache_v, int64_t batch, int64_t seq,
                                         int64_t hq, int64_t hkv, int64_t half_d, int64_t pairs,
                                         int64_t table_rows, int64_t cap, unsigned* err) {
+  DLI_PDL_ENTRY();
   const int64_t heads = hq + 2 * hkv;
   const int64_t total = batch * seq * heads * half_d;
   const int64_t d = 2 * half_d;
@@ -152,9 +154,9 @@ extern "C" dli_status dli_sm100_rotary_embedding(const void* q, const void* k, c
   unsigned* err = device_error_word();
   dli_status st = dispatch_float(dtype, "rotary_embedding", [&](auto tag) {
     using T = decltype(tag);
-    rotary_kernel<T><<<grid_for(total), 256, 0, as_stream(stream)>>>(
-        (const T*)q, (const T*)k, cos_table, sin_table, (T*)out_q, (T*)out_k, batch, q_heads,
-        k_heads, seq, head_dim / 2, pairs, table_rows, start_pos, positions, positions_numel, err);
+    launch_pdl(rotary_kernel<T>, grid_for(total), 256, 0, as_stream(stream), (const T*)q,
+               (const T*)k, cos_table, sin_table, (T*)out_q, (T*)out_k, batch, q_heads, k_heads, seq,
+               head_dim / 2, pairs, table_rows, start_pos, positions, positions_numel, err);
   });
   if (st != DLI_OK) return st;
   return check_launch("rotary_embedding");
@@ -178,9 +180,9 @@ extern "C" dli_status dli_sm100_qkv_rotary_cache(const void* qkv, const float* c
   unsigned* err = device_error_word();
   dli_status st = dispatch_float(dtype, "qkv_rotary_cache", [&](auto tag) {
     using T = decltype(tag);
-    qkv_rotary_cache_kernel<T><<<grid_for(total), 256, 0, as_stream(stream)>>>(
-        (const T*)qkv, cos_table, sin_table, positions, (T*)q_out, (T*)cache_k, (T*)cache_v, batch,
-        seq, q_heads, kv_heads, head_dim / 2, pairs, table_rows, capacity, err);
+    launch_pdl(qkv_rotary_cache_kernel<T>, grid_for(total), 256, 0, as_stream(stream),
+               (const T*)qkv, cos_table, sin_table, positions, (T*)q_out, (T*)cache_k, (T*)cache_v,
+               batch, seq, q_heads, kv_heads, head_dim / 2, pairs, table_rows, capacity, err);
   });
   if (st != DLI_OK) return st;
   return check_launch("qkv_rotary_cache");

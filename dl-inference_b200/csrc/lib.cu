@@ -1,6 +1,7 @@
 // Library-wide state of libdli_sm100.so: last-error text, device error word,
 // device properties.
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <string>
@@ -76,6 +77,13 @@ dli_status ensure_smem(const void* kernel, int bytes, const char* what) {
     return fail(DLI_ERR_CUDA, std::string(what) + " shared-memory attribute: " + cudaGetErrorString(e));
   done.insert({dev, kernel});
   return DLI_OK;
+}
+
+int tuning_knob(const char* name, int fallback) {
+  const std::string var = std::string("DLI_SM100_") + name;
+  const char* v = std::getenv(var.c_str());
+  if (v == nullptr || *v == '\0') return fallback;
+  return std::atoi(v);
 }
 
 int sm_count() {

@@ -128,6 +128,31 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ---- thread-block clusters -----------------------------------------------------
+// Full cluster barrier: every thread of every CTA of the cluster arrives
+// (release) and waits (acquire), so shared memory written before it is visible
+// to the other CTAs through distributed shared memory after it.
+__device__ __forceinline__ void cluster_sync() {
+  __syncwarp();
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Maps a shared::cta address of this CTA to the same offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
+}
+
 // Shared-memory matrix descriptor for a K-major operand tile stored with the
 // 128-byte swizzle (rows of 128 B, 8-row groups 1024 B apart): start address,
 // leading-byte offset (unused for swizzled K-major; 16 B), stride-byte offset

@@ -90,7 +90,13 @@ void reg(dli::OperatorRegistry* r, const char* name) {
 // ---------------------------------------------------------------------------
 
 // linear: y = x . W^T (+ b); python/dli_ops/aot/linear/template.cc:14-34.
+// Split-K plans need a zero-initialised workspace that the kernel leaves zeroed;
+// the operator (one instance per graph node in the engine's plan) keeps one
+// such buffer and grows it when a larger plan needs more, so a decode step
+// replayed from a CUDA graph allocates nothing.
 class LinearOp final : public dli::Operator {
+  mutable at::Tensor ws_;
+
  public:
   std::string type() const override { return "linear"; }
   void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
@@ -108,9 +114,13 @@ class LinearOp final : public dli::Operator {
     shape.back() = n;
     *out[0] = Tensor::cuda(x.dtype(), shape, x.deviceId());
     const dli_dtype dt = cdt(x.dtype());
-    at::Tensor ws = workspace(dli_sm100_linear_workspace_size(m, n, k, dt), x.deviceId());
+    const std::size_t need = dli_sm100_linear_workspace_size(m, n, k, dt);
+    if (need > wsBytes(ws_) || (ws_.defined() && ws_.device().index() != x.deviceId()))
+      ws_ = at::zeros({static_cast<std::int64_t>(need)},
+                      at::TensorOptions().dtype(at::kByte).device(at::kCUDA, x.deviceId()));
     check(dli_sm100_linear(dli::ptr(x), dli::ptr(w), in.size() == 3 ? dli::ptr(*in[2]) : nullptr,
-                           out[0]->deviceData(), m, n, k, dt, wsPtr(ws), wsBytes(ws), ctx.cuda_stream),
+                           out[0]->deviceData(), m, n, k, dt, need ? wsPtr(ws_) : nullptr,
+                           need ? wsBytes(ws_) : 0, ctx.cuda_stream),
           type());
   }
 };

@@ -147,7 +147,8 @@ def linear(x, w, bias=None, out=None):
     out = out if out is not None else torch.empty(*x.shape[:-1], n, dtype=x.dtype, device=x.device)
     L = lib()
     ws_bytes = L.dli_sm100_linear_workspace_size(m, n, k, _dt(x))
-    ws = _workspace(ws_bytes, x.device)
+    # split-K tickets must be zero on entry (the kernel leaves them zero)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
     check(L.dli_sm100_linear(_ptr(x), _ptr(w), _ptr(bias), _ptr(out), m, n, k, _dt(x), _ptr(ws),
                              ws_bytes, _stream()), "linear")
     return out

@@ -67,7 +67,12 @@ dli_status dli_sm100_check_device_error(void* stream);
  * its launcher python/dli_ops/aot/linear/template.cc:14-34 (M = product of the
  * leading dims of x, template.cc:23). BF16/F16 run on tcgen05 tensor cores
  * (TMA-fed, TMEM accumulators, fp32 accumulate); F32 runs an exact-fp32 FFMA
- * kernel (the reference's tl.dot runs fp32 as TF32). */
+ * kernel (the reference's tl.dot runs fp32 as TF32).
+ * Decode-sized problems (few rows) stream the weight matrix once with the
+ * weights on the MMA M side; when the tiles cannot fill the GPU, K is split over
+ * a thread-block cluster and reduced through distributed shared memory, so this
+ * build needs no workspace (linear_workspace_size() returns 0; the workspace
+ * arguments are kept for callers written against a build that uses one). */
 size_t dli_sm100_linear_workspace_size(int64_t m, int64_t n, int64_t k, dli_dtype dtype);
 dli_status dli_sm100_linear(const void* x, const void* w, const void* bias, void* y, int64_t m,
                             int64_t n, int64_t k, dli_dtype dtype, void* workspace,
