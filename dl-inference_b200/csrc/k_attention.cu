@@ -23,6 +23,7 @@
 //    graphs (the reference dtype) and head dims the MMA kernels do not cover.
 #include <algorithm>
 #include <cfloat>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -840,4 +841,71 @@ extern "C" dli_status dli_sm100_attention_kvcache(const void* q, const void* cac
   args.scale_log2 = sc * kLog2e;
   args.causal = 1;
   return run_attention(args, dtype, capacity, workspace, workspace_bytes, as_stream(stream));
+}
+
+// ---- attention over a KV cache without any allocation --------------------------------
+// Some callers cannot allocate device memory at all: code running inside a
+// memory budget fixed up front (a serving loop that must not grow its
+// footprint), hosts whose allocator is owned by another runtime, or callers that
+// must not take the allocator's locks on their hot path. For them this variant
+// takes the split-KV partials (the only scratch the decode path needs) from a
+// file-scope device array of fixed size instead of a caller workspace.
+namespace dli_sm100 {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB, held by every GPU that loads the library
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+// Device address of g_noalloc_scratch on the current device. In host code the
+// array's name is only a stand-in for the symbol, so the address is resolved
+// once per device with that device current (cudaGetSymbolAddress) and cached.
+dli_status noalloc_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return fail(DLI_ERR_CUDA, std::string("no-alloc scratch: ") + cudaGetErrorString(err));
+  if (dev < 0 || dev >= 64) return fail(DLI_ERR_UNSUPPORTED, "no-alloc scratch: device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess || p == nullptr)
+      return fail(DLI_ERR_CUDA, std::string("no-alloc scratch address: ") + cudaGetErrorString(err));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return DLI_OK;
+}
+
+}  // namespace
+}  // namespace dli_sm100
+
+extern "C" size_t dli_sm100_attention_kvcache_noalloc_max_scratch(void) { return kNoAllocScratchBytes; }
+
+extern "C" dli_status dli_sm100_attention_kvcache_noalloc(const void* q, const void* cache_k,
+                                                          const void* cache_v, const int64_t* positions,
+                                                          void* out, int64_t batch, int64_t seq,
+                                                          int64_t q_heads, int64_t kv_heads,
+                                                          int64_t capacity, int64_t head_dim, float scale,
+                                                          dli_dtype dtype, void* stream) {
+  if (batch < 0 || seq < 0 || q_heads <= 0 || kv_heads <= 0 || capacity <= 0 || head_dim <= 0)
+    return fail(DLI_ERR_INVALID_ARGUMENT, "attention_kvcache_noalloc: bad sizes");
+  if (q_heads % kv_heads != 0)
+    return fail(DLI_ERR_INVALID_ARGUMENT, "attention_kvcache_noalloc: q heads must be a multiple of kv heads");
+  const size_t need = attention_ws(batch, q_heads, kv_heads, seq, capacity, head_dim, dtype);
+  if (need > kNoAllocScratchBytes)
+    return fail(DLI_ERR_WORKSPACE, "attention_kvcache_noalloc: this shape needs " + std::to_string(need) +
+                                       " bytes of scratch, more than the fixed " +
+                                       std::to_string(kNoAllocScratchBytes) +
+                                       "; use dli_sm100_attention_kvcache with a caller workspace");
+  void* scratch = nullptr;
+  if (need > 0) {
+    const dli_status st = noalloc_scratch(&scratch);
+    if (st != DLI_OK) return st;
+  }
+  // The partials need no initial value: every split slot the merge reads is written
+  // by the same call first, so leftover contents of an earlier call are harmless.
+  return dli_sm100_attention_kvcache(q, cache_k, cache_v, positions, out, batch, seq, q_heads, kv_heads,
+                                     capacity, head_dim, scale, dtype, scratch, need, stream);
 }

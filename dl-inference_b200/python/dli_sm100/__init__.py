@@ -54,6 +54,8 @@ SIGNATURES = {
     "dli_sm100_qkv_rotary_cache": (N, [P, P, P, P, P, P, P] + [I] * 8 + [D, P]),
     "dli_sm100_attention_kvcache_workspace_size": (Z, [I] * 6 + [D]),
     "dli_sm100_attention_kvcache": (N, [P, P, P, P, P] + [I] * 6 + [F, D, P, Z, P]),
+    "dli_sm100_attention_kvcache_noalloc_max_scratch": (Z, []),
+    "dli_sm100_attention_kvcache_noalloc": (N, [P, P, P, P, P] + [I] * 6 + [F, D, P]),
     "dli_sm100_add": (N, [P, P, P, I, I, D, P]),
     "dli_sm100_mul": (N, [P, P, P, I, I, D, P]),
     "dli_sm100_silu": (N, [P, P, I, D, P]),

@@ -190,6 +190,26 @@ dli_status dli_sm100_attention_kvcache(const void* q, const void* cache_k, const
                                        dli_dtype dtype, void* workspace, size_t workspace_bytes,
                                        void* stream);
 
+/* Same as dli_sm100_attention_kvcache, for callers that cannot allocate device
+ * memory (a fixed memory budget set up front, an allocator owned by another
+ * runtime, or a hot path that must not take allocator locks). No counterpart in
+ * the reference: it is an additive entry point of this library. The split-KV
+ * scratch comes from one fixed device array inside the library, sized
+ * dli_sm100_attention_kvcache_noalloc_max_scratch() bytes (4 MiB) and held by
+ * every GPU that loads the library until the process exits; shapes needing more
+ * fail with DLI_ERR_WORKSPACE. The first call on a device resolves the array's
+ * device address (cudaGetSymbolAddress) with that device current, so make that
+ * first call before any stream capture. Every call shares the one array, so calls
+ * that overlap on the GPU (other streams, other threads) race; serialize them.
+ * Nothing in it has to start at zero. The call allocates nothing. */
+size_t dli_sm100_attention_kvcache_noalloc_max_scratch(void);
+dli_status dli_sm100_attention_kvcache_noalloc(const void* q, const void* cache_k,
+                                               const void* cache_v, const int64_t* positions,
+                                               void* out, int64_t batch, int64_t seq,
+                                               int64_t q_heads, int64_t kv_heads, int64_t capacity,
+                                               int64_t head_dim, float scale, dli_dtype dtype,
+                                               void* stream);
+
 /* ---- elementwise / data movement -------------------------------------- */
 
 /* out[i] = a[i] + b[i mod width] (python/dli_ops/aot/add/kernel.py:5-11). */
