@@ -387,7 +387,9 @@ def main() -> int:
     gemm_bytes = (n_gu * k_gu + b_local * (n_gu + k_gu)) * 2
     achieved = gemm_bytes / (gemm_ms / 1e3) / 1e9
     traffic = None
-    prof = ROOT / "profiles" / "traffic.json"
+    # DRAM bytes (read + write) of one launch of this kernel from an ncu capture,
+    # recorded by hand in profiles/traffic.txt (JSON text) from the committed summary
+    prof = ROOT / "profiles" / "traffic.txt"
     if prof.exists():
         traffic = json.loads(prof.read_text()).get(f"decode_gate_up_{args.model}_tp{tp}_b{b_local}")
     # prefill: gate/up GEMM at M = b_local * prompt (capped for memory)
