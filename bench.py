@@ -224,8 +224,8 @@ def main() -> int:
     import torch
     import torch.distributed as dist
 
-    import dli
     import dli_sm100
+    from dli.parallel import TensorParallelComm, parallel_layout
     from dli.qwen2 import Qwen2Runner
     from dli_export import qwen2 as Q
 
@@ -240,38 +240,18 @@ def main() -> int:
     batch = args.batch or batch
     prompt = args.prompt or prompt
     dsteps = args.decode or dsteps
-    tp = 1
-    while tp * 2 <= min(world, max_tp) and world % (tp * 2) == 0:
-        tp *= 2
-    dp = world // tp
-    group, tp_rank = rank // tp, rank % tp
-    if batch % dp:
-        raise SystemExit(f"batch {batch} not divisible by {dp} data-parallel groups")
-    b_local = batch // dp
+    lay = parallel_layout(world, rank, max_tp, shape)
+    tp, dp, group, tp_rank = lay.tp, lay.dp, lay.group, lay.tp_rank
+    try:
+        b_local = lay.local_batch(batch)
+    except ValueError as exc:
+        raise SystemExit(str(exc))
     capacity = (prompt + dsteps + 63) // 64 * 64
 
     # --- communicator: one NCCL comm per tensor-parallel group, built by the plugin
-    comm = 0
-    plugin = dli_sm100.lib()  # noqa: F841  (kernel library loaded before the plugin)
-    if tp > 1:
-        import ctypes
-
-        P = ctypes.CDLL(dli.PLUGIN_PATH)
-        P.dli_sm100_nccl_comm_init.restype = ctypes.c_void_p
-        P.dli_sm100_nccl_comm_init.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
-        ids = [None] * dp
-        if rank == 0:
-            for g in range(dp):
-                buf = ctypes.create_string_buffer(256)
-                n = P.dli_sm100_nccl_unique_id(buf, 256)
-                if n <= 0:
-                    raise SystemExit("plugin built without NCCL")
-                ids[g] = buf.raw[:n]
-        dist.broadcast_object_list(ids, src=0)
-        idb = ctypes.create_string_buffer(ids[group], len(ids[group]))
-        comm = P.dli_sm100_nccl_comm_init(idb, tp, tp_rank, local)
-        if not comm:
-            raise SystemExit("ncclCommInitRank failed")
+    dli_sm100.lib()  # kernel library loaded before the plugin
+    tpc = TensorParallelComm(lay, local)
+    comm = tpc.handle
 
     # --- weights: random N(0, 0.02), generated on the device layer by layer, sharded
     weights = {}
@@ -449,7 +429,12 @@ def main() -> int:
             "launches_per_decode_step": launches_decode,
         }
         print(json.dumps(line))
+    # graphs holding NCCL launches go before the communicator, which goes before the process group
+    del g_, ids_buf, pos_buf, next_buf
+    runner.release_graphs()
     del runner
+    torch.cuda.synchronize()
+    tpc.destroy()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -70,6 +70,13 @@ class Qwen2Runner:
     def decode_graph(self, batch: int):
         return self._graphs.get(batch) or self._capture(batch)
 
+    def release_graphs(self) -> None:
+        """Drops the captured decode graphs. A graph captured with tensor
+        parallelism holds NCCL launches on the runner's communicator: release it
+        before that communicator (or the process group) is destroyed."""
+        torch.cuda.synchronize(self.device)
+        self._graphs.clear()
+
     def prefill(self, prompt: torch.Tensor, start: torch.Tensor | None = None):
         """prompt [B,S] on the device; returns (logits of the last token, next ids)."""
         b = prompt.shape[0]

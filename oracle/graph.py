@@ -15,9 +15,12 @@ from . import ops as O
 
 
 class GraphOracle:
-    def __init__(self, graph: dict, constants: dict[str, np.ndarray]):
+    def __init__(self, graph: dict, constants: dict[str, np.ndarray], all_reduce=None):
+        """all_reduce: callable summing an array over the ranks of a tensor-parallel
+        group (for instance a torch.distributed gloo all_reduce); None = one rank."""
         self.graph = graph
         self.constants = constants
+        self.all_reduce = all_reduce
         self.cache: dict[str, dict[str, np.ndarray]] = {}
 
     def run(self, inputs: dict[str, np.ndarray]) -> dict[str, np.ndarray]:
@@ -48,7 +51,7 @@ class GraphOracle:
         if op == "argmax":
             return [O.argmax(x[0])]
         if op == "all_reduce":
-            return [x[0]]
+            return [x[0] if self.all_reduce is None else self.all_reduce(np.asarray(x[0]))]
         if op == "qkv_rotary_cache":
             return [self._qkv_rotary_cache(x, a)]
         if op == "attention_kvcache":
