@@ -250,7 +250,8 @@ def main() -> int:
 
     # --- communicator: one NCCL comm per tensor-parallel group, built by the plugin
     dli_sm100.lib()  # kernel library loaded before the plugin
-    tpc = TensorParallelComm(lay, local)
+    # NVLink exchange buffers for the fused all-reduce + add_rms_norm of decode steps
+    tpc = TensorParallelComm(lay, local, exchange=(256, shape.hidden, 2))
     comm = tpc.handle
 
     # --- weights: random N(0, 0.02), generated on the device layer by layer, sharded

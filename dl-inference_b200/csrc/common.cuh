@@ -83,6 +83,7 @@ enum DeviceError : unsigned {
   kDevErrRotaryPosition = 3,
   kDevErrAttentionTimeout = 4,
   kDevErrKvCapacity = 5,
+  kDevErrExchangeTimeout = 6,
 };
 // Device address of the error word of the current device (resolved once per
 // device with cudaGetSymbolAddress); kernels receive it as an argument.

@@ -1,0 +1,286 @@
+// Tensor-parallel all-reduce fused with the residual add and RMSNorm that
+// follow it in a Megatron block (o_proj -> all_reduce -> add_rms_norm and
+// down_proj -> all_reduce -> add_rms_norm).
+//
+// One-shot push over NVLink peer memory. Every rank owns an exchange buffer of
+// the same size, mapped into every other rank's address space (CUDA IPC):
+//
+//   flags  u32 [kMaxRanks][max_rows]      written by peers: arrival epoch of
+//                                         (source rank, row)
+//   epochs u32 [max_rows]                 local: last epoch of each row's CTA
+//   data   T   [2 slots][tp][max_rows][row_elems]
+//
+// CTA r (one per row) of rank k takes epoch e = epochs[r] + 1, stores its row of
+// the partial sum into slot e&1, source k, row r of every peer's buffer, fences
+// at system scope and release-stores e into flags[k][r] of every peer. It then
+// acquires flags[j][r] >= e for every peer j (a bounded wait), sums the tp
+// partial rows in rank order 0..tp-1 (so every rank computes bit-identical
+// results), rounds to T (the value an all_reduce would return), adds the
+// residual and applies RMSNorm exactly as dli_sm100_add_rms_norm does.
+//
+// Why two slots suffice: CTA r of rank k writes slot e&1 of a peer j only after
+// its wait at epoch e-1 saw peer j's row-r push of epoch e-1. That push happens
+// after j's kernel passed griddepcontrol.wait, i.e. after every earlier kernel
+// of j's stream, including the one that read slot e&1 at epoch e-2, completed.
+// Rows live at fixed offsets, so calls with different row counts never overlap.
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace dli_sm100 {
+namespace {
+
+constexpr int kMaxRanks = 8;
+constexpr int kVpt = 4;                    // 16-byte vectors per thread
+constexpr int64_t kHeaderAlign = 4096;
+constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;
+
+struct ExchangeParams {
+  char* buf[kMaxRanks];      // exchange buffer of each rank, as mapped in this process
+  int tp;
+  int rank0;                 // rank of blockIdx.y == 0
+  int64_t max_rows, row_elems;
+  int64_t rank_stride;       // elements between ranks' tensors when one launch runs several ranks
+  int64_t rows, hidden;
+  float eps;
+  uint64_t timeout_ns;
+  unsigned* err;
+};
+
+__host__ __device__ inline int64_t header_bytes(int64_t max_rows) {
+  const int64_t raw = (static_cast<int64_t>(kMaxRanks) + 1) * max_rows * 4;
+  return (raw + kHeaderAlign - 1) / kHeaderAlign * kHeaderAlign;
+}
+
+__device__ __forceinline__ uint64_t timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ T* row_slot(char* base, const ExchangeParams& p, int slot, int src, int64_t row) {
+  T* data = reinterpret_cast<T*>(base + header_bytes(p.max_rows));
+  return data + ((static_cast<int64_t>(slot) * p.tp + src) * p.max_rows + row) * p.row_elems;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
+    ExchangeParams p, const T* __restrict__ delta, const T* residual /* may alias residual_out */,
+    const T* __restrict__ w, T* __restrict__ normed, T* residual_out) {
+  constexpr int V = Vec16<T>::N;
+  __shared__ float scratch[32];
+  __shared__ uint32_t s_epoch;
+  pdl_wait();  // the partial comes from the previous kernel
+  pdl_trigger();
+  const int rank = p.rank0 + static_cast<int>(blockIdx.y);
+  const int64_t r = blockIdx.x;
+  const int64_t off = static_cast<int64_t>(blockIdx.y) * p.rank_stride + r * p.hidden;
+  char* mine = p.buf[rank];
+  uint32_t* flags = reinterpret_cast<uint32_t*>(mine);
+  uint32_t* epochs = flags + kMaxRanks * p.max_rows;
+  if (threadIdx.x == 0) s_epoch = epochs[r] + 1u;
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int slot = static_cast<int>(e & 1u);
+  const int64_t lanes = p.hidden / V;
+
+  // 1. own partial row into registers, pushed to every peer
+  Vec16<T> own[kVpt];
+#pragma unroll
+  for (int i = 0; i < kVpt; ++i) {
+    const int64_t c = (threadIdx.x + static_cast<int64_t>(i) * blockDim.x);
+    if (c < lanes) own[i] = load16(delta + off + c * V);
+  }
+  for (int q = 0; q < p.tp; ++q) {
+    if (q == rank) continue;
+    T* dst = row_slot<T>(p.buf[q], p, slot, rank, r);
+#pragma unroll
+    for (int i = 0; i < kVpt; ++i) {
+      const int64_t c = (threadIdx.x + static_cast<int64_t>(i) * blockDim.x);
+      if (c < lanes) store16(dst + c * V, own[i]);
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (static_cast<int>(threadIdx.x) < p.tp && static_cast<int>(threadIdx.x) != rank) {
+    uint32_t* peer_flags = reinterpret_cast<uint32_t*>(p.buf[threadIdx.x]);
+    st_release_sys(peer_flags + static_cast<int64_t>(rank) * p.max_rows + r, e);
+  }
+
+  // 2. wait for every peer's row (bounded: on timeout record the error and go on)
+  if (static_cast<int>(threadIdx.x) < p.tp && static_cast<int>(threadIdx.x) != rank) {
+    const uint32_t* f = flags + static_cast<int64_t>(threadIdx.x) * p.max_rows + r;
+    if (static_cast<int32_t>(ld_acquire_sys(f) - e) < 0) {
+      const uint64_t start = timer_ns();
+      while (static_cast<int32_t>(ld_acquire_sys(f) - e) < 0) {
+        if (timer_ns() - start > p.timeout_ns) {
+          set_device_error(p.err, kDevErrExchangeTimeout);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // 3. rank-ordered sum, residual add, RMSNorm
+  float acc[kVpt][V];
+#pragma unroll
+  for (int i = 0; i < kVpt; ++i)
+#pragma unroll
+    for (int j = 0; j < V; ++j) acc[i][j] = 0.f;
+  for (int src = 0; src < p.tp; ++src) {
+    if (src == rank) {
+#pragma unroll
+      for (int i = 0; i < kVpt; ++i)
+#pragma unroll
+        for (int j = 0; j < V; ++j) acc[i][j] += to_f32(own[i].e[j]);
+      continue;
+    }
+    const T* s = row_slot<T>(mine, p, slot, src, r);
+#pragma unroll
+    for (int i = 0; i < kVpt; ++i) {
+      const int64_t c = (threadIdx.x + static_cast<int64_t>(i) * blockDim.x);
+      if (c < lanes) {
+        Vec16<T> v;
+        *reinterpret_cast<uint4*>(&v) = __ldcg(reinterpret_cast<const uint4*>(s + c * V));
+#pragma unroll
+        for (int j = 0; j < V; ++j) acc[i][j] += to_f32(v.e[j]);
+      }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kVpt; ++i) {
+    const int64_t c = (threadIdx.x + static_cast<int64_t>(i) * blockDim.x);
+    if (c < lanes) {
+      Vec16<T> res = load16(residual + off + c * V);
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        const float sum = to_f32(from_f32<T>(acc[i][j]));  // the all-reduced value in T
+        const T h = from_f32<T>(to_f32(res.e[j]) + sum);
+        res.e[j] = h;
+        acc[i][j] = to_f32(h);
+        ss += acc[i][j] * acc[i][j];
+      }
+      store16(residual_out + off + c * V, res);
+    }
+  }
+  const float total = block_sum(ss, scratch);
+  const float inv = rsqrtf(total / static_cast<float>(p.hidden) + p.eps);
+#pragma unroll
+  for (int i = 0; i < kVpt; ++i) {
+    const int64_t c = (threadIdx.x + static_cast<int64_t>(i) * blockDim.x);
+    if (c < lanes) {
+      Vec16<T> g = load16(w + c * V), o;
+#pragma unroll
+      for (int j = 0; j < V; ++j) o.e[j] = from_f32<T>(round_through<T>(acc[i][j] * inv) * to_f32(g.e[j]));
+      store16(normed + off + c * V, o);
+    }
+  }
+  if (threadIdx.x == 0) epochs[r] = e;
+}
+
+}  // namespace
+}  // namespace dli_sm100
+
+using namespace dli_sm100;
+
+extern "C" size_t dli_sm100_tp_exchange_bytes(int tp, int64_t max_rows, int64_t row_elems, dli_dtype dtype) {
+  if (tp < 1 || tp > kMaxRanks || max_rows <= 0 || row_elems <= 0 || !is_float_dtype(dtype)) return 0;
+  return static_cast<size_t>(header_bytes(max_rows)) +
+         static_cast<size_t>(2) * tp * max_rows * row_elems * dtype_bytes(dtype);
+}
+
+extern "C" dli_status dli_sm100_tp_exchange_reset(void* buffer, int64_t max_rows, void* stream) {
+  if (buffer == nullptr || max_rows <= 0) return fail(DLI_ERR_INVALID_ARGUMENT, "tp_exchange_reset: bad arguments");
+  if (cudaMemsetAsync(buffer, 0, static_cast<size_t>(header_bytes(max_rows)), as_stream(stream)) != cudaSuccess)
+    return fail(DLI_ERR_CUDA, std::string("tp_exchange_reset: ") + cudaGetErrorString(cudaGetLastError()));
+  return ok();
+}
+
+extern "C" dli_status dli_sm100_allreduce_add_rms_norm(
+    void* const* buffers, int tp, int rank, int ranks_in_launch, int64_t max_rows, int64_t row_elems,
+    const void* delta, const void* residual, const void* w, void* normed, void* residual_out,
+    int64_t rank_stride, int64_t rows, int64_t hidden, float eps, int64_t timeout_ns, dli_dtype dtype,
+    void* stream) {
+  const char* name = "allreduce_add_rms_norm";
+  if (buffers == nullptr || tp < 1 || tp > kMaxRanks || rank < 0 || ranks_in_launch < 1 ||
+      rank + ranks_in_launch > tp || (ranks_in_launch > 1 && rank != 0))
+    return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": bad rank arguments");
+  if (rows < 0 || hidden <= 0 || max_rows <= 0 || row_elems <= 0)
+    return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": bad sizes");
+  if (rows == 0) return ok();
+  if (!delta || !residual || !w || !normed || !residual_out)
+    return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": null pointer");
+  if (rows > max_rows || hidden > row_elems)
+    return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": rows or hidden exceed the exchange buffer");
+  if (!is_float_dtype(dtype)) return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": float dtype expected");
+  const int V = static_cast<int>(16 / dtype_bytes(dtype));
+  if (hidden % V != 0 || row_elems % V != 0)
+    return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": hidden must be a multiple of 16 bytes");
+  if (ranks_in_launch > 1 && rank_stride % V != 0)
+    return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": rank_stride must be a multiple of 16 bytes");
+  const int64_t lanes = hidden / V;
+  const int64_t threads = std::max<int64_t>(64, ceil_div(ceil_div(lanes, kVpt), 32) * 32);
+  if (threads > 512) return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": hidden too large");
+  for (const void* ptr : {delta, residual, w, static_cast<const void*>(normed), static_cast<const void*>(residual_out)})
+    if (!aligned(ptr, 16)) return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": 16-byte aligned tensors expected");
+
+  ExchangeParams p{};
+  for (int i = 0; i < tp; ++i) {
+    if (buffers[i] == nullptr || !aligned(buffers[i], 256))
+      return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": exchange buffers must be 256-byte aligned");
+    p.buf[i] = static_cast<char*>(buffers[i]);
+  }
+  p.tp = tp;
+  p.rank0 = rank;
+  p.max_rows = max_rows;
+  p.row_elems = row_elems;
+  p.rank_stride = rank_stride;
+  p.rows = rows;
+  p.hidden = hidden;
+  p.eps = eps;
+  p.timeout_ns = timeout_ns > 0 ? static_cast<uint64_t>(timeout_ns) : kDefaultTimeoutNs;
+  p.err = device_error_word();
+
+  // Every CTA of the launch must be resident at once: rank 0's CTA r may wait
+  // for rank 1's CTA r, in this launch (several ranks on one device) or on a peer.
+  int per_sm = 0;
+  dli_status st = dispatch_float(dtype, name, [&](auto tag) {
+    using T = decltype(tag);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, allreduce_add_rms_norm_kernel<T>,
+                                                  static_cast<int>(threads), 0);
+  });
+  if (st != DLI_OK) return st;
+  if (static_cast<int64_t>(per_sm) * sm_count() < rows * ranks_in_launch)
+    return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": more rows than resident CTAs");
+  const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(ranks_in_launch));
+  st = dispatch_float(dtype, name, [&](auto tag) {
+    using T = decltype(tag);
+    if (ranks_in_launch == 1) {
+      launch_pdl(allreduce_add_rms_norm_kernel<T>, grid, dim3(static_cast<unsigned>(threads)), 0, as_stream(stream), p,
+                 (const T*)delta, (const T*)residual, (const T*)w, (T*)normed, (T*)residual_out);
+    } else {
+      // one cooperative launch over all ranks of the group: co-resident CTAs
+      const T* d = static_cast<const T*>(delta);
+      const T* res = static_cast<const T*>(residual);
+      const T* wt = static_cast<const T*>(w);
+      T* nm = static_cast<T*>(normed);
+      T* ro = static_cast<T*>(residual_out);
+      void* args[] = {&p, &d, &res, &wt, &nm, &ro};
+      cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(allreduce_add_rms_norm_kernel<T>), grid,
+                                  dim3(static_cast<unsigned>(threads)), args, 0, as_stream(stream));
+    }
+  });
+  if (st != DLI_OK) return st;
+  return check_launch(name);
+}

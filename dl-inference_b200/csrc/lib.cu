@@ -24,6 +24,7 @@ const char* device_error_name(unsigned code) {
     case kDevErrRotaryPosition: return "rotary position outside the cos/sin table";
     case kDevErrAttentionTimeout: return "attention pipeline wait exceeded its iteration limit";
     case kDevErrKvCapacity: return "KV-cache position outside the cache capacity";
+    case kDevErrExchangeTimeout: return "tensor-parallel exchange: a peer's rows did not arrive within the wait limit";
     default: return "unknown device error";
   }
 }

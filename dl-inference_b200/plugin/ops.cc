@@ -7,7 +7,7 @@
 // add, mul, silu, relu, softmax, max_pool2d, batch_norm2d, reshape, transpose)
 // plus additive fused operators for the batched Qwen2 graphs (add_rms_norm,
 // silu_mul, qkv_rotary_cache, attention_kvcache, last_token, argmax, cast,
-// all_reduce).
+// all_reduce, all_reduce_add_rms_norm).
 //
 // Every operator validates arity/dtype/shape on the host and throws
 // std::invalid_argument like the reference templates
@@ -16,9 +16,12 @@
 // on the run's stream (ExecutionContext::cuda_stream). There is no fallback:
 // every tensor op runs a kernel of this project.
 #include <ATen/ATen.h>
+#include <cuda_runtime.h>
 
 #include <cstring>
+#include <map>
 #include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -620,6 +623,87 @@ class AllReduceOp final : public dli::Operator {
   }
 };
 
+// ---------------------------------------------------------------------------
+// Tensor-parallel exchange buffers (one per communicator), created collectively
+// by dli_sm100_tp_exchange_create: a cudaMalloc'ed buffer per rank whose CUDA IPC
+// handle is all-gathered over the communicator and opened by every peer, so the
+// fused all-reduce kernel can store into every peer's buffer over NVLink.
+// ---------------------------------------------------------------------------
+struct Exchange {
+  int tp = 1, rank = 0, device = 0;
+  std::int64_t max_rows = 0, row_elems = 0;
+  dli_dtype dtype = DLI_DTYPE_BF16;
+  void* local = nullptr;
+  std::vector<void*> ptrs;  // rank i's buffer as mapped in this process
+};
+
+std::mutex g_exchange_mu;
+std::map<void*, std::unique_ptr<Exchange>>& exchanges() {
+  static std::map<void*, std::unique_ptr<Exchange>> m;
+  return m;
+}
+
+const Exchange* findExchange(void* comm) {
+  std::lock_guard<std::mutex> lock(g_exchange_mu);
+  auto it = exchanges().find(comm);
+  return it == exchanges().end() ? nullptr : it->second.get();
+}
+
+// all_reduce_add_rms_norm: (residual, delta, weight) -> (normed, residual + all_reduce(delta)).
+// The tensor-parallel form of add_rms_norm. With an exchange buffer registered
+// for the run's communicator and rows that fit it, one fused kernel does the
+// all-reduce over NVLink peer memory and the norm; otherwise (prefill-sized
+// rows, no buffer) an NCCL all_reduce followed by add_rms_norm. Both branches
+// depend only on shapes, so every rank of the group takes the same one.
+class AllReduceAddRmsNormOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "all_reduce_add_rms_norm"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 3, 3, 2, type());
+    floatInputs(in, 3, type());
+    const Tensor& r = *in[0];
+    const Tensor& d = *in[1];
+    if (d.shape() != r.shape()) throw std::invalid_argument("all_reduce_add_rms_norm residual/delta shape mismatch");
+    const std::int64_t hidden = r.shape().back();
+    if (static_cast<std::int64_t>(in[2]->numel()) != hidden)
+      throw std::invalid_argument("all_reduce_add_rms_norm weight size mismatch");
+    const std::int64_t rows = static_cast<std::int64_t>(r.numel()) / hidden;
+    const float eps = static_cast<float>(dli::attrDouble(attrs, "eps", 1e-6));
+    *out[0] = Tensor::cuda(r.dtype(), r.shape(), r.deviceId());
+    *out[1] = Tensor::cuda(r.dtype(), r.shape(), r.deviceId());
+    const void* delta = dli::ptr(d);
+    Tensor summed;
+    if (ctx.tp_size > 1) {
+      if (ctx.communicator == nullptr) throw std::invalid_argument(type() + ": no communicator for tp_size > 1");
+      const Exchange* ex = findExchange(ctx.communicator);
+      if (ex != nullptr && ex->tp == ctx.tp_size && ex->rank == ctx.tp_rank && ex->dtype == cdt(r.dtype()) &&
+          rows <= ex->max_rows && hidden <= ex->row_elems) {
+        const dli_status st = dli_sm100_allreduce_add_rms_norm(
+            ex->ptrs.data(), ex->tp, ex->rank, 1, ex->max_rows, ex->row_elems, delta, dli::ptr(r),
+            dli::ptr(*in[2]), out[0]->deviceData(), out[1]->deviceData(), 0, rows, hidden, eps, 0,
+            cdt(r.dtype()), ctx.cuda_stream);
+        if (st == DLI_OK) return;
+        if (st != DLI_ERR_UNSUPPORTED) check(st, type());
+      }
+#ifdef DLI_WITH_NCCL
+      summed = Tensor::cuda(d.dtype(), d.shape(), d.deviceId());
+      ncclDataType_t t = d.dtype() == DType::Float32 ? ncclFloat32
+                         : d.dtype() == DType::BFloat16 ? ncclBfloat16 : ncclFloat16;
+      const ncclResult_t res = ncclAllReduce(delta, summed.deviceData(), d.numel(), t, ncclSum,
+                                             static_cast<ncclComm_t>(ctx.communicator),
+                                             static_cast<cudaStream_t>(ctx.cuda_stream));
+      if (res != ncclSuccess) throw std::runtime_error(type() + ": " + ncclGetErrorString(res));
+      delta = summed.deviceData();
+#else
+      throw std::runtime_error(type() + ": plugin built without NCCL");
+#endif
+    }
+    check(dli_sm100_add_rms_norm(dli::ptr(r), delta, dli::ptr(*in[2]), out[0]->deviceData(), out[1]->deviceData(),
+                                 rows, hidden, eps, cdt(r.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
 }  // namespace
 
 extern "C" bool dli_register_operators(dli::OperatorRegistry* registry) {
@@ -649,6 +733,7 @@ extern "C" bool dli_register_operators(dli::OperatorRegistry* registry) {
   reg<ArgmaxOp>(registry, "argmax");
   reg<CastOp>(registry, "cast");
   reg<AllReduceOp>(registry, "all_reduce");
+  reg<AllReduceAddRmsNormOp>(registry, "all_reduce_add_rms_norm");
   return true;
 }
 
@@ -699,4 +784,96 @@ extern "C" void dli_sm100_nccl_comm_destroy(void* comm) {
 #else
   (void)comm;
 #endif
+}
+
+// Creates this rank's exchange buffer for `comm` and maps every peer's (a
+// collective: every rank of the communicator calls it at the same point).
+// Returns 0, or a negative code: -1 no NCCL, -2 bad arguments, -3 CUDA error,
+// -4 NCCL error.
+extern "C" int dli_sm100_tp_exchange_create(void* comm, int device, std::int64_t max_rows,
+                                            std::int64_t row_elems, int dtype) {
+#ifdef DLI_WITH_NCCL
+  if (comm == nullptr) return -2;
+  int tp = 0, rank = 0;
+  if (ncclCommCount(static_cast<ncclComm_t>(comm), &tp) != ncclSuccess ||
+      ncclCommUserRank(static_cast<ncclComm_t>(comm), &rank) != ncclSuccess)
+    return -4;
+  const std::size_t bytes = dli_sm100_tp_exchange_bytes(tp, max_rows, row_elems, static_cast<dli_dtype>(dtype));
+  if (bytes == 0) return -2;
+  if (cudaSetDevice(device) != cudaSuccess) return -3;
+  auto ex = std::make_unique<Exchange>();
+  ex->tp = tp;
+  ex->rank = rank;
+  ex->device = device;
+  ex->max_rows = max_rows;
+  ex->row_elems = row_elems;
+  ex->dtype = static_cast<dli_dtype>(dtype);
+  ex->ptrs.assign(tp, nullptr);
+  cudaStream_t s = nullptr;
+  void* handles_dev = nullptr;
+  std::vector<cudaIpcMemHandle_t> handles(tp);
+  int rc = 0;
+  if (cudaMalloc(&ex->local, bytes) != cudaSuccess || cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&handles_dev, sizeof(cudaIpcMemHandle_t) * tp) != cudaSuccess) {
+    rc = -3;
+  } else if (dli_sm100_tp_exchange_reset(ex->local, max_rows, s) != DLI_OK ||
+             cudaIpcGetMemHandle(&handles[rank], ex->local) != cudaSuccess ||
+             cudaMemcpyAsync(static_cast<char*>(handles_dev) + rank * sizeof(cudaIpcMemHandle_t), &handles[rank],
+                             sizeof(cudaIpcMemHandle_t), cudaMemcpyHostToDevice, s) != cudaSuccess) {
+    rc = -3;
+  } else if (ncclAllGather(static_cast<char*>(handles_dev) + rank * sizeof(cudaIpcMemHandle_t), handles_dev,
+                           sizeof(cudaIpcMemHandle_t), ncclChar, static_cast<ncclComm_t>(comm), s) != ncclSuccess) {
+    rc = -4;
+  } else if (cudaMemcpyAsync(handles.data(), handles_dev, sizeof(cudaIpcMemHandle_t) * tp, cudaMemcpyDeviceToHost, s) !=
+                 cudaSuccess ||
+             cudaStreamSynchronize(s) != cudaSuccess) {
+    rc = -3;
+  }
+  // After the all-gather completed here, every rank's header reset (ordered
+  // before its all-gather on its stream) has completed too.
+  for (int i = 0; rc == 0 && i < tp; ++i) {
+    if (i == rank) {
+      ex->ptrs[i] = ex->local;
+    } else if (cudaIpcOpenMemHandle(&ex->ptrs[i], handles[i], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      rc = -3;
+    }
+  }
+  if (handles_dev) cudaFree(handles_dev);
+  if (s) cudaStreamDestroy(s);
+  if (rc != 0) {
+    for (int i = 0; i < tp; ++i)
+      if (i != rank && ex->ptrs[i]) cudaIpcCloseMemHandle(ex->ptrs[i]);
+    if (ex->local) cudaFree(ex->local);
+    cudaGetLastError();
+    return rc;
+  }
+  std::lock_guard<std::mutex> lock(g_exchange_mu);
+  exchanges()[comm] = std::move(ex);
+  return 0;
+#else
+  (void)comm;
+  (void)device;
+  (void)max_rows;
+  (void)row_elems;
+  (void)dtype;
+  return -1;
+#endif
+}
+
+// Unmaps the peers' buffers and frees this rank's. Call when no kernel of the
+// group is in flight on any rank (after a device synchronisation and a barrier),
+// before the communicator is destroyed.
+extern "C" void dli_sm100_tp_exchange_destroy(void* comm) {
+  std::unique_ptr<Exchange> ex;
+  {
+    std::lock_guard<std::mutex> lock(g_exchange_mu);
+    auto it = exchanges().find(comm);
+    if (it == exchanges().end()) return;
+    ex = std::move(it->second);
+    exchanges().erase(it);
+  }
+  cudaSetDevice(ex->device);
+  for (int i = 0; i < ex->tp; ++i)
+    if (i != ex->rank && ex->ptrs[i]) cudaIpcCloseMemHandle(ex->ptrs[i]);
+  if (ex->local) cudaFree(ex->local);
 }

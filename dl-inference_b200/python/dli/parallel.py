@@ -62,10 +62,14 @@ class TensorParallelComm:
     group, so every rank takes the same collective steps whatever its group.
 
     `handle` is the ncclComm_t as an integer for Engine.set_communicator (0 when
-    tp == 1). Call destroy() after every CUDA graph that captured an all_reduce
-    on it has been released."""
+    tp == 1). With `exchange=(max_rows, row_elems, dtype_code)` it also creates
+    the group's NVLink exchange buffers (dli_sm100_tp_exchange_create), which
+    the `all_reduce_add_rms_norm` operator uses for rows <= max_rows. Call
+    destroy() after every CUDA graph that captured a collective on it has been
+    released; it synchronises the device and the group first."""
 
-    def __init__(self, layout: ParallelLayout, device_index: int, plugin: str = PLUGIN_PATH):
+    def __init__(self, layout: ParallelLayout, device_index: int, plugin: str = PLUGIN_PATH,
+                 exchange: tuple[int, int, int] | None = None):
         import torch.distributed as dist
 
         self.layout = layout
@@ -79,6 +83,10 @@ class TensorParallelComm:
         lib.dli_sm100_nccl_comm_init.restype = ctypes.c_void_p
         lib.dli_sm100_nccl_comm_init.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
         lib.dli_sm100_nccl_comm_destroy.argtypes = [ctypes.c_void_p]
+        lib.dli_sm100_tp_exchange_create.restype = ctypes.c_int
+        lib.dli_sm100_tp_exchange_create.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
+                                                     ctypes.c_int64, ctypes.c_int]
+        lib.dli_sm100_tp_exchange_destroy.argtypes = [ctypes.c_void_p]
         ids: list[Any] = [None] * layout.dp
         if layout.rank == 0:
             for g in range(layout.dp):
@@ -93,8 +101,28 @@ class TensorParallelComm:
         if not handle:
             raise RuntimeError(f"ncclCommInitRank failed on rank {layout.rank} (group {layout.group})")
         self.handle, self._lib = int(handle), lib
+        self.exchange = None
+        if exchange is not None:
+            rc = lib.dli_sm100_tp_exchange_create(ctypes.c_void_p(self.handle), device_index, *exchange)
+            # every rank learns whether every rank succeeded (the operator must take
+            # the same branch on all of them)
+            import torch
+            flag = torch.tensor([1 if rc == 0 else 0], device=f"cuda:{device_index}")
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            if int(flag.item()) != 1:
+                if rc == 0:
+                    lib.dli_sm100_tp_exchange_destroy(ctypes.c_void_p(self.handle))
+                raise RuntimeError(f"tensor-parallel exchange buffers unavailable (rank {layout.rank}: code {rc})")
+            self.exchange = exchange
+        self._device = device_index
 
     def destroy(self) -> None:
         if self.handle and self._lib is not None:
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.synchronize(self._device)
+            dist.barrier()  # no rank still pushes into a buffer about to be unmapped
+            self._lib.dli_sm100_tp_exchange_destroy(ctypes.c_void_p(self.handle))
             self._lib.dli_sm100_nccl_comm_destroy(ctypes.c_void_p(self.handle))
         self.handle = 0

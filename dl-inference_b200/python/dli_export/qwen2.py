@@ -156,6 +156,9 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
         nodes.append({"name": name, "op": op, "inputs": inputs, "outputs": outputs, "attrs": attrs or {}})
 
     eps = float(shape.rms_eps)
+    # residual add + RMSNorm after a row-split projection; with tensor parallelism
+    # the projection's output is a partial sum, all-reduced by the same node
+    add_norm = "all_reduce_add_rms_norm" if tp_size > 1 else "add_rms_norm"
     node("embed_tokens", "embedding", ["input_ids", "embed"], ["h0"])
     resid, delta = "h0", None
     for i in range(shape.layers):
@@ -163,7 +166,7 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
         if delta is None:
             node(f"{L}.input_layernorm", "rms_norm", [resid, f"{L}.ln_in"], [f"{L}.x"], {"eps": eps})
         else:
-            node(f"{L}.input_layernorm", "add_rms_norm", [resid, delta, f"{L}.ln_in"],
+            node(f"{L}.input_layernorm", add_norm, [resid, delta, f"{L}.ln_in"],
                  [f"{L}.x", f"{L}.h_in"], {"eps": eps})
             resid = f"{L}.h_in"
         node(f"{L}.qkv_proj", "linear", [f"{L}.x", f"{L}.wqkv", f"{L}.bqkv"], [f"{L}.qkv"])
@@ -174,21 +177,14 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
         node(f"{L}.attention", "attention_kvcache", [f"{L}.q", "positions"], [f"{L}.attn"],
              {"kv_cache": f"layer_{i}"})
         node(f"{L}.o_proj", "linear", [f"{L}.attn", f"{L}.wo"], [f"{L}.o_part"])
-        o = f"{L}.o_part"
-        if tp_size > 1:
-            node(f"{L}.o_allreduce", "all_reduce", [o], [f"{L}.o"])
-            o = f"{L}.o"
-        node(f"{L}.post_attention_layernorm", "add_rms_norm", [resid, o, f"{L}.ln_post"],
+        node(f"{L}.post_attention_layernorm", add_norm, [resid, f"{L}.o_part", f"{L}.ln_post"],
              [f"{L}.x2", f"{L}.h_mid"], {"eps": eps})
         resid = f"{L}.h_mid"
         node(f"{L}.gate_up_proj", "linear", [f"{L}.x2", f"{L}.wgu"], [f"{L}.gu"])
         node(f"{L}.act", "silu_mul", [f"{L}.gu"], [f"{L}.act"])
         node(f"{L}.down_proj", "linear", [f"{L}.act", f"{L}.wd"], [f"{L}.d_part"])
         delta = f"{L}.d_part"
-        if tp_size > 1:
-            node(f"{L}.d_allreduce", "all_reduce", [delta], [f"{L}.d"])
-            delta = f"{L}.d"
-    node("norm", "add_rms_norm", [resid, delta, "norm"], ["normed", "h_out"], {"eps": eps})
+    node("norm", add_norm, [resid, delta, "norm"], ["normed", "h_out"], {"eps": eps})
     node("last_token", "last_token", ["normed"], ["last_hidden"])
     node("lm_head", "linear", ["last_hidden", "lm_head"], ["logits"])
     outputs = ["logits"]

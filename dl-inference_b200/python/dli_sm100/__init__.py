@@ -67,6 +67,9 @@ SIGNATURES = {
     "dli_sm100_argmax": (N, [P, P, I, I, D, P]),
     "dli_sm100_select_token": (N, [P, P, I, I, I, I, D, P]),
     "dli_sm100_cast": (N, [P, D, P, D, I, P]),
+    "dli_sm100_tp_exchange_bytes": (Z, [D, I, I, D]),
+    "dli_sm100_tp_exchange_reset": (N, [P, I, P]),
+    "dli_sm100_allreduce_add_rms_norm": (N, [P, D, D, D, I, I, P, P, P, P, P, I, I, I, F, I, D, P]),
 }
 
 _lib = None
@@ -201,6 +204,38 @@ def add_rms_norm(residual, delta, w, eps=1e-6, residual_out=None):
                                        _ptr(residual_out), residual.numel() // hidden, hidden, eps,
                                        _dt(residual), _stream()), "add_rms_norm")
     return normed, residual_out
+
+
+class ExchangeGroup:
+    """Exchange buffers of a whole tensor-parallel group on ONE device, for
+    running every rank of the group in one cooperative launch of
+    dli_sm100_allreduce_add_rms_norm (ranks_in_launch = tp). Multi-process
+    groups map each rank's buffer through CUDA IPC in the operator plugin."""
+
+    def __init__(self, tp, max_rows, row_elems, dtype=torch.bfloat16, device="cuda"):
+        nbytes = lib().dli_sm100_tp_exchange_bytes(tp, max_rows, row_elems, DTYPE_CODES[dtype])
+        if nbytes == 0:
+            raise ValueError("unsupported exchange shape")
+        # torch's allocator returns 512-byte aligned blocks
+        self.buffers = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in range(tp)]
+        self.tp, self.max_rows, self.row_elems, self.dtype = tp, max_rows, row_elems, dtype
+        for b in self.buffers:
+            check(lib().dli_sm100_tp_exchange_reset(_ptr(b), max_rows, _stream()), "tp_exchange_reset")
+        self._ptrs = (ctypes.c_void_p * tp)(*[b.data_ptr() for b in self.buffers])
+
+    def allreduce_add_rms_norm(self, residual, delta, w, eps=1e-6, timeout_ns=0, ranks=None):
+        """residual/delta [tp, rows, hidden] (rank-major); returns (normed, residual_out).
+        ranks < tp launches only ranks 0..ranks-1 (their waits for the others run out)."""
+        _contig(residual, delta, w)
+        tp, rows, hidden = delta.shape
+        ranks = tp if ranks is None else ranks
+        normed, residual_out = torch.empty_like(residual), torch.empty_like(residual)
+        st = lib().dli_sm100_allreduce_add_rms_norm(
+            self._ptrs, self.tp, 0, ranks, self.max_rows, self.row_elems, _ptr(delta), _ptr(residual),
+            _ptr(w), _ptr(normed), _ptr(residual_out), rows * hidden, rows, hidden, eps, timeout_ns,
+            _dt(delta), _stream())
+        check(st, "allreduce_add_rms_norm")
+        return normed, residual_out
 
 
 def batch_norm2d(x, weight, bias, running_mean, running_var, eps=1e-5):

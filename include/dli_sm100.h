@@ -253,6 +253,45 @@ dli_status dli_sm100_select_token(const void* x, void* out, int64_t batch, int64
 dli_status dli_sm100_cast(const void* x, dli_dtype x_dtype, void* out, dli_dtype out_dtype,
                           int64_t n, void* stream);
 
+/* ---- tensor-parallel exchange ---------------------------------------------
+ * No counterpart in the reference, which runs every graph on one device. Used
+ * by the Qwen2 tensor-parallel graphs (all_reduce after o_proj and down_proj).
+ *
+ * Each rank of a tensor-parallel group owns one exchange buffer of
+ * dli_sm100_tp_exchange_bytes(tp, max_rows, row_elems, dtype) bytes, 256-byte
+ * aligned, mapped into every other rank's process (CUDA IPC). Before first use
+ * every rank zeroes its buffer's header with dli_sm100_tp_exchange_reset and
+ * the group synchronises on the host; afterwards the buffers are never reset
+ * (epochs advance on the device, so CUDA-graph replays need no host work).
+ * Returns 0 for unsupported arguments (tp outside 1..8). */
+size_t dli_sm100_tp_exchange_bytes(int tp, int64_t max_rows, int64_t row_elems, dli_dtype dtype);
+dli_status dli_sm100_tp_exchange_reset(void* buffer, int64_t max_rows, void* stream);
+
+/* All-reduce of `delta` over the group fused with add_rms_norm:
+ * residual_out = residual + sum_ranks(delta) (the sum rounded to dtype, as an
+ * all_reduce returns it); normed = rms_norm(residual_out, w) exactly as
+ * dli_sm100_add_rms_norm. One CTA per row pushes its row of delta into every
+ * peer's buffer over NVLink and waits (bounded by timeout_ns, 0 = 2 s) for the
+ * peers' rows; the sum runs in rank order, so every rank gets identical bits.
+ * A wait that runs out sets the device error word (dli_sm100_check_device_error)
+ * instead of hanging. Every rank of the group must make the same calls with
+ * the same rows, in the same order.
+ *   buffers[i]      rank i's exchange buffer as mapped in this process (tp entries)
+ *   rank            this process's rank; ranks_in_launch = 1 for one process per GPU.
+ *                   ranks_in_launch = tp (with rank = 0) runs the whole group in one
+ *                   cooperative launch on one device, all buffers on that device,
+ *                   per-rank tensors rank_stride elements apart (a test harness mode)
+ *   rows <= max_rows, hidden <= row_elems, hidden * element size a multiple of 16
+ * residual_out may alias residual. DLI_ERR_UNSUPPORTED when the shape does not
+ * fit the exchange buffer or the launch cannot be resident at once (callers
+ * then fall back to a library all-reduce + dli_sm100_add_rms_norm). */
+dli_status dli_sm100_allreduce_add_rms_norm(void* const* buffers, int tp, int rank, int ranks_in_launch,
+                                            int64_t max_rows, int64_t row_elems, const void* delta,
+                                            const void* residual, const void* w, void* normed,
+                                            void* residual_out, int64_t rank_stride, int64_t rows,
+                                            int64_t hidden, float eps, int64_t timeout_ns, dli_dtype dtype,
+                                            void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -50,6 +50,10 @@ class GraphOracle:
             return [np.asarray(x[0])[:, a.get("index", np.asarray(x[0]).shape[1] - 1)]]
         if op == "argmax":
             return [O.argmax(x[0])]
+        if op == "all_reduce_add_rms_norm":
+            d = x[1] if self.all_reduce is None else self.all_reduce(np.asarray(x[1]))
+            n, r = O.add_rms_norm(x[0], d, x[2], a.get("eps", 1e-6))
+            return [n, r]
         if op == "all_reduce":
             return [x[0] if self.all_reduce is None else self.all_reduce(np.asarray(x[0]))]
         if op == "qkv_rotary_cache":

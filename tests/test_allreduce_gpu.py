@@ -1,0 +1,96 @@
+"""GPU tests of dli_sm100_allreduce_add_rms_norm, the tensor-parallel
+all-reduce fused with the residual add and RMSNorm, on ONE device: every rank
+of the group runs in one cooperative launch (ranks_in_launch = tp) over
+exchange buffers that all live on this device, so the push / flag / bounded
+wait protocol runs exactly as across GPUs, without two launches waiting on
+each other.
+
+Expected values: the rank-ordered fp32 sum of the partials rounded to the
+dtype (what an all_reduce returns), fed to dli_sm100_add_rms_norm. The fused
+kernel must match that bit for bit on every rank, and every rank must hold the
+same bits. The float64 oracle (oracle/ops.py add_rms_norm over the summed
+partials) bounds both at bf16 tolerance.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import dli_sm100 as C
+from oracle import ops as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _expected(residual, delta, w, eps):
+    acc = delta[0].float()
+    for k in range(1, delta.shape[0]):
+        acc = acc + delta[k].float()
+    summed = acc.to(delta.dtype)
+    return C.add_rms_norm(residual[0], summed, w, eps)
+
+
+def _case(tp, rows, hidden, dtype, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    residual = torch.randn(rows, hidden, device="cuda", generator=g).to(dtype)
+    residual = residual.unsqueeze(0).expand(tp, rows, hidden).contiguous()  # replicated on every rank
+    delta = (torch.randn(tp, rows, hidden, device="cuda", generator=g) * 0.5).to(dtype)
+    w = (1 + 0.1 * torch.randn(hidden, device="cuda", generator=g)).to(dtype)
+    return residual, delta, w
+
+
+@pytest.mark.parametrize("tp", [2, 4, 8])
+@pytest.mark.parametrize("rows,hidden", [(1, 896), (32, 3584), (64, 8192), (7, 1024)])
+def test_fused_allreduce_matches_sum_then_add_rms_norm(tp, rows, hidden):
+    group = C.ExchangeGroup(tp, max_rows=64, row_elems=8192, dtype=torch.bfloat16)
+    for seed in range(3):  # consecutive calls: epochs advance, slots alternate
+        residual, delta, w = _case(tp, rows, hidden, torch.bfloat16, seed)
+        normed, res_out = group.allreduce_add_rms_norm(residual, delta, w, eps=1e-6)
+        ref_n, ref_r = _expected(residual, delta, w, 1e-6)
+        torch.cuda.synchronize()
+        for k in range(tp):
+            assert torch.equal(res_out[k], ref_r), (seed, k)
+            assert torch.equal(normed[k], ref_n), (seed, k)
+    # float64 oracle on the last case
+    d64 = delta.double().cpu().numpy().sum(0)
+    on, orr = O.add_rms_norm(residual[0].double().cpu().numpy(), d64, w.double().cpu().numpy(), 1e-6)
+    rel = np.linalg.norm(normed[0].double().cpu().numpy() - on) / np.linalg.norm(on)
+    assert rel < 1.5e-2, rel
+    C.check_device_error()
+
+
+def test_fp32_and_changing_row_counts():
+    tp = 4
+    group = C.ExchangeGroup(tp, max_rows=128, row_elems=4096, dtype=torch.float32)
+    for seed, rows in enumerate([128, 3, 64, 128, 1]):
+        residual, delta, w = _case(tp, rows, 4096, torch.float32, 10 + seed)
+        normed, res_out = group.allreduce_add_rms_norm(residual, delta, w, eps=1e-5)
+        ref_n, ref_r = _expected(residual, delta, w, 1e-5)
+        torch.cuda.synchronize()
+        for k in range(tp):
+            assert torch.equal(res_out[k], ref_r), (rows, k)
+            assert torch.equal(normed[k], ref_n), (rows, k)
+    C.check_device_error()
+
+
+def test_missing_peer_times_out_with_an_error_status():
+    """Only rank 0 of a two-rank group is launched: its wait for rank 1's rows
+    (a flag nothing sets) must run out after the stated limit and report through
+    the device error word; the context stays usable."""
+    group = C.ExchangeGroup(2, max_rows=8, row_elems=1024, dtype=torch.bfloat16)
+    residual, delta, w = _case(2, 4, 1024, torch.bfloat16, 0)
+    group.allreduce_add_rms_norm(residual, delta, w, timeout_ns=50_000_000, ranks=1)
+    with pytest.raises(RuntimeError, match="exchange"):
+        C.check_device_error()
+    # the device still works and the error word was cleared
+    x = torch.ones(4, 1024, device="cuda", dtype=torch.bfloat16)
+    C.rms_norm(x, torch.ones(1024, device="cuda", dtype=torch.bfloat16))
+    C.check_device_error()
+
+
+def test_rejects_shapes_beyond_the_exchange_buffer():
+    group = C.ExchangeGroup(2, max_rows=8, row_elems=1024, dtype=torch.bfloat16)
+    residual, delta, w = _case(2, 16, 1024, torch.bfloat16, 0)
+    with pytest.raises(RuntimeError, match="exceed"):
+        group.allreduce_add_rms_norm(residual, delta, w)

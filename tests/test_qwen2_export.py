@@ -54,7 +54,10 @@ def test_graph_structure_per_layer():
     assert ops[19:] == ["add_rms_norm", "last_token", "linear", "argmax"]
     assert g["inputs"] == ["input_ids", "positions"] and g["outputs"] == ["logits", "next_ids"]
     g2 = build_graph(TINY, capacity=64, tp_size=2)
-    assert [n["op"] for n in g2["nodes"]].count("all_reduce") == 2 * TINY.layers
+    ops2 = [n["op"] for n in g2["nodes"]]
+    # every add_rms_norm after a row-split projection becomes the all-reduce form
+    assert ops2.count("all_reduce_add_rms_norm") == 2 * TINY.layers
+    assert "add_rms_norm" not in ops2 and "all_reduce" not in ops2
     rc = next(n for n in g2["nodes"] if n["op"] == "qkv_rotary_cache")
     assert rc["attrs"]["q_heads"] == 2 and rc["attrs"]["kv_heads"] == 1
 
@@ -148,9 +151,11 @@ def _run_tp(oracles, ids, pos, ref):
         for o, env in zip(oracles, envs):
             n = o.graph["nodes"][idx]
             outs.append(o._op(n["op"], [env[x] for x in n["inputs"]], n.get("attrs", {})))
-        if node["op"] == "all_reduce":
-            total = sum(np.asarray(r[0]) for r in outs)
-            outs = [[total] for _ in outs]
+        if node["op"] == "all_reduce_add_rms_norm":
+            # sum the partials (input 1) over the ranks, then the residual add + norm
+            total = sum(np.asarray(env[node["inputs"][1]]) for env in envs)
+            outs = [o._op("add_rms_norm", [env[node["inputs"][0]], total, env[node["inputs"][2]]], node["attrs"])
+                    for o, env in zip(oracles, envs)]
         for env, res in zip(envs, outs):
             for name, val in zip(node["outputs"], res):
                 env[name] = val
