@@ -2,27 +2,31 @@
 // follow it in a Megatron block (o_proj -> all_reduce -> add_rms_norm and
 // down_proj -> all_reduce -> add_rms_norm).
 //
-// One-shot push over NVLink peer memory. Every rank owns an exchange buffer of
-// the same size, mapped into every other rank's address space (CUDA IPC):
+// One-shot push over NVLink peer memory with a low-latency word format: every
+// 8-byte word carries 4 payload bytes and the 4-byte epoch of the call that
+// wrote it, stored and loaded as one single-copy-atomic 64-bit access. A reader
+// that sees the current epoch in a word therefore sees that call's payload, so
+// the protocol needs no memory fence and no separate flag: the only latency is
+// one NVLink store. Every rank owns an exchange buffer of the same size, mapped
+// into every other rank's address space (CUDA IPC):
 //
-//   flags  u32 [kMaxRanks][max_rows]      written by peers: arrival epoch of
-//                                         (source rank, row)
-//   epochs u32 [max_rows]                 local: last epoch of each row's CTA
-//   data   T   [2 slots][tp][max_rows][row_elems]
+//   epochs u32 [max_rows]                        local: last epoch of each row's CTA
+//   words  u64 [2 slots][tp][max_rows][row_words] written by peers (row_words =
+//                                                row_elems * sizeof(T) / 4)
 //
-// CTA r (one per row) of rank k takes epoch e = epochs[r] + 1, stores its row of
-// the partial sum into slot e&1, source k, row r of every peer's buffer, fences
-// at system scope and release-stores e into flags[k][r] of every peer. It then
-// acquires flags[j][r] >= e for every peer j (a bounded wait), sums the tp
-// partial rows in rank order 0..tp-1 (so every rank computes bit-identical
-// results), rounds to T (the value an all_reduce would return), adds the
-// residual and applies RMSNorm exactly as dli_sm100_add_rms_norm does.
+// CTA r (one per row) of rank k takes epoch e = epochs[r] + 1 and stores its row
+// of the partial sum into slot e&1, source k, row r of every peer's buffer. It
+// then polls its own buffer's words of every peer j until they carry epoch e (a
+// bounded wait), sums the tp partial rows in rank order 0..tp-1 (so every rank
+// computes bit-identical results), rounds to T (the value an all_reduce would
+// return), adds the residual and applies RMSNorm as dli_sm100_add_rms_norm does.
 //
 // Why two slots suffice: CTA r of rank k writes slot e&1 of a peer j only after
-// its wait at epoch e-1 saw peer j's row-r push of epoch e-1. That push happens
-// after j's kernel passed griddepcontrol.wait, i.e. after every earlier kernel
-// of j's stream, including the one that read slot e&1 at epoch e-2, completed.
-// Rows live at fixed offsets, so calls with different row counts never overlap.
+// its own call at epoch e-1 read peer j's epoch e-1 words. j stored those after
+// its kernel passed griddepcontrol.wait, i.e. after every earlier kernel of j's
+// stream, including the one that read slot e&1 at epoch e-2, completed. Rows
+// live at fixed offsets, so calls with different row counts never overlap, and
+// a word left from epoch e-2 never matches epoch e.
 #include <algorithm>
 
 #include "common.cuh"
@@ -39,7 +43,7 @@ struct ExchangeParams {
   char* buf[kMaxRanks];      // exchange buffer of each rank, as mapped in this process
   int tp;
   int rank0;                 // rank of blockIdx.y == 0
-  int64_t max_rows, row_elems;
+  int64_t max_rows, row_words;
   int64_t rank_stride;       // elements between ranks' tensors when one launch runs several ranks
   int64_t rows, hidden;
   float eps;
@@ -48,8 +52,7 @@ struct ExchangeParams {
 };
 
 __host__ __device__ inline int64_t header_bytes(int64_t max_rows) {
-  const int64_t raw = (static_cast<int64_t>(kMaxRanks) + 1) * max_rows * 4;
-  return (raw + kHeaderAlign - 1) / kHeaderAlign * kHeaderAlign;
+  return (max_rows * 4 + kHeaderAlign - 1) / kHeaderAlign * kHeaderAlign;
 }
 
 __device__ __forceinline__ uint64_t timer_ns() {
@@ -57,19 +60,48 @@ __device__ __forceinline__ uint64_t timer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// two low-latency words: payload in the low half, epoch in the high half
+__device__ __forceinline__ void st_ll2(uint64_t* p, uint32_t a, uint32_t b, uint32_t e) {
+  const uint64_t wa = (static_cast<uint64_t>(e) << 32) | a;
+  const uint64_t wb = (static_cast<uint64_t>(e) << 32) | b;
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(wa), "l"(wb) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void ld_ll2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
-template <typename T>
-__device__ __forceinline__ T* row_slot(char* base, const ExchangeParams& p, int slot, int src, int64_t row) {
-  T* data = reinterpret_cast<T*>(base + header_bytes(p.max_rows));
-  return data + ((static_cast<int64_t>(slot) * p.tp + src) * p.max_rows + row) * p.row_elems;
+__device__ __forceinline__ uint64_t* row_words(char* base, const ExchangeParams& p, int slot, int src, int64_t row) {
+  uint64_t* w = reinterpret_cast<uint64_t*>(base + header_bytes(p.max_rows));
+  return w + ((static_cast<int64_t>(slot) * p.tp + src) * p.max_rows + row) * p.row_words;
+}
+
+// Waits until the 4 words at `p` carry epoch e; returns their payload. On
+// timeout records the error in `failed` (and the device word) and returns what
+// is there.
+__device__ __forceinline__ uint4 wait_ll4(const uint64_t* p, uint32_t e, uint64_t timeout_ns, unsigned* err,
+                                          bool& failed) {
+  uint64_t w0, w1, w2, w3;
+  ld_ll2(p, w0, w1);
+  ld_ll2(p + 2, w2, w3);
+  auto ready = [&] {
+    return static_cast<uint32_t>(w0 >> 32) == e && static_cast<uint32_t>(w1 >> 32) == e &&
+           static_cast<uint32_t>(w2 >> 32) == e && static_cast<uint32_t>(w3 >> 32) == e;
+  };
+  if (!ready() && !failed) {
+    const uint64_t start = timer_ns();
+    while (true) {
+      ld_ll2(p, w0, w1);
+      ld_ll2(p + 2, w2, w3);
+      if (ready()) break;
+      if (timer_ns() - start > timeout_ns) {
+        set_device_error(err, kDevErrExchangeTimeout);
+        failed = true;
+        break;
+      }
+    }
+  }
+  return make_uint4(static_cast<uint32_t>(w0), static_cast<uint32_t>(w1), static_cast<uint32_t>(w2),
+                    static_cast<uint32_t>(w3));
 }
 
 template <typename T>
@@ -85,58 +117,40 @@ __global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
   const int64_t r = blockIdx.x;
   const int64_t off = static_cast<int64_t>(blockIdx.y) * p.rank_stride + r * p.hidden;
   char* mine = p.buf[rank];
-  uint32_t* flags = reinterpret_cast<uint32_t*>(mine);
-  uint32_t* epochs = flags + kMaxRanks * p.max_rows;
+  uint32_t* epochs = reinterpret_cast<uint32_t*>(mine);
   if (threadIdx.x == 0) s_epoch = epochs[r] + 1u;
   __syncthreads();
   const uint32_t e = s_epoch;
   const int slot = static_cast<int>(e & 1u);
   const int64_t lanes = p.hidden / V;
 
-  // 1. own partial row into registers, pushed to every peer
+  // 1. own partial row into registers, pushed to every peer (4 words per 16 bytes)
   Vec16<T> own[kVpt];
 #pragma unroll
   for (int i = 0; i < kVpt; ++i) {
-    const int64_t c = (threadIdx.x + static_cast<int64_t>(i) * blockDim.x);
+    const int64_t c = threadIdx.x + static_cast<int64_t>(i) * blockDim.x;
     if (c < lanes) own[i] = load16(delta + off + c * V);
   }
   for (int q = 0; q < p.tp; ++q) {
     if (q == rank) continue;
-    T* dst = row_slot<T>(p.buf[q], p, slot, rank, r);
+    uint64_t* dst = row_words(p.buf[q], p, slot, rank, r);
 #pragma unroll
     for (int i = 0; i < kVpt; ++i) {
-      const int64_t c = (threadIdx.x + static_cast<int64_t>(i) * blockDim.x);
-      if (c < lanes) store16(dst + c * V, own[i]);
-    }
-  }
-  __threadfence_system();
-  __syncthreads();
-  if (static_cast<int>(threadIdx.x) < p.tp && static_cast<int>(threadIdx.x) != rank) {
-    uint32_t* peer_flags = reinterpret_cast<uint32_t*>(p.buf[threadIdx.x]);
-    st_release_sys(peer_flags + static_cast<int64_t>(rank) * p.max_rows + r, e);
-  }
-
-  // 2. wait for every peer's row (bounded: on timeout record the error and go on)
-  if (static_cast<int>(threadIdx.x) < p.tp && static_cast<int>(threadIdx.x) != rank) {
-    const uint32_t* f = flags + static_cast<int64_t>(threadIdx.x) * p.max_rows + r;
-    if (static_cast<int32_t>(ld_acquire_sys(f) - e) < 0) {
-      const uint64_t start = timer_ns();
-      while (static_cast<int32_t>(ld_acquire_sys(f) - e) < 0) {
-        if (timer_ns() - start > p.timeout_ns) {
-          set_device_error(p.err, kDevErrExchangeTimeout);
-          break;
-        }
+      const int64_t c = threadIdx.x + static_cast<int64_t>(i) * blockDim.x;
+      if (c < lanes) {
+        st_ll2(dst + c * 4, own[i].raw.x, own[i].raw.y, e);
+        st_ll2(dst + c * 4 + 2, own[i].raw.z, own[i].raw.w, e);
       }
     }
   }
-  __syncthreads();
 
-  // 3. rank-ordered sum, residual add, RMSNorm
+  // 2. rank-ordered sum; each peer's words are awaited where they are consumed
   float acc[kVpt][V];
 #pragma unroll
   for (int i = 0; i < kVpt; ++i)
 #pragma unroll
     for (int j = 0; j < V; ++j) acc[i][j] = 0.f;
+  bool failed = false;
   for (int src = 0; src < p.tp; ++src) {
     if (src == rank) {
 #pragma unroll
@@ -145,22 +159,24 @@ __global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
         for (int j = 0; j < V; ++j) acc[i][j] += to_f32(own[i].e[j]);
       continue;
     }
-    const T* s = row_slot<T>(mine, p, slot, src, r);
+    const uint64_t* s = row_words(mine, p, slot, src, r);
 #pragma unroll
     for (int i = 0; i < kVpt; ++i) {
-      const int64_t c = (threadIdx.x + static_cast<int64_t>(i) * blockDim.x);
+      const int64_t c = threadIdx.x + static_cast<int64_t>(i) * blockDim.x;
       if (c < lanes) {
         Vec16<T> v;
-        *reinterpret_cast<uint4*>(&v) = __ldcg(reinterpret_cast<const uint4*>(s + c * V));
+        v.raw = wait_ll4(s + c * 4, e, p.timeout_ns, p.err, failed);
 #pragma unroll
         for (int j = 0; j < V; ++j) acc[i][j] += to_f32(v.e[j]);
       }
     }
   }
+
+  // 3. residual add and RMSNorm
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < kVpt; ++i) {
-    const int64_t c = (threadIdx.x + static_cast<int64_t>(i) * blockDim.x);
+    const int64_t c = threadIdx.x + static_cast<int64_t>(i) * blockDim.x;
     if (c < lanes) {
       Vec16<T> res = load16(residual + off + c * V);
 #pragma unroll
@@ -178,7 +194,7 @@ __global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
   const float inv = rsqrtf(total / static_cast<float>(p.hidden) + p.eps);
 #pragma unroll
   for (int i = 0; i < kVpt; ++i) {
-    const int64_t c = (threadIdx.x + static_cast<int64_t>(i) * blockDim.x);
+    const int64_t c = threadIdx.x + static_cast<int64_t>(i) * blockDim.x;
     if (c < lanes) {
       Vec16<T> g = load16(w + c * V), o;
 #pragma unroll
@@ -196,13 +212,15 @@ using namespace dli_sm100;
 
 extern "C" size_t dli_sm100_tp_exchange_bytes(int tp, int64_t max_rows, int64_t row_elems, dli_dtype dtype) {
   if (tp < 1 || tp > kMaxRanks || max_rows <= 0 || row_elems <= 0 || !is_float_dtype(dtype)) return 0;
+  // 8-byte words carrying 4 payload bytes each
   return static_cast<size_t>(header_bytes(max_rows)) +
-         static_cast<size_t>(2) * tp * max_rows * row_elems * dtype_bytes(dtype);
+         static_cast<size_t>(2) * tp * max_rows * (row_elems * dtype_bytes(dtype) / 4) * 8;
 }
 
-extern "C" dli_status dli_sm100_tp_exchange_reset(void* buffer, int64_t max_rows, void* stream) {
-  if (buffer == nullptr || max_rows <= 0) return fail(DLI_ERR_INVALID_ARGUMENT, "tp_exchange_reset: bad arguments");
-  if (cudaMemsetAsync(buffer, 0, static_cast<size_t>(header_bytes(max_rows)), as_stream(stream)) != cudaSuccess)
+extern "C" dli_status dli_sm100_tp_exchange_reset(void* buffer, size_t bytes, void* stream) {
+  // zero epochs and words: a word matches an epoch only once a peer stored it
+  if (buffer == nullptr || bytes == 0) return fail(DLI_ERR_INVALID_ARGUMENT, "tp_exchange_reset: bad arguments");
+  if (cudaMemsetAsync(buffer, 0, bytes, as_stream(stream)) != cudaSuccess)
     return fail(DLI_ERR_CUDA, std::string("tp_exchange_reset: ") + cudaGetErrorString(cudaGetLastError()));
   return ok();
 }
@@ -244,7 +262,7 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm(
   p.tp = tp;
   p.rank0 = rank;
   p.max_rows = max_rows;
-  p.row_elems = row_elems;
+  p.row_words = row_elems * static_cast<int64_t>(dtype_bytes(dtype)) / 4;
   p.rank_stride = rank_stride;
   p.rows = rows;
   p.hidden = hidden;

@@ -816,7 +816,7 @@ extern "C" int dli_sm100_tp_exchange_create(void* comm, int device, std::int64_t
   if (cudaMalloc(&ex->local, bytes) != cudaSuccess || cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&handles_dev, sizeof(cudaIpcMemHandle_t) * tp) != cudaSuccess) {
     rc = -3;
-  } else if (dli_sm100_tp_exchange_reset(ex->local, max_rows, s) != DLI_OK ||
+  } else if (dli_sm100_tp_exchange_reset(ex->local, bytes, s) != DLI_OK ||
              cudaIpcGetMemHandle(&handles[rank], ex->local) != cudaSuccess ||
              cudaMemcpyAsync(static_cast<char*>(handles_dev) + rank * sizeof(cudaIpcMemHandle_t), &handles[rank],
                              sizeof(cudaIpcMemHandle_t), cudaMemcpyHostToDevice, s) != cudaSuccess) {
@@ -829,7 +829,7 @@ extern "C" int dli_sm100_tp_exchange_create(void* comm, int device, std::int64_t
              cudaStreamSynchronize(s) != cudaSuccess) {
     rc = -3;
   }
-  // After the all-gather completed here, every rank's header reset (ordered
+  // After the all-gather completed here, every rank's buffer reset (ordered
   // before its all-gather on its stream) has completed too.
   for (int i = 0; rc == 0 && i < tp; ++i) {
     if (i == rank) {

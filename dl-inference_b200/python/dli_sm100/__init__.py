@@ -68,7 +68,7 @@ SIGNATURES = {
     "dli_sm100_select_token": (N, [P, P, I, I, I, I, D, P]),
     "dli_sm100_cast": (N, [P, D, P, D, I, P]),
     "dli_sm100_tp_exchange_bytes": (Z, [D, I, I, D]),
-    "dli_sm100_tp_exchange_reset": (N, [P, I, P]),
+    "dli_sm100_tp_exchange_reset": (N, [P, Z, P]),
     "dli_sm100_allreduce_add_rms_norm": (N, [P, D, D, D, I, I, P, P, P, P, P, I, I, I, F, I, D, P]),
 }
 
@@ -220,7 +220,7 @@ class ExchangeGroup:
         self.buffers = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in range(tp)]
         self.tp, self.max_rows, self.row_elems, self.dtype = tp, max_rows, row_elems, dtype
         for b in self.buffers:
-            check(lib().dli_sm100_tp_exchange_reset(_ptr(b), max_rows, _stream()), "tp_exchange_reset")
+            check(lib().dli_sm100_tp_exchange_reset(_ptr(b), nbytes, _stream()), "tp_exchange_reset")
         self._ptrs = (ctypes.c_void_p * tp)(*[b.data_ptr() for b in self.buffers])
 
     def allreduce_add_rms_norm(self, residual, delta, w, eps=1e-6, timeout_ns=0, ranks=None):

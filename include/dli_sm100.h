@@ -260,19 +260,22 @@ dli_status dli_sm100_cast(const void* x, dli_dtype x_dtype, void* out, dli_dtype
  * Each rank of a tensor-parallel group owns one exchange buffer of
  * dli_sm100_tp_exchange_bytes(tp, max_rows, row_elems, dtype) bytes, 256-byte
  * aligned, mapped into every other rank's process (CUDA IPC). Before first use
- * every rank zeroes its buffer's header with dli_sm100_tp_exchange_reset and
- * the group synchronises on the host; afterwards the buffers are never reset
- * (epochs advance on the device, so CUDA-graph replays need no host work).
- * Returns 0 for unsupported arguments (tp outside 1..8). */
+ * every rank zeroes its whole buffer with dli_sm100_tp_exchange_reset and the
+ * group synchronises; afterwards the buffers are never reset (epochs advance on
+ * the device, so CUDA-graph replays need no host work). A buffer whose call
+ * timed out is out of step with its peers: reset the group before reusing it.
+ * dli_sm100_tp_exchange_bytes returns 0 for unsupported arguments (tp outside
+ * 1..8). */
 size_t dli_sm100_tp_exchange_bytes(int tp, int64_t max_rows, int64_t row_elems, dli_dtype dtype);
-dli_status dli_sm100_tp_exchange_reset(void* buffer, int64_t max_rows, void* stream);
+dli_status dli_sm100_tp_exchange_reset(void* buffer, size_t bytes, void* stream);
 
 /* All-reduce of `delta` over the group fused with add_rms_norm:
  * residual_out = residual + sum_ranks(delta) (the sum rounded to dtype, as an
  * all_reduce returns it); normed = rms_norm(residual_out, w) exactly as
  * dli_sm100_add_rms_norm. One CTA per row pushes its row of delta into every
- * peer's buffer over NVLink and waits (bounded by timeout_ns, 0 = 2 s) for the
- * peers' rows; the sum runs in rank order, so every rank gets identical bits.
+ * peer's buffer over NVLink as 8-byte words carrying the call's epoch, and
+ * polls its own buffer (bounded by timeout_ns, 0 = 2 s) for the peers' words of
+ * that epoch; the sum runs in rank order, so every rank gets identical bits.
  * A wait that runs out sets the device error word (dli_sm100_check_device_error)
  * instead of hanging. Every rank of the group must make the same calls with
  * the same rows, in the same order.
