@@ -22,6 +22,11 @@ struct GemmPlan {
   size_t workspace = 0;   // bytes of split-K scratch (partials + tile counters)
 };
 
+// Occupancy of the tcgen05 GEMM with tile width bn and `stages` pipeline stages:
+// CTAs per SM for cluster <= 1, else resident clusters of `cluster` CTAs
+// (cached per device; 0 when no device answers).
+int gemm_occupancy(int bn, int stages, int cluster);
+
 // Plans a TN GEMM with rows_a x K and rows_b x K operands.
 GemmPlan plan_tn_gemm(int64_t rows_a, int64_t rows_b, int64_t k, dli_dtype dtype, bool allow_split);
 

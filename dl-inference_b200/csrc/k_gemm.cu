@@ -11,9 +11,9 @@
 //              lane quarter, bias add, convert, store.
 // Decode-sized problems (few activation rows) run swap-AB: A = weights (rows N
 // fill the 128-row MMA), B = activations (BN = rows rounded up to 16), so the
-// weight matrix streams through HBM exactly once; tiles with too little K-work
-// per SM are split along K, each split writing an fp32 partial tile to the
-// workspace and the last-arriving CTA of a tile (atomic ticket) reducing them.
+// weight matrix streams through HBM exactly once; when the tiles cannot fill the
+// GPU, K is split over a thread-block cluster of S CTAs per tile, whose fp32
+// partial tiles are reduced through distributed shared memory in rank order.
 // Prefill-sized problems run A = activations, B = weights with BN = 128/256 and
 // grouped tile rasterisation for L2 reuse.
 //
@@ -21,7 +21,9 @@
 // python/dli_ops/aot/linear/kernel.py:24-38, runs fp32 tl.dot as TF32; the
 // accuracy target here is fp32), and for shapes TMA cannot address.
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <type_traits>
 
 #include "gemm.cuh"
@@ -268,12 +270,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // keeps every CTA's shared memory alive until all ranks finished reading.
     cluster_sync();
     const int S = p.splits;
-    const int R = kBM / S;
+    const int R = (kBM + S - 1) / S;  // rows reduced by each rank (the last may get fewer)
     const int quads = R * (BN / 4);
     const uint32_t red_local = smem_u32(smem);
     for (int q = threadIdx.x; q < quads; q += kGemmThreads) {
       const int rr = split * R + q % R;  // consecutive threads: consecutive rows
       const int cq = (q / R) * 4;
+      if (rr >= kBM) continue;
       const uint32_t off = static_cast<uint32_t>((rr * (BN + 4) + cq) * 4);
       float v[4] = {0.f, 0.f, 0.f, 0.f};
       for (int s = 0; s < S; ++s) {
@@ -388,16 +391,20 @@ dli_status make_kmajor_map(CUtensorMap* map, const void* base, int64_t rows, int
   return DLI_OK;
 }
 
-// Pipeline depth per tile width. Narrow (decode, swap-AB) tiles keep two CTAs
-// resident per SM (<= ~113 KB shared memory each) so one CTA's prologue and
-// split-K epilogue overlap the other's weight streaming.
-int stages_for(int bn) { return bn >= 256 ? 4 : (bn >= 128 ? 6 : (bn >= 64 ? 4 : 5)); }
-// DLI_SM100_GEMM_NARROW_DEEP=1 selects one CTA per SM with 8 stages instead.
-bool narrow_deep() {
-  static const bool deep = tuning_knob("GEMM_NARROW_DEEP", 0) != 0;
+// Pipeline depth per tile width. Narrow (decode, swap-AB) tiles use ~100 KB of
+// shared memory so two CTAs share an SM: one CTA's prologue and split-K
+// epilogue overlap the other's weight streaming. Wide tiles fill ~200 KB.
+// DLI_SM100_GEMM_DEEP=1 gives narrow tiles one ~200 KB CTA per SM instead.
+bool gemm_deep() {
+  static const bool deep = tuning_knob("GEMM_DEEP", 0) != 0;
   return deep;
 }
-int ctas_per_sm(int bn) { return bn <= 64 && !narrow_deep() ? 2 : 1; }
+int stages_for(int bn) {
+  if (bn >= 256) return 4;
+  if (bn >= 128) return 6;
+  if (bn >= 64) return gemm_deep() ? 8 : 4;
+  return gemm_deep() ? 10 : 5;
+}
 
 template <typename T, int BN, int STAGES>
 dli_status launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p, int splits,
@@ -416,8 +423,8 @@ template <typename T>
 dli_status launch_tc_bn(int bn, int stages, const CUtensorMap& ma, const CUtensorMap& mb,
                         const TcParams& p, int splits, cudaStream_t stream) {
   switch (bn) {
-    case 32: return stages == 8 ? launch_tc<T, 32, 8>(ma, mb, p, splits, stream)
-                                : launch_tc<T, 32, 5>(ma, mb, p, splits, stream);
+    case 32: return stages == 10 ? launch_tc<T, 32, 10>(ma, mb, p, splits, stream)
+                                 : launch_tc<T, 32, 5>(ma, mb, p, splits, stream);
     case 64: return stages == 8 ? launch_tc<T, 64, 8>(ma, mb, p, splits, stream)
                                 : launch_tc<T, 64, 4>(ma, mb, p, splits, stream);
     case 128: return launch_tc<T, 128, 6>(ma, mb, p, splits, stream);
@@ -426,7 +433,85 @@ dli_status launch_tc_bn(int bn, int stages, const CUtensorMap& ma, const CUtenso
   return fail(DLI_ERR_UNSUPPORTED, "gemm: unsupported tile width");
 }
 
+// Occupancy of one kernel configuration: CTAs per SM (cluster == 1) or
+// resident clusters of `cluster` CTAs (clusters are placed within a GPC, so
+// the latter is below sm_count * CTAs-per-SM / cluster for clusters above 2).
+// The calculator reports one CTA per SM for any kernel that allocates tensor
+// memory, while the hardware co-schedules as many as shared memory, registers
+// and the 512 TMEM columns allow (two 101 KB GEMM CTAs of 32-256 columns run
+// side by side on B200). The query therefore runs on a proxy kernel with this
+// configuration's block size and shared memory and no TMEM use; registers
+// (<= 96 per thread here) never bind before shared memory does.
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_occupancy_proxy(int* sink) {
+  extern __shared__ int proxy_smem[];
+  if (sink != nullptr) sink[threadIdx.x] = proxy_smem[threadIdx.x];
+}
+
+int query_occupancy(int smem_bytes, int cluster) {
+  // the proxy serves every configuration: set its limit to this one's size
+  if (cudaFuncSetAttribute(gemm_occupancy_proxy, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  int n = 0;
+  if (cluster <= 1) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemm_occupancy_proxy, kGemmThreads, smem_bytes) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    return n;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, static_cast<unsigned>(cluster), 1);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes);
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 1;
+  attr.val.clusterDim.y = static_cast<unsigned>(cluster);
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_occupancy_proxy, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+int layout_bytes(int bn, int stages) {
+  switch (bn * 100 + stages) {
+    case 3205: return TcLayout<32, 5>::kBytes;
+    case 3210: return TcLayout<32, 10>::kBytes;
+    case 6404: return TcLayout<64, 4>::kBytes;
+    case 6408: return TcLayout<64, 8>::kBytes;
+    case 12806: return TcLayout<128, 6>::kBytes;
+    case 25604: return TcLayout<256, 4>::kBytes;
+    default: return 0;
+  }
+}
+
 }  // namespace
+
+int gemm_occupancy(int bn, int stages, int cluster) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  const auto key = std::make_tuple(dev, bn, stages, cluster);
+  std::lock_guard<std::mutex> lock(mu);  // also serialises the proxy's attribute changes
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  const int bytes = layout_bytes(bn, stages);
+  const int n = bytes > 0 ? query_occupancy(bytes, cluster) : 0;
+  cache[key] = n;
+  return n;
+}
 
 GemmPlan plan_tn_gemm(int64_t rows_a, int64_t rows_b, int64_t k, dli_dtype dtype, bool allow_split) {
   GemmPlan plan;
@@ -445,21 +530,22 @@ GemmPlan plan_tn_gemm(int64_t rows_a, int64_t rows_b, int64_t k, dli_dtype dtype
   plan.kblocks = static_cast<int>(ceil_div(k, kBK));
   plan.splits = 1;
   const int64_t tiles = static_cast<int64_t>(plan.tiles_i) * plan.tiles_j;
-  if (plan.bn <= 64 && narrow_deep()) plan.stages = 8;
-  static const int kSplitSlots = tuning_knob("GEMM_SPLIT_SLOTS", 0);  // CTAs per SM to fill
-  const int per_sm = plan.stages == 8 ? 1 : ctas_per_sm(plan.bn);
-  const int slots = sm_count() * (kSplitSlots > 0 ? kSplitSlots : per_sm);
+  const int slots = sm_count() * std::max(1, gemm_occupancy(plan.bn, plan.stages, 1));
   // When the tiles alone cannot fill the SMs, split K over a thread-block cluster
-  // of S in {8, 4, 2} CTAs per tile (reduced through distributed shared memory,
-  // so splits cost no global traffic); each split keeps >= 2 K blocks.
-  if (allow_split && tiles < slots) {
-    for (const int s : {8, 4, 2}) {
-      if (tiles * s <= slots && plan.kblocks >= 2 * s) {
+  // of S <= 8 CTAs per tile (reduced through distributed shared memory, so splits
+  // cost no global traffic): the largest S whose clusters all fit on the GPU at
+  // once, each split keeping >= 3 K blocks.
+  static const int kForceSplits = tuning_knob("GEMM_SPLITS", 0);  // fixed S (launch-shape sweeps)
+  if (allow_split && tiles < slots && kForceSplits > 0) {
+    plan.splits = std::max(1, std::min({kForceSplits, 8, plan.kblocks / 2}));
+  } else if (allow_split && tiles < slots) {
+    for (int s = 8; s >= 2; --s) {
+      if (plan.kblocks < 3 * s || tiles * s > slots) continue;
+      if (tiles <= gemm_occupancy(plan.bn, plan.stages, s)) {
         plan.splits = s;
         break;
       }
     }
-    if (plan.splits == 1 && plan.kblocks >= 4) plan.splits = 2;
   }
   plan.workspace = 0;
   return plan;

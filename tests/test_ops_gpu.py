@@ -84,6 +84,10 @@ LINEAR_SHAPES = [  # (M, N, K)
     (1, 896, 896), (8, 1152, 896), (8, 9728, 896), (8, 896, 4864), (32, 4608, 3584),
     (32, 3584, 18944), (64, 3696, 8192), (100, 200, 96), (128, 896, 896), (129, 1152, 896),
     (512, 4864, 896), (2048, 3584, 3584), (300, 37888 // 8, 3584), (7, 152064 // 16, 896),
+    # tensor-parallel decode shards (7B at TP 2/4, 72B at TP 8): few tiles, so K is split
+    # over clusters of 2..8 CTAs, including sizes that do not divide the 128-row tile
+    (32, 3584, 3584), (32, 2304, 3584), (32, 3584, 1792), (32, 9472, 3584), (32, 3584, 896),
+    (32, 1152, 3584), (16, 3584, 4736), (64, 1280, 8192), (64, 8192, 1024), (32, 640, 3584),
 ]
 
 
