@@ -10,6 +10,10 @@ enum GemmEpilogue : int {
   kEpiRowMajor = 0,   // out[i * ldo + j], bias[j]           (A = activations, B = weights)
   kEpiTransposed = 1, // out[j * ldo + i], bias[i]           (swap-AB: A = weights, B = activations)
   kEpiNchw = 2,       // i = img * ohw + pix, j = channel -> out[(img * OC + j) * ohw + pix], bias[j]
+  // SwiGLU over weights in 64-row gate/up blocks (rows 128b..128b+63 = gate rows
+  // 64b.., rows 128b+64.. = the matching up rows): out = silu(gate) * up, I cols
+  kEpiGluT = 3,       // swap-AB: D row i = weight row -> out[j * ldo + (i/128)*64 + i%64]
+  kEpiGlu = 4,        // D column j = weight row -> out[i * ldo + (j/128)*64 + j%64]
 };
 
 struct GemmPlan {
@@ -41,7 +45,7 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
                                int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,
                                dli_dtype dtype, const GemmPlan& plan, void* workspace,
                                size_t workspace_bytes, cudaStream_t stream, bool const_a,
-                               bool const_b);
+                               bool const_b, int64_t glu_cols = 0);
 
 // SIMT fallback (any float dtype, any alignment): out[M,N] = A[M,K] . B + bias,
 // with B given as [N,K] (b_kmajor) or [K,N].

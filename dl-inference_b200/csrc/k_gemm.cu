@@ -59,6 +59,7 @@ struct TcParams {
   int out_vec;  // output base is 16-byte aligned
   int const_a;  // operand A is read-only weights: its first tiles load before pdl_wait
   int const_b;  // same for operand B
+  int glu_cols; // SwiGLU epilogues: valid output columns (the intermediate size)
   const void* bias;
   void* out;
   unsigned* err;
@@ -114,6 +115,27 @@ __device__ __forceinline__ void store_vals(const TcParams& p, int64_t gi, int jc
     }
   }
 }
+
+// SwiGLU of one gate/up accumulator pair, rounded like the unfused graph
+// (linear output in T, silu output in T, product in T).
+template <typename T>
+__device__ __forceinline__ T glu_val(float g, float u) {
+  const float gt = round_through<T>(g), ut = round_through<T>(u);
+  const float sg = round_through<T>(gt / (1.0f + expf(-gt)));
+  return from_f32<T>(sg * ut);
+}
+
+// kEpiGluT: n (<= 32) consecutive tokens j0.. of gate row `grow` (0..63) of tile ti.
+template <typename T>
+__device__ __forceinline__ void store_glu_t(const TcParams& p, int ti, int grow, int j0, const float* g,
+                                            const float* u, int n) {
+  const int64_t col = static_cast<int64_t>(ti) * 64 + grow;
+  if (col >= p.glu_cols) return;
+  T* out = static_cast<T*>(p.out);
+  for (int k = 0; k < n && j0 + k < p.rows_b; ++k) out[static_cast<int64_t>(j0 + k) * p.ldo + col] = glu_val<T>(g[k], u[k]);
+}
+
+__device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 template <typename T, int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -231,8 +253,62 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       flags[0] = 1;
     }
     tc_fence_after();
+    epilogue_bar();  // every epilogue warp sees the same abort flag
     const bool aborted = flags[0] != 0;
-    if (!aborted && p.splits == 1) {
+    if (!aborted && p.splits == 1 && p.epilogue == kEpiGluT) {
+      // gate rows live in TMEM lanes 0-63 (quarters 0, 1), up rows in lanes 64-127:
+      // the up quarters pass their values through shared memory (the idle ring)
+      float* xch = reinterpret_cast<float*>(smem);  // [64][33]
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c, r);
+        tmem_ld_wait();
+        if (quarter >= 2) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) xch[(row - 64) * 33 + k] = __uint_as_float(r[k]);
+        }
+        epilogue_bar();
+        const int64_t col = static_cast<int64_t>(ti) * 64 + row;
+        if (quarter < 2 && col < p.glu_cols) {
+          T* out = static_cast<T*>(p.out) + col;
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            if (j0 + c + k < p.rows_b)
+              out[static_cast<int64_t>(j0 + c + k) * p.ldo] = glu_val<T>(__uint_as_float(r[k]), xch[row * 33 + k]);
+        }
+        epilogue_bar();
+      }
+    } else if (!aborted && p.splits == 1 && p.epilogue == kEpiGlu) {
+      // this thread's token row; columns hold 64-wide gate/up blocks
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 128) {
+#pragma unroll 1
+        for (int h = 0; h < 64; h += 32) {
+          uint32_t rg[32], ru[32];
+          tmem_ld_32x32b_x32(tbase + c + h, rg);
+          tmem_ld_32x32b_x32(tbase + c + 64 + h, ru);
+          tmem_ld_wait();
+          const int64_t oc = (static_cast<int64_t>(j0) + c) / 2 + h;
+          if (gi < p.rows_a && oc < p.glu_cols) {
+            T* dst = static_cast<T*>(p.out) + gi * p.ldo + oc;
+            if (p.out_vec && (p.ldo % 8) == 0 && oc + 32 <= p.glu_cols) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                Vec16<T> pack;
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  pack.e[e] = glu_val<T>(__uint_as_float(rg[q * 8 + e]), __uint_as_float(ru[q * 8 + e]));
+                store16(dst + q * 8, pack);
+              }
+            } else {
+              for (int k = 0; k < 32 && oc + k < p.glu_cols; ++k)
+                dst[k] = glu_val<T>(__uint_as_float(rg[k]), __uint_as_float(ru[k]));
+            }
+          }
+        }
+      }
+    } else if (!aborted && p.splits == 1) {
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
@@ -270,9 +346,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // keeps every CTA's shared memory alive until all ranks finished reading.
     cluster_sync();
     const int S = p.splits;
-    const int R = (kBM + S - 1) / S;  // rows reduced by each rank (the last may get fewer)
-    const int quads = R * (BN / 4);
     const uint32_t red_local = smem_u32(smem);
+    if (p.epilogue == kEpiGluT) {
+      // each rank reduces gate rows [split*R, ...) of 0..63 and their up rows (+64)
+      const int R = (64 + S - 1) / S;
+      const int quads = R * (BN / 4);
+      for (int q = threadIdx.x; q < quads; q += kGemmThreads) {
+        const int rr = split * R + q % R;
+        const int cq = (q / R) * 4;
+        if (rr >= 64) continue;
+        const uint32_t og = static_cast<uint32_t>((rr * (BN + 4) + cq) * 4);
+        const uint32_t ou = static_cast<uint32_t>(((rr + 64) * (BN + 4) + cq) * 4);
+        float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int s2 = 0; s2 < S; ++s2) {
+          const float4 a = ld_dsmem_f4(mapa_shared(red_local + og, s2));
+          const float4 b = ld_dsmem_f4(mapa_shared(red_local + ou, s2));
+          g[0] += a.x; g[1] += a.y; g[2] += a.z; g[3] += a.w;
+          u[0] += b.x; u[1] += b.y; u[2] += b.z; u[3] += b.w;
+        }
+        if (tj * BN + cq < p.rows_b) store_glu_t<T>(p, ti, rr, tj * BN + cq, g, u, 4);
+      }
+    }
+    const int R = (kBM + S - 1) / S;  // rows reduced by each rank (the last may get fewer)
+    const int quads = p.epilogue == kEpiGluT ? 0 : R * (BN / 4);
     for (int q = threadIdx.x; q < quads; q += kGemmThreads) {
       const int rr = split * R + q % R;  // consecutive threads: consecutive rows
       const int cq = (q / R) * 4;
@@ -556,7 +652,7 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
                                int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,
                                dli_dtype dtype, const GemmPlan& plan, void* workspace,
                                size_t workspace_bytes, cudaStream_t stream, bool const_a,
-                               bool const_b) {
+                               bool const_b, int64_t glu_cols) {
   if (!plan.tcgen05) return fail(DLI_ERR_UNSUPPORTED, "gemm: shape not served by tcgen05");
   if (!aligned(a, 16) || !aligned(b, 16) || lda % 8 != 0 || ldb % 8 != 0)
     return fail(DLI_ERR_UNSUPPORTED, "gemm: TMA needs 16-byte aligned operands and row strides");
@@ -584,6 +680,7 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
   p.err = device_error_word();
   p.const_a = const_a ? 1 : 0;
   p.const_b = const_b ? 1 : 0;
+  p.glu_cols = static_cast<int>(glu_cols);
   if (bf16) return launch_tc_bn<__nv_bfloat16>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
   return launch_tc_bn<__half>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
 }
@@ -640,6 +737,30 @@ extern "C" dli_status dli_sm100_linear(const void* x, const void* w, const void*
                                workspace, workspace_bytes, as_stream(stream), false, true);
   }
   return run_gemm_simt(x, w, bias, y, m, n, k, true, dtype, as_stream(stream));
+}
+
+extern "C" dli_status dli_sm100_linear_silu_mul(const void* x, const void* w_glu, void* y, int64_t m,
+                                                int64_t inter, int64_t k, dli_dtype dtype, void* stream) {
+  const char* name = "linear_silu_mul";
+  if (m < 0 || inter <= 0 || k <= 0) return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": bad sizes");
+  if (dtype != DLI_DTYPE_BF16 && dtype != DLI_DTYPE_F16)
+    return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": bfloat16/float16 only (tcgen05 epilogue)");
+  if (m == 0) return ok();
+  if (!x || !w_glu || !y) return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": null pointer");
+  if (!aligned(x, 16) || !aligned(w_glu, 16) || k % 8 != 0)
+    return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": 16-byte aligned operands and K % 8 == 0 expected");
+  const int64_t rows_w = 2 * ceil_div(inter, 64) * 64;  // gate/up blocks, the last one zero-padded
+  if (m <= kSwapRows) {
+    const GemmPlan plan = plan_tn_gemm(rows_w, m, k, dtype, true);
+    if (!plan.tcgen05) return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": shape not served by tcgen05");
+    return run_tn_gemm_tcgen05(w_glu, x, nullptr, y, rows_w, m, k, k, k, inter, kEpiGluT, 0, dtype, plan, nullptr,
+                               0, as_stream(stream), true, false, inter);
+  }
+  const GemmPlan plan = plan_tn_gemm(m, rows_w, k, dtype, false);
+  if (!plan.tcgen05 || plan.bn % 128 != 0)
+    return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": shape not served by tcgen05");
+  return run_tn_gemm_tcgen05(x, w_glu, nullptr, y, m, rows_w, k, k, k, inter, kEpiGlu, 0, dtype, plan, nullptr, 0,
+                             as_stream(stream), false, true, inter);
 }
 
 extern "C" dli_status dli_sm100_matmul(const void* a, const void* b, void* out, int64_t m, int64_t n,

@@ -7,7 +7,7 @@
 // add, mul, silu, relu, softmax, max_pool2d, batch_norm2d, reshape, transpose)
 // plus additive fused operators for the batched Qwen2 graphs (add_rms_norm,
 // silu_mul, qkv_rotary_cache, attention_kvcache, last_token, argmax, cast,
-// all_reduce, all_reduce_add_rms_norm).
+// all_reduce, all_reduce_add_rms_norm, linear_silu_mul).
 //
 // Every operator validates arity/dtype/shape on the host and throws
 // std::invalid_argument like the reference templates
@@ -474,6 +474,33 @@ int64_t requireIntAttr(const Attributes& attrs, const std::string& name, const s
   return attrs.require<std::int64_t>(name);
 }
 
+// linear_silu_mul: (x [.., K], w_glu [2*ceil(I/64)*64, K]) -> silu(x.Wg^T) * (x.Wu^T) [.., I],
+// attr `intermediate` = I; w_glu holds gate/up rows in 64-row blocks. One
+// tcgen05 GEMM with a SwiGLU epilogue (bfloat16/float16).
+class LinearSiluMulOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "linear_silu_mul"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 2, 2, 1, type());
+    floatInputs(in, 2, type());
+    const Tensor& x = *in[0];
+    const Tensor& w = *in[1];
+    const std::int64_t inter = requireIntAttr(attrs, "intermediate", type());
+    if (w.rank() != 2 || inter <= 0) throw std::invalid_argument("linear_silu_mul: bad weight or intermediate");
+    const std::int64_t k = x.shape().back();
+    if (w.dim(1) != k || w.dim(0) != 2 * ((inter + 63) / 64) * 64)
+      throw std::invalid_argument("linear_silu_mul weight shape " + dli::formatShape(w.shape()) +
+                                  " does not match the 64-row gate/up blocks of intermediate " + std::to_string(inter));
+    const std::int64_t m = dli::product(x.shape(), 0, x.rank() - 1);
+    auto shape = x.shape();
+    shape.back() = inter;
+    *out[0] = Tensor::cuda(x.dtype(), shape, x.deviceId());
+    check(dli_sm100_linear_silu_mul(dli::ptr(x), dli::ptr(w), out[0]->deviceData(), m, inter, k, cdt(x.dtype()),
+                                    ctx.cuda_stream),
+          type());
+  }
+};
+
 // qkv_rotary_cache: (qkv [B,S,(Hq+2Hkv)D], cos, sin, positions[B] int64) -> q [B,S,Hq,D].
 // Rotated k and raw v go to rows positions[b]+s of the kv_cache entry (reserved
 // with `capacity` rows on first use).
@@ -727,6 +754,7 @@ extern "C" bool dli_register_operators(dli::OperatorRegistry* registry) {
   reg<TransposeOp>(registry, "transpose");
   reg<AddRmsNormOp>(registry, "add_rms_norm");
   reg<SiluMulOp>(registry, "silu_mul");
+  reg<LinearSiluMulOp>(registry, "linear_silu_mul");
   reg<QkvRotaryCacheOp>(registry, "qkv_rotary_cache");
   reg<AttentionKvCacheOp>(registry, "attention_kvcache");
   reg<LastTokenOp>(registry, "last_token");

@@ -101,13 +101,39 @@ def _permute_heads(t: torch.Tensor, heads: int, head_dim: int) -> torch.Tensor:
     return x.index_select(1, perm).reshape(shp)
 
 
+GLU_BLOCK = 64
+
+
+def glu_blocked(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """[I, K] gate and up weights -> the layout of the fused `linear_silu_mul`
+    operator: 64-row blocks, rows [128b, 128b+64) = gate rows [64b, 64b+64) and
+    rows [128b+64, 128b+128) = the matching up rows; rows past I are zero. One
+    128-row tensor-core tile then holds matching gate and up rows."""
+    inter, k = w_gate.shape
+    blocks = (inter + GLU_BLOCK - 1) // GLU_BLOCK
+    g = torch.zeros(blocks * GLU_BLOCK, k, dtype=w_gate.dtype, device=w_gate.device)
+    u = torch.zeros_like(g)
+    g[:inter], u[:inter] = w_gate, w_up
+    return torch.stack([g.view(blocks, GLU_BLOCK, k), u.view(blocks, GLU_BLOCK, k)], 1) \
+        .reshape(2 * blocks * GLU_BLOCK, k).contiguous()
+
+
+def glu_unblocked(w_glu: torch.Tensor, inter: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Inverse of glu_blocked: (gate [I, K], up [I, K])."""
+    k = w_glu.shape[-1]
+    b = w_glu.reshape(-1, 2, GLU_BLOCK, k)
+    return b[:, 0].reshape(-1, k)[:inter], b[:, 1].reshape(-1, k)[:inter]
+
+
 def transform_weights(state: dict[str, torch.Tensor], shape: Qwen2Shape, tp_size: int = 1,
                       tp_rank: int = 0, dtype: torch.dtype | None = None,
-                      layers: range | None = None) -> dict[str, torch.Tensor]:
+                      layers: range | None = None, fused_glu: bool = True) -> dict[str, torch.Tensor]:
     """HF-named Qwen2 state dict -> plugin weights for one tensor-parallel rank.
 
     Output names: embed, layers.{i}.{ln_in,wqkv,bqkv,wo,ln_post,wgu,wd}, norm,
-    lm_head. Tensors are contiguous and cast to `dtype` when given.
+    lm_head. Tensors are contiguous and cast to `dtype` when given. `wgu` is
+    [gate; up] for the linear + silu_mul graph, or the glu_blocked() layout of
+    the fused linear_silu_mul operator when `fused_glu`.
     """
     hq, hkv, d, inter = shape.q_heads, shape.kv_heads, shape.head_dim, shape.intermediate
     if hq % tp_size or hkv % tp_size or inter % tp_size:
@@ -133,8 +159,8 @@ def transform_weights(state: dict[str, torch.Tensor], shape: Qwen2Shape, tp_size
         out[f"layers.{i}.bqkv"] = cast(torch.cat([q_b[qs], k_b[ks], v_b[ks]], 0))
         out[f"layers.{i}.wo"] = cast(state[p + "self_attn.o_proj.weight"][:, qs])
         isl = slice(tp_rank * ish, (tp_rank + 1) * ish)
-        out[f"layers.{i}.wgu"] = cast(torch.cat([state[p + "mlp.gate_proj.weight"][isl],
-                                                 state[p + "mlp.up_proj.weight"][isl]], 0))
+        gate, up = state[p + "mlp.gate_proj.weight"][isl], state[p + "mlp.up_proj.weight"][isl]
+        out[f"layers.{i}.wgu"] = cast(glu_blocked(gate, up) if fused_glu else torch.cat([gate, up], 0))
         out[f"layers.{i}.wd"] = cast(state[p + "mlp.down_proj.weight"][:, isl])
         out[f"layers.{i}.ln_in"] = cast(state[p + "input_layernorm.weight"])
         out[f"layers.{i}.ln_post"] = cast(state[p + "post_attention_layernorm.weight"])
@@ -146,9 +172,11 @@ def transform_weights(state: dict[str, torch.Tensor], shape: Qwen2Shape, tp_size
 
 
 def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: str = "qwen2",
-                weights_file: str = "", with_argmax: bool = True) -> dict[str, Any]:
+                weights_file: str = "", with_argmax: bool = True, fused_glu: bool = True) -> dict[str, Any]:
     """dli.graph.v1 dict for one rank. Inputs: input_ids [B,S] int64, positions [B]
-    int64, rotary_cos/rotary_sin, and the weights of transform_weights()."""
+    int64, rotary_cos/rotary_sin, and the weights of transform_weights() (made
+    with the same `fused_glu`: one linear_silu_mul node instead of linear +
+    silu_mul; the fused operator serves bfloat16/float16)."""
     hq, hkv, d = shape.q_heads // tp_size, shape.kv_heads // tp_size, shape.head_dim
     nodes: list[dict[str, Any]] = []
 
@@ -180,8 +208,12 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
         node(f"{L}.post_attention_layernorm", add_norm, [resid, f"{L}.o_part", f"{L}.ln_post"],
              [f"{L}.x2", f"{L}.h_mid"], {"eps": eps})
         resid = f"{L}.h_mid"
-        node(f"{L}.gate_up_proj", "linear", [f"{L}.x2", f"{L}.wgu"], [f"{L}.gu"])
-        node(f"{L}.act", "silu_mul", [f"{L}.gu"], [f"{L}.act"])
+        if fused_glu:
+            node(f"{L}.gate_up_proj", "linear_silu_mul", [f"{L}.x2", f"{L}.wgu"], [f"{L}.act"],
+                 {"intermediate": shape.intermediate // tp_size})
+        else:
+            node(f"{L}.gate_up_proj", "linear", [f"{L}.x2", f"{L}.wgu"], [f"{L}.gu"])
+            node(f"{L}.act", "silu_mul", [f"{L}.gu"], [f"{L}.act"])
         node(f"{L}.down_proj", "linear", [f"{L}.act", f"{L}.wd"], [f"{L}.d_part"])
         delta = f"{L}.d_part"
     node("norm", add_norm, [resid, delta, "norm"], ["normed", "h_out"], {"eps": eps})
@@ -267,11 +299,12 @@ def export_qwen2(model_or_state: Any, out_dir: str | Path, stem: str = "qwen2",
         state = model_or_state
     if shape is None:
         raise ValueError("shape is required with a state dict")
-    weights = transform_weights(state, shape, tp_size, tp_rank, dtype)
+    fused = dtype in (torch.bfloat16, torch.float16)  # the fused SwiGLU GEMM is 16-bit only
+    weights = transform_weights(state, shape, tp_size, tp_rank, dtype, fused_glu=fused)
     cos, sin = rotary_tables(shape, capacity)
     weights["rotary_cos"], weights["rotary_sin"] = cos, sin
     wpath = write_weights(weights, out, stem)
-    graph = build_graph(shape, capacity, tp_size, weights_file=wpath.name)
+    graph = build_graph(shape, capacity, tp_size, weights_file=wpath.name, fused_glu=fused)
     gpath = out / f"{stem}.dli.json"
     gpath.write_text(json.dumps(graph, indent=1), encoding="utf-8")
     meta = {"shape": asdict(shape), "capacity": capacity, "tp_size": tp_size, "tp_rank": tp_rank}

@@ -41,6 +41,7 @@ SIGNATURES = {
     "dli_sm100_linear_workspace_size": (Z, [I, I, I, D]),
     "dli_sm100_linear": (N, [P, P, P, P, I, I, I, D, P, Z, P]),
     "dli_sm100_matmul": (N, [P, P, P, I, I, I, D, P]),
+    "dli_sm100_linear_silu_mul": (N, [P, P, P, I, I, I, D, P]),
     "dli_sm100_conv2d_workspace_size": (Z, [I] * 11 + [D]),
     "dli_sm100_conv2d": (N, [P, P, P, P] + [I] * 11 + [D, P, Z, P]),
     "dli_sm100_rms_norm": (N, [P, P, P, I, I, F, D, P]),
@@ -156,6 +157,18 @@ def linear(x, w, bias=None, out=None):
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
     check(L.dli_sm100_linear(_ptr(x), _ptr(w), _ptr(bias), _ptr(out), m, n, k, _dt(x), _ptr(ws),
                              ws_bytes, _stream()), "linear")
+    return out
+
+
+def linear_silu_mul(x, w_glu, inter):
+    """silu(x @ Wg^T) * (x @ Wu^T); w_glu in the 64-row gate/up block layout
+    (dli_export.qwen2.glu_blocked)."""
+    _contig(x, w_glu)
+    k = x.shape[-1]
+    m = x.numel() // k
+    out = torch.empty(*x.shape[:-1], inter, dtype=x.dtype, device=x.device)
+    check(lib().dli_sm100_linear_silu_mul(_ptr(x), _ptr(w_glu), _ptr(out), m, inter, k, _dt(x), _stream()),
+          "linear_silu_mul")
     return out
 
 

@@ -78,6 +78,18 @@ dli_status dli_sm100_linear(const void* x, const void* w, const void* bias, void
                             int64_t n, int64_t k, dli_dtype dtype, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* Fused gate/up projection + SwiGLU (additive; the reference graph runs
+ * linear -> silu -> mul): y[M, inter] = silu(x · Wg^T) * (x · Wu^T), rounded like
+ * the unfused nodes (each linear output, the silu output and the product in
+ * dtype). w_glu holds Wg and Wu interleaved in 64-row blocks: rows
+ * [128b, 128b+64) are gate rows [64b, 64b+64) and rows [128b+64, 128b+128) the
+ * matching up rows, 2*ceil(inter/64)*64 rows of K in all, the rows past `inter`
+ * zero. BF16/F16 only (DLI_ERR_UNSUPPORTED otherwise): one tcgen05 GEMM whose
+ * epilogue pairs the gate and up accumulators, so the [M, 2*inter] gate/up
+ * tensor is never written. */
+dli_status dli_sm100_linear_silu_mul(const void* x, const void* w_glu, void* y, int64_t m, int64_t inter,
+                                     int64_t k, dli_dtype dtype, void* stream);
+
 /* matmul: out[M,N] = a[M,K] · b[K,N] (both row-major, 2-D).
  * Replaces python/dli_ops/aot/matmul/kernel.py:5-40, template.cc:14-30. */
 dli_status dli_sm100_matmul(const void* a, const void* b, void* out, int64_t m, int64_t n,

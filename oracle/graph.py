@@ -44,6 +44,13 @@ class GraphOracle:
             return [n, r]
         if op == "linear":
             return [O.linear(x[0], x[1], x[2] if len(x) > 2 else None)]
+        if op == "linear_silu_mul":
+            # weights in 64-row gate/up blocks (dli_export.qwen2.glu_blocked)
+            w = np.asarray(x[1], dtype=np.float64)
+            inter, k = int(a["intermediate"]), w.shape[-1]
+            b = w.reshape(-1, 2, 64, k)
+            gate, up = b[:, 0].reshape(-1, k)[:inter], b[:, 1].reshape(-1, k)[:inter]
+            return [O.silu_mul(np.concatenate([O.linear(x[0], gate), O.linear(x[0], up)], -1))]
         if op == "silu_mul":
             return [O.silu_mul(x[0])]
         if op == "last_token":

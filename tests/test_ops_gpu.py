@@ -91,6 +91,38 @@ LINEAR_SHAPES = [  # (M, N, K)
 ]
 
 
+GLU_SHAPES = [  # (M, intermediate, K): decode (swap-AB, split-K clusters) and prefill tiles
+    (1, 4864, 896), (8, 4864, 896), (32, 18944, 3584), (32, 9472, 3584), (32, 4736, 3584),
+    (64, 3696, 8192), (128, 100, 64), (7, 96, 64), (129, 4864, 896), (512, 2368, 896), (2048, 1000, 512),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("m,inter,k", GLU_SHAPES)
+def test_linear_silu_mul_matches_unfused(m, inter, k, dtype):
+    """The fused gate/up GEMM + SwiGLU epilogue against linear -> silu_mul through
+    the library (same rounding points; the fp32 accumulation order may differ
+    with the split-K plan, so a bf16 tolerance plus >= 99% identical elements) and
+    against an fp32 reference."""
+    import dli_sm100 as C
+    from dli_export.qwen2 import glu_blocked
+
+    g = torch.Generator(device="cuda").manual_seed(m + inter + k)
+    x = torch.randn(m, k, device="cuda", generator=g).to(dtype)
+    wg = (torch.randn(inter, k, device="cuda", generator=g) * 0.03).to(dtype)
+    wu = (torch.randn(inter, k, device="cuda", generator=g) * 0.03).to(dtype)
+    y = C.linear_silu_mul(x, glu_blocked(wg, wu), inter)
+    y2 = C.linear_silu_mul(x, glu_blocked(wg, wu), inter)
+    C.check_device_error()
+    unfused = C.silu_mul(C.linear(x, torch.cat([wg, wu])))
+    assert torch.equal(y, y2)
+    same = (y == unfused).float().mean().item()
+    assert same >= 0.99, same
+    gate, up = x.float() @ wg.float().T, x.float() @ wu.float().T
+    ref = torch.nn.functional.silu(gate) * up
+    assert_close(y.float(), ref, dtype, f"linear_silu_mul {m}x{inter}x{k}")
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
 @pytest.mark.parametrize("m,n,k", LINEAR_SHAPES)
 def test_linear_tcgen05_model_shapes(m, n, k, dtype):

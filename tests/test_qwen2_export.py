@@ -8,7 +8,7 @@ import json
 import numpy as np
 import torch
 
-from dli_export.qwen2 import (Qwen2Shape, build_graph, export_qwen2, interleave_permutation,
+from dli_export.qwen2 import (Qwen2Shape, build_graph, export_qwen2, glu_unblocked, interleave_permutation,
                               random_state, rotary_tables, transform_weights)
 from oracle import ops as O
 
@@ -43,7 +43,7 @@ def test_interleaved_rotary_on_permuted_rows_equals_rotate_half():
 
 
 def test_graph_structure_per_layer():
-    g = build_graph(TINY, capacity=64, tp_size=1)
+    g = build_graph(TINY, capacity=64, tp_size=1, fused_glu=False)
     ops = [n["op"] for n in g["nodes"]]
     assert ops[0] == "embedding"
     layer0 = ["rms_norm", "linear", "qkv_rotary_cache", "attention_kvcache", "linear", "add_rms_norm",
@@ -52,6 +52,11 @@ def test_graph_structure_per_layer():
     assert ops[1:1 + 9] == layer0
     assert ops[10:19] == layer1
     assert ops[19:] == ["add_rms_norm", "last_token", "linear", "argmax"]
+    # fused SwiGLU: gate/up projection + silu_mul become one node
+    gf = build_graph(TINY, capacity=64, tp_size=1)
+    fused = [n for n in gf["nodes"] if n["op"] == "linear_silu_mul"]
+    assert len(fused) == TINY.layers and "silu_mul" not in [n["op"] for n in gf["nodes"]]
+    assert fused[0]["attrs"]["intermediate"] == TINY.intermediate
     assert g["inputs"] == ["input_ids", "positions"] and g["outputs"] == ["logits", "next_ids"]
     g2 = build_graph(TINY, capacity=64, tp_size=2)
     ops2 = [n["op"] for n in g2["nodes"]]
@@ -78,9 +83,19 @@ def test_tensor_parallel_shards_recompose():
         torch.testing.assert_close(torch.cat([s[f"layers.{i}.wo"] for s in shards], 1), full[f"layers.{i}.wo"])
         torch.testing.assert_close(torch.cat([s[f"layers.{i}.wd"] for s in shards], 1), full[f"layers.{i}.wd"])
         inter = TINY.intermediate
-        gate = torch.cat([s[f"layers.{i}.wgu"][:inter // 2] for s in shards])
-        up = torch.cat([s[f"layers.{i}.wgu"][inter // 2:] for s in shards])
-        torch.testing.assert_close(torch.cat([gate, up]), full[f"layers.{i}.wgu"])
+        p = f"model.layers.{i}.mlp."
+        # fused layout: 64-row gate/up blocks, zero-padded (96 -> 128 rows, 48 -> 64 per shard)
+        assert full[f"layers.{i}.wgu"].shape[0] == 2 * 128 and shards[0][f"layers.{i}.wgu"].shape[0] == 2 * 64
+        g_full, u_full = glu_unblocked(full[f"layers.{i}.wgu"], inter)
+        torch.testing.assert_close(g_full, st[p + "gate_proj.weight"])
+        torch.testing.assert_close(u_full, st[p + "up_proj.weight"])
+        gs = [glu_unblocked(s[f"layers.{i}.wgu"], inter // 2) for s in shards]
+        torch.testing.assert_close(torch.cat([g for g, _ in gs]), g_full)
+        torch.testing.assert_close(torch.cat([u for _, u in gs]), u_full)
+        assert not full[f"layers.{i}.wgu"].reshape(2, 2, 64, -1)[1, :, 32:].any()  # padding rows
+        # unfused layout: [gate; up]
+        plain = transform_weights(st, TINY, 1, 0, fused_glu=False)[f"layers.{i}.wgu"]
+        torch.testing.assert_close(plain, torch.cat([g_full, u_full]))
 
 
 def test_export_writes_loadable_graph_and_weights(tmp_path):
