@@ -23,10 +23,13 @@
 //    graphs (the reference dtype) and head dims the MMA kernels do not cover.
 #include <algorithm>
 #include <cfloat>
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <type_traits>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace dli_sm100 {
 namespace {
@@ -523,6 +526,283 @@ __global__ void __launch_bounds__(128, STAGES == 2 ? 3 : 2)
   }
 }
 
+// ---- decode with keys on the MMA M side, split-KV reduced inside a cluster ----------
+// For up to 8 query rows per KV head (decode: the GQA group of one token).
+// S^T = K Q^T puts 16 keys on the m16 side and the <= 8 query rows on n8, so a
+// 7-head group wastes 1/8 of the tensor work instead of 9/16 with a 16-row
+// query tile, and each thread keeps 2 rows' softmax state and a D x 8 O^T
+// accumulator (32 registers at D = 128). P^T for O^T += V^T P^T is the
+// transpose of the S^T fragment: movmatrix turns the accumulator layout into
+// the B-operand layout without shared memory. The S splits of one (sequence,
+// KV head) form a thread-block cluster; their (m, l, O) states are merged
+// through distributed shared memory in rank order (deterministic), so the
+// kernel needs no workspace and no combine launch.
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ void ldsm_x4_a(uint32_t (&r)[4], uint32_t addr) { ldsm_x4(r, addr); }
+
+template <typename T, int D, int STAGES>
+struct DecodeClusterSmem {
+  static constexpr int kRing = 2 * STAGES * 64 * D * 2;     // K and V stages
+  static constexpr int kQ = 8 * D * 2;                      // swizzled Q rows
+  static constexpr int kWarpO = 4 * 8 * D * 4;              // per-warp scaled O^T (aliases the ring)
+  static constexpr int kState = 8 * D * 4 + 2 * 8 * 4;      // merged O [8][D], m[8], l[8]
+  static constexpr int kWarpML = 2 * 4 * 8 * 4;             // per-warp m, l
+  static constexpr int kBytes = kRing + kQ + kState + kWarpML;
+  static_assert(kWarpO <= kRing, "warp partials alias the K/V ring");
+};
+
+template <typename T, int D, int STAGES>
+__global__ void __launch_bounds__(128)
+    attn_decode_cluster_kernel(const AttnArgs a) {
+  DLI_PDL_ENTRY();
+  using L = DecodeClusterSmem<T, D, STAGES>;
+  constexpr int BN = 64;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  T* sk = reinterpret_cast<T*>(smem_raw);                       // [STAGES][BN*D]
+  T* sv = sk + STAGES * BN * D;                                  // [STAGES][BN*D]
+  T* sq = reinterpret_cast<T*>(smem_raw + L::kRing);            // [8][D] swizzled
+  float* co = reinterpret_cast<float*>(smem_raw + L::kRing + L::kQ);  // merged O [8][D]
+  float* cm = co + 8 * D;                                        // merged m [8]
+  float* cl = cm + 8;                                            // merged l [8]
+  float* wm = cl + 8;                                            // [4][8]
+  float* wl = wm + 32;                                           // [4][8]
+  float* wo = reinterpret_cast<float*>(smem_raw);                // [4][8][D], after the loop
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int nsplit = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int kv_len = kv_len_of(a, b);
+  const int off = kv_len - a.seq_q;
+  const int rows = a.group * a.seq_q;  // <= 8
+  const int total_blocks = (kv_len + BN - 1) / BN;
+  const int blk0 = static_cast<int>(static_cast<int64_t>(split) * total_blocks / nsplit);
+  const int blk1 = static_cast<int>(static_cast<int64_t>(split + 1) * total_blocks / nsplit);
+  const int nblocks = blk1 - blk0;
+
+  const T* kbase = static_cast<const T*>(a.k) + b * a.k_sb + kvh * a.k_sh;
+  const T* vbase = static_cast<const T*>(a.v) + b * a.k_sb + kvh * a.k_sh;
+
+  // Q rows r -> (token s = r / group, head kvh*group + r % group); rows >= `rows` zero
+  {
+    const T* qb = static_cast<const T*>(a.q) + b * a.q_sb;
+    const uint32_t s0 = static_cast<uint32_t>(__cvta_generic_to_shared(sq));
+    for (int c = threadIdx.x; c < 8 * (D / 8); c += 128) {
+      const int r = c / (D / 8), ch = c - r * (D / 8);
+      const bool valid = r < rows;
+      const int qs = valid ? r / a.group : 0, hh = kvh * a.group + (valid ? r - qs * a.group : 0);
+      cp_async16(s0 + swz<D>(r, ch * 8) * 2, qb + hh * a.q_sh + qs * a.q_ss + ch * 8, valid);
+    }
+  }
+#pragma unroll
+  for (int st = 0; st < STAGES - 1; ++st) {
+    if (st < nblocks) {
+      load_tile<T, D, BN, 128>(sk + st * BN * D, kbase, (blk0 + st) * BN, kv_len);
+      load_tile<T, D, BN, 128>(sv + st * BN * D, vbase, (blk0 + st) * BN, kv_len);
+    }
+    cp_async_commit();  // the first group also carries Q
+  }
+
+  // query token of the thread's two score columns (rows 2t, 2t+1), for the causal mask
+  const int qs0 = (2 * t) < rows ? (2 * t) / a.group : 0;
+  const int qs1 = (2 * t + 1) < rows ? (2 * t + 1) / a.group : 0;
+
+  uint32_t qf[D / 16][2];
+  float o[D / 16][4];
+#pragma unroll
+  for (int i = 0; i < D / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const int kw = warp * 16;  // this warp's 16 keys of every block
+
+  for (int it = 0; it < nblocks; ++it) {
+    const int pre = it + STAGES - 1;
+    if (pre < nblocks) {
+      const int st = pre % STAGES;
+      load_tile<T, D, BN, 128>(sk + st * BN * D, kbase, (blk0 + pre) * BN, kv_len);
+      load_tile<T, D, BN, 128>(sv + st * BN * D, vbase, (blk0 + pre) * BN, kv_len);
+    }
+    cp_async_commit();
+    cp_async_wait<STAGES - 1>();
+    __syncthreads();
+    if (it == 0) {
+      // Q^T B fragments: ldmatrix of the [8 rows][16 dims] slices
+      const uint32_t qa = static_cast<uint32_t>(__cvta_generic_to_shared(sq));
+#pragma unroll
+      for (int kk = 0; kk < D / 16; kk += 2) {
+        uint32_t r4[4];
+        ldsm_x4(r4, qa + swz<D>(lane & 7, kk * 16 + (lane >> 3) * 8) * 2);
+        qf[kk][0] = r4[0];
+        qf[kk][1] = r4[1];
+        qf[kk + 1][0] = r4[2];
+        qf[kk + 1][1] = r4[3];
+      }
+    }
+    const int st = it % STAGES;
+    const uint32_t ks = static_cast<uint32_t>(__cvta_generic_to_shared(sk + st * BN * D));
+    const uint32_t vs = static_cast<uint32_t>(__cvta_generic_to_shared(sv + st * BN * D));
+
+    // S^T [16 keys x 8 rows]
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t af[4];
+      ldsm_x4_a(af, ks + swz<D>(kw + (lane & 7) + ((lane >> 3) & 1) * 8, kk * 16 + (lane >> 4) * 8) * 2);
+      mma16816<T>(sc, af, qf[kk][0], qf[kk][1]);
+    }
+    const int key0 = (blk0 + it) * BN + kw + g, key1 = key0 + 8;
+    const bool v00 = key0 < kv_len && (!a.causal || key0 <= qs0 + off);
+    const bool v01 = key0 < kv_len && (!a.causal || key0 <= qs1 + off);
+    const bool v10 = key1 < kv_len && (!a.causal || key1 <= qs0 + off);
+    const bool v11 = key1 < kv_len && (!a.causal || key1 <= qs1 + off);
+    const float s00 = v00 ? sc[0] * a.scale_log2 : -INFINITY;  // key0, row 2t
+    const float s01 = v01 ? sc[1] * a.scale_log2 : -INFINITY;  // key0, row 2t+1
+    const float s10 = v10 ? sc[2] * a.scale_log2 : -INFINITY;  // key1, row 2t
+    const float s11 = v11 ? sc[3] * a.scale_log2 : -INFINITY;  // key1, row 2t+1
+    float mx0 = fmaxf(s00, s10), mx1 = fmaxf(s01, s11);
+#pragma unroll
+    for (int sh = 4; sh < 32; sh <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, sh));
+    }
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+    const float al0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - n0);
+    const float al1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - n1);
+    m0 = n0;
+    m1 = n1;
+    const float p00 = (n0 == -INFINITY) ? 0.f : exp2f(s00 - n0);
+    const float p10 = (n0 == -INFINITY) ? 0.f : exp2f(s10 - n0);
+    const float p01 = (n1 == -INFINITY) ? 0.f : exp2f(s01 - n1);
+    const float p11 = (n1 == -INFINITY) ? 0.f : exp2f(s11 - n1);
+    l0 = l0 * al0 + p00 + p10;  // this thread's keys; summed over the warp at the end
+    l1 = l1 * al1 + p01 + p11;
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) {
+      o[i][0] *= al0;
+      o[i][1] *= al1;
+      o[i][2] *= al0;
+      o[i][3] *= al1;
+    }
+    // P^T as the B operand: transpose the two 8x8 accumulator blocks
+    const uint32_t pb0 = movmatrix_t(pack2<T>(p00, p01));
+    const uint32_t pb1 = movmatrix_t(pack2<T>(p10, p11));
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+      uint32_t va[4];
+      ldsm_x4_t(va, vs + swz<D>(kw + (lane & 7) + (lane >> 4) * 8, mt * 16 + ((lane >> 3) & 1) * 8) * 2);
+      mma16816<T>(o[mt], va, pb0, pb1);
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  __syncthreads();  // the ring becomes the warp-partial area
+
+  // merge the 4 warps (fixed order)
+#pragma unroll
+  for (int sh = 4; sh < 32; sh <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, sh);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, sh);
+  }
+  if (g == 0) {
+    wm[warp * 8 + 2 * t] = m0;
+    wm[warp * 8 + 2 * t + 1] = m1;
+    wl[warp * 8 + 2 * t] = l0;
+    wl[warp * 8 + 2 * t + 1] = l1;
+  }
+  __syncthreads();
+  {
+    float M0 = -INFINITY, M1 = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      M0 = fmaxf(M0, wm[w * 8 + 2 * t]);
+      M1 = fmaxf(M1, wm[w * 8 + 2 * t + 1]);
+    }
+    const float f0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - M0);
+    const float f1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - M1);
+    float* myo = wo + warp * 8 * D;
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt) {
+      const int d = mt * 16 + g;
+      myo[(2 * t) * D + d] = o[mt][0] * f0;
+      myo[(2 * t + 1) * D + d] = o[mt][1] * f1;
+      myo[(2 * t) * D + d + 8] = o[mt][2] * f0;
+      myo[(2 * t + 1) * D + d + 8] = o[mt][3] * f1;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 8 * D; i += 128) {
+    co[i] = ((wo[i] + wo[8 * D + i]) + wo[2 * 8 * D + i]) + wo[3 * 8 * D + i];
+  }
+  if (threadIdx.x < 8) {
+    const int r = threadIdx.x;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w * 8 + r]);
+    float Lsum = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = wm[w * 8 + r];
+      Lsum += (mw == -INFINITY) ? 0.f : wl[w * 8 + r] * exp2f(mw - M);
+    }
+    cm[r] = M;
+    cl[r] = Lsum;
+  }
+  if (nsplit == 1) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < rows * D; i += 128) {
+      const int r = i / D, d = i - r * D;
+      const int qs = r / a.group, hh = kvh * a.group + (r - qs * a.group);
+      T* dst = static_cast<T*>(a.out) + b * a.o_sb + hh * a.o_sh + qs * a.o_ss + d;
+      *dst = from_f32<T>(cl[r] > 0.f ? co[r * D + d] / cl[r] : 0.f);
+    }
+    return;
+  }
+  // merge the cluster's splits: rank r writes every nsplit-th quad of the output
+  cluster_sync();
+  const uint32_t co_local = static_cast<uint32_t>(__cvta_generic_to_shared(co));
+  const uint32_t cm_local = static_cast<uint32_t>(__cvta_generic_to_shared(cm));
+  uint32_t rank;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+  const int quads = rows * (D / 4);
+  for (int q = static_cast<int>(rank) * 128 + threadIdx.x; q < quads; q += nsplit * 128) {
+    const int r = q / (D / 4), d = (q - r * (D / 4)) * 4;
+    float ms[8], ls[8];
+    float M = -INFINITY;
+    for (int s2 = 0; s2 < nsplit; ++s2) {
+      const uint32_t base = mapa_shared(cm_local, static_cast<uint32_t>(s2));
+      float mv, lv;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(mv) : "r"(base + r * 4) : "memory");
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(lv) : "r"(base + (8 + r) * 4) : "memory");
+      ms[s2] = mv;
+      ls[s2] = lv;
+      M = fmaxf(M, mv);
+    }
+    float Lsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s2 = 0; s2 < nsplit; ++s2) {
+      if (ms[s2] == -INFINITY) continue;
+      const float w = exp2f(ms[s2] - M);
+      Lsum += ls[s2] * w;
+      const float4 v = ld_dsmem_f4(mapa_shared(co_local + (r * D + d) * 4, static_cast<uint32_t>(s2)));
+      acc.x += v.x * w;
+      acc.y += v.y * w;
+      acc.z += v.z * w;
+      acc.w += v.w * w;
+    }
+    const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+    const int qs = r / a.group, hh = kvh * a.group + (r - qs * a.group);
+    T* dst = static_cast<T*>(a.out) + b * a.o_sb + hh * a.o_sh + qs * a.o_ss + d;
+    dst[0] = from_f32<T>(acc.x * inv);
+    dst[1] = from_f32<T>(acc.y * inv);
+    dst[2] = from_f32<T>(acc.z * inv);
+    dst[3] = from_f32<T>(acc.w * inv);
+  }
+  cluster_sync();  // keep this CTA's state alive until every rank has read it
+}
+
 // Merges split partials: out = sum_s O_s 2^(m_s - M) / sum_s l_s 2^(m_s - M).
 template <typename T>
 __global__ void attn_combine_kernel(const AttnArgs a) {
@@ -637,9 +917,61 @@ __global__ void attn_fallback_kernel(const AttnArgs a) {
 // ---- host dispatch ----------------------------------------------------------------------
 struct DecodePlan {
   bool decode = false;
+  bool cluster = false;  // attn_decode_cluster_kernel (<= 8 query rows per KV head)
   int splits = 1;
   size_t workspace = 0;
 };
+
+// K/V stages of the cluster decode kernel: 3 (two CTAs per SM at D = 128) or 2.
+static const int kClusterStages = tuning_knob("ATTN_CLUSTER_STAGES", 3) == 2 ? 2 : 3;
+
+template <int D, int STAGES>
+int cluster_decode_occupancy(int cluster) {
+  using L = DecodeClusterSmem<__nv_bfloat16, D, STAGES>;
+  auto kern = attn_decode_cluster_kernel<__nv_bfloat16, D, STAGES>;
+  if (ensure_smem(reinterpret_cast<const void*>(kern), L::kBytes, "attention decode") != DLI_OK) return 0;
+  int n = 0;
+  if (cluster <= 1) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 128, L::kBytes) != cudaSuccess) n = 0;
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(cluster), 1, 1);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = L::kBytes;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  return n;
+}
+
+// CTAs per SM (cluster <= 1) or resident clusters, cached per device.
+int cluster_decode_capacity(int head_dim, int cluster) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  const auto key = std::make_tuple(dev, head_dim, kClusterStages, cluster);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (head_dim == 64)
+    n = kClusterStages == 3 ? cluster_decode_occupancy<64, 3>(cluster) : cluster_decode_occupancy<64, 2>(cluster);
+  else
+    n = kClusterStages == 3 ? cluster_decode_occupancy<128, 3>(cluster) : cluster_decode_occupancy<128, 2>(cluster);
+  cache[key] = n;
+  return n;
+}
 
 DecodePlan plan_decode(int64_t batch, int64_t hkv, int64_t group, int64_t seq_q, int64_t max_kv,
                        int64_t head_dim) {
@@ -648,6 +980,21 @@ DecodePlan plan_decode(int64_t batch, int64_t hkv, int64_t group, int64_t seq_q,
   p.decode = true;
   const int64_t pairs = batch * hkv;
   const int64_t blocks = std::max<int64_t>(1, ceil_div(max_kv, 64));
+  static const bool kClusterOn = tuning_knob("ATTN_CLUSTER", 1) != 0;
+  if (group * seq_q <= 8 && kClusterOn) {
+    // One resident wave: the largest cluster size S <= 8 with pairs * S CTAs all
+    // resident at once and every split holding >= 1 key block.
+    p.cluster = true;
+    const int64_t slots = static_cast<int64_t>(std::max(1, cluster_decode_capacity(static_cast<int>(head_dim), 1))) *
+                          sm_count();
+    for (int s = 8; s >= 2; --s) {
+      if (pairs * s <= slots && s <= blocks && pairs <= cluster_decode_capacity(static_cast<int>(head_dim), s)) {
+        p.splits = s;
+        break;
+      }
+    }
+    return p;
+  }
   // Few, long splits measure best: each split pays a pipeline fill, a 4-warp
   // merge and a partial round trip, so splits only need to fill the SMs once.
   static const int kWaves = tuning_knob("ATTN_WAVES", 1);
@@ -677,8 +1024,44 @@ dli_status launch_decode(const AttnArgs& args, const DecodePlan& plan, cudaStrea
   return DLI_OK;
 }
 
+template <typename T, int D, int STAGES>
+dli_status launch_decode_cluster(const AttnArgs& args, const DecodePlan& plan, cudaStream_t stream) {
+  using L = DecodeClusterSmem<T, D, STAGES>;
+  auto kern = attn_decode_cluster_kernel<T, D, STAGES>;
+  const dli_status st = ensure_smem(reinterpret_cast<const void*>(kern), L::kBytes, "attention decode");
+  if (st != DLI_OK) return st;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(plan.splits), static_cast<unsigned>(args.hkv),
+                     static_cast<unsigned>(args.batch));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (plan.splits > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = static_cast<unsigned>(plan.splits);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  cudaLaunchKernelEx(&cfg, kern, args);
+  return check_launch("attention decode");
+}
+
 template <typename T, int D>
 dli_status launch_tc_attention(const AttnArgs& args, const DecodePlan& plan, cudaStream_t stream) {
+  if (plan.decode && plan.cluster) {
+    return kClusterStages == 3 ? launch_decode_cluster<T, D, 3>(args, plan, stream)
+                               : launch_decode_cluster<T, D, 2>(args, plan, stream);
+  }
   if (plan.decode) {
     const dli_status st = kDecodeStages == 3 ? launch_decode<T, D, 3>(args, plan, stream)
                                              : launch_decode<T, D, 2>(args, plan, stream);
@@ -705,7 +1088,7 @@ dli_status run_attention(AttnArgs& args, dli_dtype dtype, int64_t max_kv, void* 
                   aligned(args.v, 16) && aligned(args.out, 4);
   if (tc) {
     const DecodePlan plan = plan_decode(args.batch, args.hkv, args.group, args.seq_q, max_kv, args.head_dim);
-    if (plan.decode && plan.splits > 1) {
+    if (plan.decode && !plan.cluster && plan.splits > 1) {
       if (workspace == nullptr || workspace_bytes < plan.workspace)
         return fail(DLI_ERR_WORKSPACE, "attention: workspace too small (need " +
                                            std::to_string(plan.workspace) + " bytes)");

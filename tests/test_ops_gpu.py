@@ -215,12 +215,20 @@ def _cache_reference(q_bshd, ck, cv, positions):
     return torch.cat(outs, 0)
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16], ids=["bf16"])
+_RAG32 = [(i * 997) % 2559 for i in range(32)]  # ragged cache positions, 0 and near-capacity included
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
 @pytest.mark.parametrize("b,s,hq,hkv,d,cap,positions", [
     (4, 1, 28, 4, 128, 2560, [100, 513, 2000, 0]),
     (8, 1, 14, 2, 64, 768, [512, 600, 700, 767 - 1, 3, 64, 65, 128]),
     (2, 3, 64, 8, 128, 1024, [10, 500]),
     (2, 77, 14, 2, 64, 512, [0, 40]),
+    # one token, <= 8 query rows per KV head: the cluster-merged decode kernel at the
+    # 7B shape and its TP 2 / TP 4 shards, the 72B group of 8, a group of 6, 2 tokens x 4
+    (32, 1, 28, 4, 128, 2560, _RAG32), (32, 1, 14, 2, 128, 2560, _RAG32), (32, 1, 7, 1, 128, 2560, _RAG32),
+    (16, 1, 64, 8, 128, 4608, [(i * 1237) % 4607 for i in range(16)]), (3, 1, 12, 2, 64, 256, [0, 1, 254]),
+    (4, 2, 16, 4, 128, 512, [0, 63, 64, 509]), (1, 1, 8, 1, 128, 64, [0]),
 ])
 def test_attention_kvcache(b, s, hq, hkv, d, cap, positions, dtype):
     import dli_sm100 as C

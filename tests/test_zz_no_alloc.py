@@ -6,7 +6,10 @@ instead of a caller workspace.
 
 Checked through the C ABI against dli_sm100_attention_kvcache (the entry point
 with a caller workspace) on two calls in a row with different inputs, so
-leftovers of the first call in the shared array cannot leak into the second;
+leftovers of the first call in the shared array cannot leak into the second.
+The case decodes two tokens per sequence at the 7B head shape: 2 x 7 query
+rows per KV head take the split-KV kernel whose partials need scratch (single
+tokens take the cluster kernel, which needs none);
 bf16 tolerance as in test_ops_gpu.py (relative Frobenius error <= 1.5e-2; the two
 calls run the same kernels, so in practice they agree exactly). The file name
 sorts last so a run that stops at the first failure has run everything else.
@@ -34,18 +37,18 @@ def _noalloc(q, ck, cv, pos):
     return out
 
 
-def _case(seed, b=32, hq=28, hkv=4, d=128, cap=2560):
+def _case(seed, b=32, hq=28, hkv=4, d=128, cap=2560, seq=2):
     g = torch.Generator(device="cuda").manual_seed(seed)
-    q = torch.randn(b, 1, hq, d, device="cuda", generator=g).to(torch.bfloat16)
+    q = torch.randn(b, seq, hq, d, device="cuda", generator=g).to(torch.bfloat16)
     ck = torch.randn(b, hkv, cap, d, device="cuda", generator=g).to(torch.bfloat16)
     cv = torch.randn(b, hkv, cap, d, device="cuda", generator=g).to(torch.bfloat16)
-    pos = torch.randint(1, cap - 1, (b,), device="cuda", generator=g)
+    pos = torch.randint(1, cap - seq, (b,), device="cuda", generator=g)
     return q, ck, cv, pos
 
 
 def test_noalloc_matches_workspace_entry_point_on_two_calls():
-    # the 7B decode shape: split-KV partials live in the fixed scratch array
-    need = C.lib().dli_sm100_attention_kvcache_workspace_size(32, 1, 28, 4, 2560, 128, 2)
+    # the 7B head shape, two tokens: split-KV partials live in the fixed scratch array
+    need = C.lib().dli_sm100_attention_kvcache_workspace_size(32, 2, 28, 4, 2560, 128, 2)
     assert 0 < need <= C.lib().dli_sm100_attention_kvcache_noalloc_max_scratch()
     for seed in (1, 2):
         q, ck, cv, pos = _case(seed)
@@ -61,11 +64,11 @@ _REJECT = r"""
 import sys, torch
 import dli_sm100 as C
 b, hq, hkv, d, cap = 32, 28, 4, 128, 2560
-need = C.lib().dli_sm100_attention_kvcache_workspace_size(b, 1, hq, hkv, cap, d, 2)
+need = C.lib().dli_sm100_attention_kvcache_workspace_size(b, 2, hq, hkv, cap, d, 2)
 assert need > C.lib().dli_sm100_attention_kvcache_noalloc_max_scratch(), need
 q = torch.zeros(16, device="cuda", dtype=torch.bfloat16)  # never read: the call is rejected first
 st = C.lib().dli_sm100_attention_kvcache_noalloc(C._ptr(q), C._ptr(q), C._ptr(q), C._ptr(q), C._ptr(q),
-                                                 b, 1, hq, hkv, cap, d, 0.0, 2, C._stream())
+                                                 b, 2, hq, hkv, cap, d, 0.0, 2, C._stream())
 assert st == C.DLI_ERR_WORKSPACE, st
 assert "scratch" in C.last_error(), C.last_error()
 print("rejected")
