@@ -10,6 +10,10 @@
 // b*k_sb + kvh*k_sh + j*D. The key count of sequence b is `kv_len[b]` (a device
 // array, so CUDA-graph replays can advance it) or the dense `seq_k`.
 //
+//  * cluster decode kernel (Sq * group <= 8 query rows per KV head): split-KV
+//    flash decoding with keys on the MMA M side (S^T = K Q^T, O^T = V^T P^T),
+//    the splits of one (sequence, KV head) merged inside a thread-block cluster
+//    through distributed shared memory (no workspace, no combine launch).
 //  * decode kernel (Sq * group <= 16 query rows per KV head): split-KV flash
 //    decoding. CTA = (split, kv head, batch); the group's query rows form one
 //    16-row MMA tile so each K/V byte fetched from HBM serves every query head
