@@ -773,28 +773,33 @@ __global__ void __launch_bounds__(128)
   const int quads = rows * (D / 4);
   for (int q = static_cast<int>(rank) * 128 + threadIdx.x; q < quads; q += nsplit * 128) {
     const int r = q / (D / 4), d = (q - r * (D / 4)) * 4;
+    // every rank's (m, l, O quad) is requested before any is used: one DSMEM round trip
     float ms[8], ls[8];
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < nsplit; ++s2) {
-      const uint32_t base = mapa_shared(cm_local, static_cast<uint32_t>(s2));
-      float mv, lv;
-      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(mv) : "r"(base + r * 4) : "memory");
-      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(lv) : "r"(base + (8 + r) * 4) : "memory");
-      ms[s2] = mv;
-      ls[s2] = lv;
-      M = fmaxf(M, mv);
+    float4 ov[8];
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2) {
+      if (s2 < nsplit) {
+        const uint32_t base = mapa_shared(cm_local, static_cast<uint32_t>(s2));
+        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(ms[s2]) : "r"(base + r * 4) : "memory");
+        asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(ls[s2]) : "r"(base + (8 + r) * 4) : "memory");
+        ov[s2] = ld_dsmem_f4(mapa_shared(co_local + (r * D + d) * 4, static_cast<uint32_t>(s2)));
+      }
     }
+    float M = -INFINITY;
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2)
+      if (s2 < nsplit) M = fmaxf(M, ms[s2]);
     float Lsum = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s2 = 0; s2 < nsplit; ++s2) {
-      if (ms[s2] == -INFINITY) continue;
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2) {
+      if (s2 >= nsplit || ms[s2] == -INFINITY) continue;
       const float w = exp2f(ms[s2] - M);
       Lsum += ls[s2] * w;
-      const float4 v = ld_dsmem_f4(mapa_shared(co_local + (r * D + d) * 4, static_cast<uint32_t>(s2)));
-      acc.x += v.x * w;
-      acc.y += v.y * w;
-      acc.z += v.z * w;
-      acc.w += v.w * w;
+      acc.x += ov[s2].x * w;
+      acc.y += ov[s2].y * w;
+      acc.z += ov[s2].z * w;
+      acc.w += ov[s2].w * w;
     }
     const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
     const int qs = r / a.group, hh = kvh * a.group + (r - qs * a.group);

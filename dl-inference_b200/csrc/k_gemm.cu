@@ -357,12 +357,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (rr >= 64) continue;
         const uint32_t og = static_cast<uint32_t>((rr * (BN + 4) + cq) * 4);
         const uint32_t ou = static_cast<uint32_t>(((rr + 64) * (BN + 4) + cq) * 4);
+        float4 pg[8], pu[8];
+#pragma unroll
+        for (int s2 = 0; s2 < 8; ++s2) {
+          if (s2 < S) {
+            pg[s2] = ld_dsmem_f4(mapa_shared(red_local + og, s2));
+            pu[s2] = ld_dsmem_f4(mapa_shared(red_local + ou, s2));
+          }
+        }
         float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int s2 = 0; s2 < S; ++s2) {
-          const float4 a = ld_dsmem_f4(mapa_shared(red_local + og, s2));
-          const float4 b = ld_dsmem_f4(mapa_shared(red_local + ou, s2));
-          g[0] += a.x; g[1] += a.y; g[2] += a.z; g[3] += a.w;
-          u[0] += b.x; u[1] += b.y; u[2] += b.z; u[3] += b.w;
+#pragma unroll
+        for (int s2 = 0; s2 < 8; ++s2) {
+          if (s2 < S) {
+            g[0] += pg[s2].x; g[1] += pg[s2].y; g[2] += pg[s2].z; g[3] += pg[s2].w;
+            u[0] += pu[s2].x; u[1] += pu[s2].y; u[2] += pu[s2].z; u[3] += pu[s2].w;
+          }
         }
         if (tj * BN + cq < p.rows_b) store_glu_t<T>(p, ti, rr, tj * BN + cq, g, u, 4);
       }
@@ -374,13 +383,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int cq = (q / R) * 4;
       if (rr >= kBM) continue;
       const uint32_t off = static_cast<uint32_t>((rr * (BN + 4) + cq) * 4);
+      // issue every rank's load before the first add: one DSMEM round trip, not S
+      float4 part[8];
+#pragma unroll
+      for (int s = 0; s < 8; ++s)
+        if (s < S) part[s] = ld_dsmem_f4(mapa_shared(red_local + off, s));
       float v[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int s = 0; s < S; ++s) {
-        const float4 o = ld_dsmem_f4(mapa_shared(red_local + off, s));
-        v[0] += o.x;
-        v[1] += o.y;
-        v[2] += o.z;
-        v[3] += o.w;
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        if (s < S) {
+          v[0] += part[s].x;
+          v[1] += part[s].y;
+          v[2] += part[s].z;
+          v[3] += part[s].w;
+        }
       }
       const int64_t gi = static_cast<int64_t>(ti) * kBM + rr;
       if (tj * BN + cq < p.rows_b) store_vals<T>(p, gi, tj * BN + cq, v, 4);
