@@ -17,7 +17,7 @@ over ranks.
 
 Printed JSON (rank 0): value = decode tok/s of the whole job; prefill tok/s,
 e2e (decode through the public API with host ids in and out every token),
-roofline of the dominant decode kernel (gate/up GEMM, HBM-bound) and of the
+roofline of the dominant decode kernel (gate/up + SwiGLU GEMM, HBM-bound) and of the
 dominant prefill kernel (tensor-bound), clocks sampled during the timed region,
 CPU baseline, and the number of this library's kernels launched.
 """
@@ -349,41 +349,43 @@ def main() -> int:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
     e2e_tok_s = total_seqs * e2e_steps / (e2e_ms.item() / 1e3)
 
-    # --- roofline of the dominant kernels, timed live with CUDA events
+    # --- roofline of the dominant kernels, timed live with CUDA events: the fused
+    #     gate/up + SwiGLU GEMM (linear_silu_mul) the decode and prefill graphs run
     pk = peaks()
     inter_local = shape.intermediate // tp
-    n_gu, k_gu = 2 * inter_local, shape.hidden
+    k_gu = shape.hidden
+    w_gu = weights["layers.0.wgu"]  # 64-row gate/up blocks, [2*ceil(I/64)*64, K]
+    rows_w = w_gu.shape[0]
     x_dec = torch.randn(b_local, k_gu, device=dev).to(torch.bfloat16)
-    w_gu = weights["layers.0.wgu"]
     reps = 20
     for _ in range(3):
-        dli_sm100.linear(x_dec, w_gu)
+        dli_sm100.linear_silu_mul(x_dec, w_gu, inter_local)
     ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ea.record(stream)
     for _ in range(reps):
-        dli_sm100.linear(x_dec, w_gu)
+        dli_sm100.linear_silu_mul(x_dec, w_gu, inter_local)
     eb.record(stream)
     torch.cuda.synchronize()
     gemm_ms = ea.elapsed_time(eb) / reps
-    gemm_bytes = (n_gu * k_gu + b_local * (n_gu + k_gu)) * 2
+    gemm_bytes = (rows_w * k_gu + b_local * (k_gu + inter_local)) * 2  # weights + x + act
     achieved = gemm_bytes / (gemm_ms / 1e3) / 1e9
     traffic = None
     # DRAM bytes (read + write) of one launch of this kernel from an ncu capture,
     # recorded by hand in profiles/traffic.txt (JSON text) from the committed summary
     prof = ROOT / "profiles" / "traffic.txt"
     if prof.exists():
-        traffic = json.loads(prof.read_text()).get(f"decode_gate_up_{args.model}_tp{tp}_b{b_local}")
-    # prefill: gate/up GEMM at M = b_local * prompt (capped for memory)
+        traffic = json.loads(prof.read_text()).get(f"decode_glu_gate_up_{args.model}_tp{tp}_b{b_local}")
+    # prefill: the same kernel at M = b_local * prompt (capped for memory)
     m_pre = min(b_local * prompt, 16384)
     x_pre = torch.randn(m_pre, k_gu, device=dev).to(torch.bfloat16)
-    dli_sm100.linear(x_pre, w_gu)
+    dli_sm100.linear_silu_mul(x_pre, w_gu, inter_local)
     ea.record(stream)
     for _ in range(5):
-        dli_sm100.linear(x_pre, w_gu)
+        dli_sm100.linear_silu_mul(x_pre, w_gu, inter_local)
     eb.record(stream)
     torch.cuda.synchronize()
     pre_gemm_ms = ea.elapsed_time(eb) / 5
-    pre_tflops = 2.0 * m_pre * n_gu * k_gu / (pre_gemm_ms / 1e3) / 1e12
+    pre_tflops = 2.0 * m_pre * 2 * inter_local * k_gu / (pre_gemm_ms / 1e3) / 1e12
     step_bytes = Q.decode_bytes_per_step(shape, b_local, prompt + dsteps // 2) / tp
     step_ms = dec_ms / (args.steps * dsteps)
     launches = args.steps * (launches_prefill + dsteps * launches_decode)
@@ -414,14 +416,16 @@ def main() -> int:
             "e2e": {"value": e2e_tok_s, "unit": "tok/s (decode)", "h2d_bytes_per_step": 8 * b_local,
                     "d2h_bytes_per_step": 8 * b_local, "steps": e2e_steps,
                     "path": "Qwen2Runner decode graph fed from pinned host ids, next ids read to host every token"},
-            "roofline": {"bound": "hbm", "kernel": f"tcgen05 swap-AB GEMM gate_up [{b_local}x{k_gu}]x[{n_gu}x{k_gu}]^T",
+            "roofline": {"bound": "hbm",
+                         "kernel": f"tcgen05 swap-AB GEMM gate/up + SwiGLU epilogue [{b_local}x{k_gu}]x[{rows_w}x{k_gu}]^T",
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
                          "algorithmic_bytes": gemm_bytes, "ms": gemm_ms, "peak_source": pk["source"]},
             "roofline_decode_step": {"bound": "hbm", "bytes": step_bytes, "ms": step_ms,
                                      "achieved": step_bytes / (step_ms / 1e3) / 1e9, "peak": pk["hbm_gbs"],
                                      "unit": "GB/s", "frac": step_bytes / (step_ms / 1e3) / 1e9 / pk["hbm_gbs"]},
-            "roofline_prefill": {"bound": "tensor", "kernel": f"tcgen05 GEMM gate_up [{m_pre}x{k_gu}]x[{n_gu}x{k_gu}]^T",
+            "roofline_prefill": {"bound": "tensor",
+                                 "kernel": f"tcgen05 GEMM gate/up + SwiGLU epilogue [{m_pre}x{k_gu}]x[{rows_w}x{k_gu}]^T",
                                  "achieved": pre_tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                                  "frac": pre_tflops / pk["bf16_tflops"]},
             "clocks": clock,

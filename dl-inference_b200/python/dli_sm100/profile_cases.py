@@ -26,6 +26,15 @@ def _gemm(m, n, k):
     return (lambda: C.linear(x, w)), 2 * (n * k + m * (n + k)), 2.0 * m * n * k
 
 
+def _glu(m, inter, k):
+    from dli_export.qwen2 import glu_blocked
+
+    x = torch.randn(m, k, device="cuda").to(BF)
+    w = glu_blocked((torch.randn(inter, k, device="cuda") * 0.02).to(BF),
+                    (torch.randn(inter, k, device="cuda") * 0.02).to(BF))
+    return (lambda: C.linear_silu_mul(x, w, inter)), 2 * (2 * inter * k + m * (inter + k)), 4.0 * m * inter * k
+
+
 def _attn_decode(b=32, hq=28, hkv=4, d=128, cap=2560, ctx=2304):
     q = torch.randn(b, 1, hq, d, device="cuda").to(BF)
     ck = torch.randn(b, hkv, cap, d, device="cuda").to(BF)
@@ -53,7 +62,10 @@ CASES = {
     "gemm_decode_lm_head": lambda: _gemm(32, 152064, 3584),
     "gemm_prefill_gate_up": lambda: _gemm(8192, 37888, 3584),
     "gemm_prefill_o": lambda: _gemm(8192, 3584, 3584),
+    "glu_decode_gate_up": lambda: _glu(32, 18944, 3584),
+    "glu_prefill_gate_up": lambda: _glu(8192, 18944, 3584),
     "attn_decode": _attn_decode,
+    "attn_decode_tp4": lambda: _attn_decode(hq=7, hkv=1),
     "attn_prefill": _attn_prefill,
 }
 
