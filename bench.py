@@ -263,8 +263,12 @@ def main() -> int:
         del st
     g = torch.Generator(device=dev).manual_seed(7)
     weights["embed"] = (torch.randn(shape.vocab, shape.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-    weights["lm_head"] = weights["embed"] if shape.tie_embeddings else \
+    lm = weights["embed"] if shape.tie_embeddings else \
         (torch.randn(shape.vocab, shape.hidden, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    if Q.vocab_parallel(shape, tp):  # this rank's vocabulary rows (the graph picks with tp_argmax)
+        vs = shape.vocab // tp
+        lm = lm[tp_rank * vs:(tp_rank + 1) * vs].contiguous()
+    weights["lm_head"] = lm
     weights["norm"] = torch.ones(shape.hidden, device=dev, dtype=torch.bfloat16)
     cos, sin = Q.rotary_tables(shape, capacity)
     weights["rotary_cos"], weights["rotary_sin"] = cos.to(dev), sin.to(dev)

@@ -11,8 +11,10 @@
 // into every other rank's address space (CUDA IPC):
 //
 //   epochs u32 [max_rows]                        local: last epoch of each row's CTA
+//   epochs u32 [max_rows]                        local: same for the argmax exchange
 //   words  u64 [2 slots][tp][max_rows][row_words] written by peers (row_words =
 //                                                row_elems * sizeof(T) / 4)
+//   words  u64 [2 slots][tp][max_rows][2]        argmax candidates (value, id)
 //
 // CTA r (one per row) of rank k takes epoch e = epochs[r] + 1 and stores its row
 // of the partial sum into slot e&1, source k, row r of every peer's buffer. It
@@ -52,7 +54,7 @@ struct ExchangeParams {
 };
 
 __host__ __device__ inline int64_t header_bytes(int64_t max_rows) {
-  return (max_rows * 4 + kHeaderAlign - 1) / kHeaderAlign * kHeaderAlign;
+  return (2 * max_rows * 4 + kHeaderAlign - 1) / kHeaderAlign * kHeaderAlign;
 }
 
 __device__ __forceinline__ uint64_t timer_ns() {
@@ -73,6 +75,12 @@ __device__ __forceinline__ void ld_ll2(const uint64_t* p, uint64_t& a, uint64_t&
 __device__ __forceinline__ uint64_t* row_words(char* base, const ExchangeParams& p, int slot, int src, int64_t row) {
   uint64_t* w = reinterpret_cast<uint64_t*>(base + header_bytes(p.max_rows));
   return w + ((static_cast<int64_t>(slot) * p.tp + src) * p.max_rows + row) * p.row_words;
+}
+
+// (value, id) candidate words of the argmax exchange, after the row words.
+__device__ __forceinline__ uint64_t* argmax_words(char* base, const ExchangeParams& p, int slot, int src, int64_t row) {
+  uint64_t* w = reinterpret_cast<uint64_t*>(base + header_bytes(p.max_rows)) + 2 * p.tp * p.max_rows * p.row_words;
+  return w + ((static_cast<int64_t>(slot) * p.tp + src) * p.max_rows + row) * 2;
 }
 
 // Waits until the 4 words at `p` carry epoch e; returns their payload. On
@@ -205,6 +213,92 @@ __global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
   if (threadIdx.x == 0) epochs[r] = e;
 }
 
+// Vocabulary-parallel greedy pick: rank i holds the logits of ids
+// [i*width, (i+1)*width). CTA r finds its row's local argmax (largest value,
+// lowest id), pushes (value, global id) to every peer as two epoch-tagged words
+// and picks the winner over the ranks in rank order, so ties go to the lowest
+// id exactly as one argmax over the whole row would.
+__device__ __forceinline__ void better(float v, int64_t i, float& bv, int64_t& bi) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) allgather_argmax_kernel(ExchangeParams p, const T* __restrict__ x,
+                                                               int64_t width, int64_t* __restrict__ out) {
+  constexpr int V = Vec16<T>::N;
+  constexpr int64_t kNone = INT64_MAX;
+  constexpr uint32_t kNoId = 0x7fffffffu;
+  __shared__ float sval[8];
+  __shared__ int64_t sidx[8];
+  pdl_wait();  // the logits come from the previous kernel
+  pdl_trigger();
+  const int rank = p.rank0 + static_cast<int>(blockIdx.y);
+  const int64_t r = blockIdx.x;
+  const T* row = x + static_cast<int64_t>(blockIdx.y) * p.rank_stride + r * width;
+  float best = -INFINITY;
+  int64_t bi = kNone;
+  const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const int64_t nvec = vec ? width / V : 0;
+  for (int64_t v0 = threadIdx.x; v0 < nvec; v0 += blockDim.x) {
+    const Vec16<T> pk = load16(row + v0 * V);
+#pragma unroll
+    for (int j = 0; j < V; ++j) better(to_f32(pk.e[j]), v0 * V + j, best, bi);
+  }
+  for (int64_t c = nvec * V + threadIdx.x; c < width; c += blockDim.x) better(to_f32(row[c]), c, best, bi);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    better(ov, oi, best, bi);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sval[threadIdx.x >> 5] = best;
+    sidx[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) better(sval[w], sidx[w], best, bi);
+  const uint32_t gid = bi == kNone ? kNoId : static_cast<uint32_t>(rank * width + bi);
+  char* mine = p.buf[rank];
+  uint32_t* epochs = reinterpret_cast<uint32_t*>(mine) + p.max_rows;
+  const uint32_t e = epochs[r] + 1u;
+  const int slot = static_cast<int>(e & 1u);
+  for (int q = 0; q < p.tp; ++q)
+    if (q != rank) st_ll2(argmax_words(p.buf[q], p, slot, rank, r), __float_as_uint(best), gid, e);
+  float wv = -INFINITY;
+  int64_t wi = kNone;
+  bool failed = false;
+  for (int src = 0; src < p.tp; ++src) {
+    float v = best;
+    uint32_t id = gid;
+    if (src != rank) {
+      const uint64_t* w = argmax_words(mine, p, slot, src, r);
+      uint64_t a, b;
+      ld_ll2(w, a, b);
+      if (!failed && (static_cast<uint32_t>(a >> 32) != e || static_cast<uint32_t>(b >> 32) != e)) {
+        const uint64_t start = timer_ns();
+        while (true) {
+          ld_ll2(w, a, b);
+          if (static_cast<uint32_t>(a >> 32) == e && static_cast<uint32_t>(b >> 32) == e) break;
+          if (timer_ns() - start > p.timeout_ns) {
+            set_device_error(p.err, kDevErrExchangeTimeout);
+            failed = true;
+            break;
+          }
+        }
+      }
+      v = __uint_as_float(static_cast<uint32_t>(a));
+      id = static_cast<uint32_t>(b);
+    }
+    if (id != kNoId) better(v, id, wv, wi);
+  }
+  out[static_cast<int64_t>(blockIdx.y) * p.rows + r] = wi == kNone ? 0 : wi;
+  epochs[r] = e;
+}
+
 }  // namespace
 }  // namespace dli_sm100
 
@@ -212,9 +306,10 @@ using namespace dli_sm100;
 
 extern "C" size_t dli_sm100_tp_exchange_bytes(int tp, int64_t max_rows, int64_t row_elems, dli_dtype dtype) {
   if (tp < 1 || tp > kMaxRanks || max_rows <= 0 || row_elems <= 0 || !is_float_dtype(dtype)) return 0;
-  // 8-byte words carrying 4 payload bytes each
+  // 8-byte words carrying 4 payload bytes each, then two argmax words per row
   return static_cast<size_t>(header_bytes(max_rows)) +
-         static_cast<size_t>(2) * tp * max_rows * (row_elems * dtype_bytes(dtype) / 4) * 8;
+         static_cast<size_t>(2) * tp * max_rows * (row_elems * dtype_bytes(dtype) / 4) * 8 +
+         static_cast<size_t>(2) * tp * max_rows * 2 * 8;
 }
 
 extern "C" dli_status dli_sm100_tp_exchange_reset(void* buffer, size_t bytes, void* stream) {
@@ -297,6 +392,64 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm(
       void* args[] = {&p, &d, &res, &wt, &nm, &ro};
       cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(allreduce_add_rms_norm_kernel<T>), grid,
                                   dim3(static_cast<unsigned>(threads)), args, 0, as_stream(stream));
+    }
+  });
+  if (st != DLI_OK) return st;
+  return check_launch(name);
+}
+
+extern "C" dli_status dli_sm100_allgather_argmax(void* const* buffers, int tp, int rank, int ranks_in_launch,
+                                                int64_t max_rows, int64_t row_elems, dli_dtype exchange_dtype,
+                                                const void* logits, int64_t rows, int64_t width,
+                                                int64_t rank_stride, int64_t* out_ids, int64_t timeout_ns,
+                                                dli_dtype dtype, void* stream) {
+  const char* name = "allgather_argmax";
+  if (buffers == nullptr || tp < 1 || tp > kMaxRanks || rank < 0 || ranks_in_launch < 1 ||
+      rank + ranks_in_launch > tp || (ranks_in_launch > 1 && rank != 0))
+    return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": bad rank arguments");
+  if (rows < 0 || width <= 0 || max_rows <= 0 || row_elems <= 0 || !is_float_dtype(exchange_dtype))
+    return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": bad sizes");
+  if (static_cast<int64_t>(tp) * width >= 0x7fffffffll)
+    return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": vocabulary beyond 2^31 ids");
+  if (rows == 0) return ok();
+  if (!logits || !out_ids) return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": null pointer");
+  if (rows > max_rows) return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": rows exceed the exchange buffer");
+  if (!is_float_dtype(dtype)) return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": float dtype expected");
+  ExchangeParams p{};
+  for (int i = 0; i < tp; ++i) {
+    if (buffers[i] == nullptr || !aligned(buffers[i], 256))
+      return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": exchange buffers must be 256-byte aligned");
+    p.buf[i] = static_cast<char*>(buffers[i]);
+  }
+  p.tp = tp;
+  p.rank0 = rank;
+  p.max_rows = max_rows;
+  p.row_words = row_elems * static_cast<int64_t>(dtype_bytes(exchange_dtype)) / 4;
+  p.rank_stride = rank_stride;
+  p.rows = rows;
+  p.timeout_ns = timeout_ns > 0 ? static_cast<uint64_t>(timeout_ns) : kDefaultTimeoutNs;
+  p.err = device_error_word();
+  constexpr int kThreadsAm = 256;
+  // every CTA of the launch must be resident at once (rank 0's CTA r may wait for rank 1's)
+  int per_sm = 0;
+  dli_status st = dispatch_float(dtype, name, [&](auto tag) {
+    using T = decltype(tag);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, allgather_argmax_kernel<T>, kThreadsAm, 0);
+  });
+  if (st != DLI_OK) return st;
+  if (static_cast<int64_t>(per_sm) * sm_count() < rows * ranks_in_launch)
+    return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": more rows than resident CTAs");
+  const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(ranks_in_launch));
+  st = dispatch_float(dtype, name, [&](auto tag) {
+    using T = decltype(tag);
+    const T* x = static_cast<const T*>(logits);
+    if (ranks_in_launch == 1) {
+      launch_pdl(allgather_argmax_kernel<T>, grid, dim3(kThreadsAm), 0, as_stream(stream), p, x, width, out_ids);
+    } else {
+      // one cooperative launch over all ranks of the group: co-resident CTAs
+      void* args[] = {&p, &x, &width, &out_ids};
+      cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(allgather_argmax_kernel<T>), grid, dim3(kThreadsAm),
+                                  args, 0, as_stream(stream));
     }
   });
   if (st != DLI_OK) return st;

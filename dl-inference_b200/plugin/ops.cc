@@ -7,7 +7,7 @@
 // add, mul, silu, relu, softmax, max_pool2d, batch_norm2d, reshape, transpose)
 // plus additive fused operators for the batched Qwen2 graphs (add_rms_norm,
 // silu_mul, qkv_rotary_cache, attention_kvcache, last_token, argmax, cast,
-// all_reduce, all_reduce_add_rms_norm, linear_silu_mul).
+// all_reduce, all_reduce_add_rms_norm, tp_argmax, linear_silu_mul).
 //
 // Every operator validates arity/dtype/shape on the host and throws
 // std::invalid_argument like the reference templates
@@ -731,6 +731,39 @@ class AllReduceAddRmsNormOp final : public dli::Operator {
   }
 };
 
+// tp_argmax: logits [.., width] holding ids [tp_rank*width, (tp_rank+1)*width) of a
+// vocabulary split over the tensor-parallel group -> int64 ids of the row maxima
+// over the whole vocabulary (lowest id on ties). One kernel: local argmax and an
+// exchange of (value, id) candidates through the group's NVLink exchange
+// buffers. With tp_size == 1 it is argmax.
+class TpArgmaxOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "tp_argmax"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
+    arity(in, out, 1, 1, 1, type());
+    floatInputs(in, 1, type());
+    const Tensor& x = *in[0];
+    const std::int64_t width = x.shape().back();
+    const std::int64_t rows = static_cast<std::int64_t>(x.numel()) / width;
+    auto shape = x.shape();
+    shape.pop_back();
+    if (shape.empty()) shape.push_back(1);
+    *out[0] = Tensor::cuda(DType::Int64, shape, x.deviceId());
+    auto* ids = static_cast<std::int64_t*>(out[0]->deviceData());
+    if (ctx.tp_size <= 1) {
+      check(dli_sm100_argmax(dli::ptr(x), ids, rows, width, cdt(x.dtype()), ctx.cuda_stream), type());
+      return;
+    }
+    const Exchange* ex = ctx.communicator ? findExchange(ctx.communicator) : nullptr;
+    if (ex == nullptr || ex->tp != ctx.tp_size || ex->rank != ctx.tp_rank || rows > ex->max_rows)
+      throw std::invalid_argument(type() + ": needs the group's exchange buffers with max_rows >= " +
+                                  std::to_string(rows) + " (dli_sm100_tp_exchange_create)");
+    check(dli_sm100_allgather_argmax(ex->ptrs.data(), ex->tp, ex->rank, 1, ex->max_rows, ex->row_elems, ex->dtype,
+                                     dli::ptr(x), rows, width, 0, ids, 0, cdt(x.dtype()), ctx.cuda_stream),
+          type());
+  }
+};
+
 }  // namespace
 
 extern "C" bool dli_register_operators(dli::OperatorRegistry* registry) {
@@ -762,6 +795,7 @@ extern "C" bool dli_register_operators(dli::OperatorRegistry* registry) {
   reg<CastOp>(registry, "cast");
   reg<AllReduceOp>(registry, "all_reduce");
   reg<AllReduceAddRmsNormOp>(registry, "all_reduce_add_rms_norm");
+  reg<TpArgmaxOp>(registry, "tp_argmax");
   return true;
 }
 

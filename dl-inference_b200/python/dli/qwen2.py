@@ -41,7 +41,10 @@ class Qwen2Runner:
 
     # -- plain engine calls -------------------------------------------------------
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor):
-        """input_ids [B,S] int64, positions [B] int64 (cache row of the first token)."""
+        """input_ids [B,S] int64, positions [B] int64 (cache row of the first token).
+        Returns (logits of the last token, next ids). With tensor parallelism over a
+        vocabulary that divides evenly, the logits are this rank's slice of the
+        vocabulary (ids [rank*V/tp, (rank+1)*V/tp)); the next ids are global."""
         out = self.engine.run(self.graph, {"input_ids": input_ids, "positions": positions})
         return out["logits"], out["next_ids"]
 

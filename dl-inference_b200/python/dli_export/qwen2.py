@@ -104,6 +104,13 @@ def _permute_heads(t: torch.Tensor, heads: int, head_dim: int) -> torch.Tensor:
 GLU_BLOCK = 64
 
 
+def vocab_parallel(shape: "Qwen2Shape", tp_size: int) -> bool:
+    """With tensor parallelism the LM head is split by vocabulary rows (each rank
+    streams V/tp rows per token and a tp_argmax node picks the global id), when
+    the vocabulary divides evenly; otherwise it is replicated."""
+    return tp_size > 1 and shape.vocab % tp_size == 0
+
+
 def glu_blocked(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
     """[I, K] gate and up weights -> the layout of the fused `linear_silu_mul`
     operator: 64-row blocks, rows [128b, 128b+64) = gate rows [64b, 64b+64) and
@@ -167,7 +174,11 @@ def transform_weights(state: dict[str, torch.Tensor], shape: Qwen2Shape, tp_size
     if full:
         out["norm"] = cast(state["model.norm.weight"])
         lm = state.get("lm_head.weight")
-        out["lm_head"] = cast(lm if lm is not None else state["model.embed_tokens.weight"])
+        lm = lm if lm is not None else state["model.embed_tokens.weight"]
+        if vocab_parallel(shape, tp_size):  # rank r holds ids [r*V/tp, (r+1)*V/tp)
+            vs = shape.vocab // tp_size
+            lm = lm[tp_rank * vs:(tp_rank + 1) * vs]
+        out["lm_head"] = cast(lm)
     return out
 
 
@@ -218,10 +229,11 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
         delta = f"{L}.d_part"
     node("norm", add_norm, [resid, delta, "norm"], ["normed", "h_out"], {"eps": eps})
     node("last_token", "last_token", ["normed"], ["last_hidden"])
+    # with a vocab-parallel LM head, `logits` is this rank's slice of the vocabulary
     node("lm_head", "linear", ["last_hidden", "lm_head"], ["logits"])
     outputs = ["logits"]
     if with_argmax:
-        node("greedy", "argmax", ["logits"], ["next_ids"])
+        node("greedy", "tp_argmax" if vocab_parallel(shape, tp_size) else "argmax", ["logits"], ["next_ids"])
         outputs.append("next_ids")
     return {"format": "dli.graph.v1", "model_type": model_type, "weights": weights_file,
             "inputs": ["input_ids", "positions"], "outputs": outputs, "nodes": nodes}

@@ -71,6 +71,7 @@ SIGNATURES = {
     "dli_sm100_tp_exchange_bytes": (Z, [D, I, I, D]),
     "dli_sm100_tp_exchange_reset": (N, [P, Z, P]),
     "dli_sm100_allreduce_add_rms_norm": (N, [P, D, D, D, I, I, P, P, P, P, P, I, I, I, F, I, D, P]),
+    "dli_sm100_allgather_argmax": (N, [P, D, D, D, I, I, D, P, I, I, I, P, I, D, P]),
 }
 
 _lib = None
@@ -249,6 +250,19 @@ class ExchangeGroup:
             _dt(delta), _stream())
         check(st, "allreduce_add_rms_norm")
         return normed, residual_out
+
+    def allgather_argmax(self, logits, timeout_ns=0, ranks=None):
+        """logits [tp, rows, width] (rank i holds ids [i*width, (i+1)*width));
+        returns [tp, rows] int64 global argmax ids (the same row on every rank)."""
+        _contig(logits)
+        tp, rows, width = logits.shape
+        ranks = tp if ranks is None else ranks
+        out = torch.empty(tp, rows, dtype=torch.int64, device=logits.device)
+        st = lib().dli_sm100_allgather_argmax(self._ptrs, self.tp, 0, ranks, self.max_rows, self.row_elems,
+                                              DTYPE_CODES[self.dtype], _ptr(logits), rows, width, rows * width,
+                                              _ptr(out), timeout_ns, _dt(logits), _stream())
+        check(st, "allgather_argmax")
+        return out
 
 
 def batch_norm2d(x, weight, bias, running_mean, running_var, eps=1e-5):

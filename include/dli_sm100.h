@@ -300,6 +300,21 @@ dli_status dli_sm100_tp_exchange_reset(void* buffer, size_t bytes, void* stream)
  * residual_out may alias residual. DLI_ERR_UNSUPPORTED when the shape does not
  * fit the exchange buffer or the launch cannot be resident at once (callers
  * then fall back to a library all-reduce + dli_sm100_add_rms_norm). */
+/* Greedy pick over a vocabulary split across the group (vocab-parallel LM head):
+ * rank i holds logits[rows, width] for ids [i*width, (i+1)*width). out_ids[r] =
+ * the id of the largest logit of row r over all ranks, lowest id on ties (the
+ * result dli_sm100_argmax gives over the whole row; 0 for a row without a
+ * candidate). Each CTA pushes its row's (value, id) to every peer as two
+ * epoch-tagged words and polls for theirs (bounded by timeout_ns, 0 = 2 s).
+ * Same buffers, rank arguments and call-order rule as
+ * dli_sm100_allreduce_add_rms_norm; exchange_dtype and row_elems are the
+ * buffers' (they place the candidate words). With ranks_in_launch = tp the
+ * ranks' logits are rank_stride elements apart and out_ids holds tp x rows ids. */
+dli_status dli_sm100_allgather_argmax(void* const* buffers, int tp, int rank, int ranks_in_launch, int64_t max_rows,
+                                      int64_t row_elems, dli_dtype exchange_dtype, const void* logits, int64_t rows,
+                                      int64_t width, int64_t rank_stride, int64_t* out_ids, int64_t timeout_ns,
+                                      dli_dtype dtype, void* stream);
+
 dli_status dli_sm100_allreduce_add_rms_norm(void* const* buffers, int tp, int rank, int ranks_in_launch,
                                             int64_t max_rows, int64_t row_elems, const void* delta,
                                             const void* residual, const void* w, void* normed,

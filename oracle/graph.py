@@ -15,12 +15,15 @@ from . import ops as O
 
 
 class GraphOracle:
-    def __init__(self, graph: dict, constants: dict[str, np.ndarray], all_reduce=None):
+    def __init__(self, graph: dict, constants: dict[str, np.ndarray], all_reduce=None, all_gather=None):
         """all_reduce: callable summing an array over the ranks of a tensor-parallel
-        group (for instance a torch.distributed gloo all_reduce); None = one rank."""
+        group (for instance a torch.distributed gloo all_reduce); all_gather:
+        callable returning the list of every rank's array in rank order; None =
+        one rank."""
         self.graph = graph
         self.constants = constants
         self.all_reduce = all_reduce
+        self.all_gather = all_gather
         self.cache: dict[str, dict[str, np.ndarray]] = {}
 
     def run(self, inputs: dict[str, np.ndarray]) -> dict[str, np.ndarray]:
@@ -57,6 +60,11 @@ class GraphOracle:
             return [np.asarray(x[0])[:, a.get("index", np.asarray(x[0]).shape[1] - 1)]]
         if op == "argmax":
             return [O.argmax(x[0])]
+        if op == "tp_argmax":
+            # vocab-parallel greedy pick: every rank's slice, concatenated in rank order
+            if self.all_gather is None:
+                return [O.argmax(x[0])]
+            return [O.argmax(np.concatenate(self.all_gather(np.asarray(x[0], dtype=np.float64)), -1))]
         if op == "all_reduce_add_rms_norm":
             d = x[1] if self.all_reduce is None else self.all_reduce(np.asarray(x[1]))
             n, r = O.add_rms_norm(x[0], d, x[2], a.get("eps", 1e-6))

@@ -100,3 +100,41 @@ def test_rejects_shapes_beyond_the_exchange_buffer():
     residual, delta, w = _case(2, 16, 1024, torch.bfloat16, 0)
     with pytest.raises(RuntimeError, match="exceed"):
         group.allreduce_add_rms_norm(residual, delta, w)
+
+
+@pytest.mark.parametrize("tp", [2, 4, 8])
+@pytest.mark.parametrize("rows,width", [(32, 152064 // 4), (8, 151936 // 8), (1, 1000), (64, 4096)])
+def test_vocab_parallel_argmax_matches_argmax_over_the_whole_row(tp, rows, width):
+    """dli_sm100_allgather_argmax over a vocabulary split into tp slices equals
+    dli_sm100_argmax over the concatenated row, on every rank, on consecutive
+    calls (epochs advance) that also alternate with all-reduce calls on the same
+    buffers; planted ties across slices must go to the lowest id."""
+    rows = min(rows, 256 // tp)
+    group = C.ExchangeGroup(tp, max_rows=64, row_elems=4096, dtype=torch.bfloat16)
+    g = torch.Generator(device="cuda").manual_seed(tp * 1000 + rows)
+    for step in range(3):
+        logits = torch.randn(tp, rows, width, device="cuda", generator=g).to(torch.bfloat16)
+        if rows > 1:  # the same maximum in the last slice and the first: the first slice's id wins
+            logits[:, 1, :] = -1.0
+            logits[tp - 1, 1, 5] = 7.0
+            logits[0, 1, 3] = 7.0
+        got = group.allgather_argmax(logits)
+        full = logits.permute(1, 0, 2).reshape(rows, tp * width).contiguous()
+        ref = C.argmax(full)
+        torch.cuda.synchronize()
+        for k in range(tp):
+            assert torch.equal(got[k], ref), (step, k)
+        if rows > 1:
+            assert int(got[0, 1]) == 3
+        # an all-reduce on the same buffers between the argmax calls
+        residual, delta, w = _case(tp, min(rows, 4), 1024, torch.bfloat16, step)
+        group.allreduce_add_rms_norm(residual, delta, w)
+    C.check_device_error()
+
+
+def test_vocab_parallel_argmax_missing_peer_times_out():
+    group = C.ExchangeGroup(2, max_rows=8, row_elems=1024, dtype=torch.bfloat16)
+    logits = torch.randn(2, 4, 512, device="cuda").to(torch.bfloat16)
+    group.allgather_argmax(logits, timeout_ns=50_000_000, ranks=1)
+    with pytest.raises(RuntimeError, match="exchange"):
+        C.check_device_error()

@@ -1,9 +1,11 @@
 """CPU tests of the multi-rank host logic: the tensor-parallel x data-parallel
 layout that bench.py and Qwen2Runner use, and the sharded Qwen2 graph run
 rank by rank as separate gloo processes (world size 2 and 4). A real
-torch.distributed all_reduce stands in for the NCCL all_reduce operator; each
-rank's logits must equal the single-rank graph's logits for its share of
-the batch (float64 oracle, so the only difference is summation order)."""
+torch.distributed all_reduce stands in for the NCCL all_reduce operator and an
+all_gather for the vocab-parallel greedy pick; each rank's logits must equal
+the single-rank graph's logits for its share of the batch and its slice of the
+vocabulary, and every rank's next ids the single-rank ids (float64 oracle, so
+the only difference is summation order)."""
 from __future__ import annotations
 
 import socket
@@ -49,14 +51,15 @@ def _inputs():
     return ids, nxt
 
 
-def _oracle(tp, tp_rank, all_reduce=None):
+def _oracle(tp, tp_rank, all_reduce=None, all_gather=None):
     from oracle.graph import GraphOracle
 
     st = random_state(TINY, dtype=torch.float32, seed=5, std=0.2)
     w = {k: v.double().numpy() for k, v in transform_weights(st, TINY, tp, tp_rank).items()}
     cos, sin = rotary_tables(TINY, CAP)
     w["rotary_cos"], w["rotary_sin"] = cos.double().numpy(), sin.double().numpy()
-    return GraphOracle(build_graph(TINY, capacity=CAP, tp_size=tp), w, all_reduce=all_reduce)
+    return GraphOracle(build_graph(TINY, capacity=CAP, tp_size=tp), w, all_reduce=all_reduce,
+                       all_gather=all_gather)
 
 
 def _run(o, ids, nxt):
@@ -81,16 +84,23 @@ def _rank_main(rank, world, port, max_tp, out_dir):
             calls.append(t.numel())
             return t.numpy()
 
+        def all_gather(a):
+            t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float64))
+            parts = [torch.empty_like(t) for _ in range(lay.tp)]
+            dist.all_gather(parts, t, group=pg)
+            return [x.numpy() for x in parts]
+
         ids, nxt = _inputs()
         bl = lay.local_batch(BATCH)
         rows = slice(lay.group * bl, (lay.group + 1) * bl)
-        o = _oracle(lay.tp, lay.tp_rank, all_reduce if lay.tp > 1 else None)
+        tp_hooks = (all_reduce, all_gather) if lay.tp > 1 else (None, None)
+        o = _oracle(lay.tp, lay.tp_rank, *tp_hooks)
         pre, dec, next_ids = _run(o, ids[rows], nxt[rows])
         # the bench's timing rule: every rank's time, max over ranks
         t = torch.tensor([float(rank + 1)])
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         np.savez(f"{out_dir}/rank{rank}.npz", pre=pre, dec=dec, next_ids=next_ids, tp=lay.tp,
-                 group=lay.group, calls=len(calls), tmax=t.item())
+                 tp_rank=lay.tp_rank, group=lay.group, calls=len(calls), tmax=t.item())
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -110,11 +120,14 @@ def test_sharded_graph_over_gloo_matches_single_rank(tmp_path, world, max_tp):
     ref_pre, ref_dec, ref_next = _run(_oracle(1, 0), ids, nxt)
     for r in range(world):
         res = np.load(tmp_path / f"rank{r}.npz")
-        tp, group = int(res["tp"]), int(res["group"])
+        tp, group, tp_rank = int(res["tp"]), int(res["group"]), int(res["tp_rank"])
         bl = BATCH // (world // tp)
         rows = slice(group * bl, (group + 1) * bl)
-        np.testing.assert_allclose(res["pre"], ref_pre[rows], rtol=1e-10, atol=1e-12)
-        np.testing.assert_allclose(res["dec"], ref_dec[rows], rtol=1e-10, atol=1e-12)
+        # vocab-parallel LM head: each rank holds its slice of the logits
+        vs = TINY.vocab // tp
+        cols = slice(tp_rank * vs, (tp_rank + 1) * vs)
+        np.testing.assert_allclose(res["pre"], ref_pre[rows][:, cols], rtol=1e-10, atol=1e-12)
+        np.testing.assert_allclose(res["dec"], ref_dec[rows][:, cols], rtol=1e-10, atol=1e-12)
         np.testing.assert_array_equal(res["next_ids"], ref_next[rows])
         # two all_reduce nodes per layer (after o_proj and after down_proj), prefill + decode
         assert int(res["calls"]) == (2 * TINY.layers * 2 if tp > 1 else 0)

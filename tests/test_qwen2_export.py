@@ -63,6 +63,7 @@ def test_graph_structure_per_layer():
     # every add_rms_norm after a row-split projection becomes the all-reduce form
     assert ops2.count("all_reduce_add_rms_norm") == 2 * TINY.layers
     assert "add_rms_norm" not in ops2 and "all_reduce" not in ops2
+    assert ops2[-1] == "tp_argmax" and ops[-1] == "argmax"
     rc = next(n for n in g2["nodes"] if n["op"] == "qkv_rotary_cache")
     assert rc["attrs"]["q_heads"] == 2 and rc["attrs"]["kv_heads"] == 1
 
@@ -166,6 +167,10 @@ def _run_tp(oracles, ids, pos, ref):
         for o, env in zip(oracles, envs):
             n = o.graph["nodes"][idx]
             outs.append(o._op(n["op"], [env[x] for x in n["inputs"]], n.get("attrs", {})))
+        if node["op"] == "tp_argmax":
+            # vocab-parallel greedy pick over every rank's logits slice
+            full = np.concatenate([np.asarray(env[node["inputs"][0]]) for env in envs], -1)
+            outs = [[O.argmax(full)] for _ in envs]
         if node["op"] == "all_reduce_add_rms_norm":
             # sum the partials (input 1) over the ranks, then the residual add + norm
             total = sum(np.asarray(env[node["inputs"][1]]) for env in envs)
@@ -174,5 +179,8 @@ def _run_tp(oracles, ids, pos, ref):
         for env, res in zip(envs, outs):
             for name, val in zip(node["outputs"], res):
                 env[name] = val
+    # vocab-parallel LM head: rank r holds logits columns [r*V/tp, (r+1)*V/tp)
+    logits = np.concatenate([env["logits"] for env in envs], -1)
+    np.testing.assert_allclose(logits, ref, rtol=1e-4, atol=1e-5)
     for env in envs:
-        np.testing.assert_allclose(env["logits"], ref, rtol=1e-4, atol=1e-5)
+        np.testing.assert_array_equal(env["next_ids"], np.argmax(ref, -1))

@@ -5,7 +5,9 @@ Each of two spawned ranks (one per GPU, NCCL process group, 127.0.0.1
 rendezvous) runs a tp=2 Qwen2Runner on its half of the weights, and a tp=1
 runner with the full weights on the same GPU. The all-reduce after o_proj and
 down_proj runs as the fused NVLink exchange kernel for decode-sized rows and as
-NCCL all_reduce + add_rms_norm for prefill. Prefill logits, eager decode
+NCCL all_reduce + add_rms_norm for prefill; the LM head is split by vocabulary
+and the greedy pick exchanges (value, id) candidates (each rank's logits are
+compared with its slice of the single-GPU logits). Prefill logits, eager decode
 logits and CUDA-graph decode ids (the graph captures the NCCL all_reduce) are
 compared: bf16 with a different summation order across ranks, so logits within
 2e-2 relative Frobenius error and at least 90% of teacher-forced greedy ids
@@ -60,8 +62,11 @@ def _rank_main(rank, port, out_dir):
         g = torch.Generator(device=dev).manual_seed(3)
         ids = torch.randint(0, shape.vocab, (4, 40), device=dev, generator=g)
         rel, agree = [], []
+        vs = shape.vocab // 2  # vocab-parallel LM head: this rank's logits columns
+        cols = slice(lay.tp_rank * vs, (lay.tp_rank + 1) * vs)
         lf, nf = full.prefill(ids)
         ls, ns = shard.prefill(ids)
+        lf = lf[:, cols]
         rel.append(((ls.float() - lf.float()).norm() / lf.float().norm()).item())
         agree.append((nf == ns).float().mean().item())
         pos = torch.full((4,), 40, dtype=torch.int64, device=dev)
@@ -69,6 +74,7 @@ def _rank_main(rank, port, out_dir):
         for _ in range(6):  # teacher-forced: both see the single-GPU model's tokens
             lf, nf = full.forward(step_ids, pos)
             ls, ns = shard.forward(step_ids, pos)
+            lf = lf[:, cols]
             rel.append(((ls.float() - lf.float()).norm() / lf.float().norm()).item())
             agree.append((nf == ns).float().mean().item())
             step_ids, pos = nf.view(4, 1), pos + 1
