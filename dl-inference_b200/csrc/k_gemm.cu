@@ -137,6 +137,55 @@ __device__ __forceinline__ void store_glu_t(const TcParams& p, int ti, int grow,
 
 __device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Epilogue of one finished (un-split) accumulator tile for the layouts whose D
+// row lives in one thread: this thread's row `gi`, TMEM columns from `tbase`
+// (its lane quarter), tile column origin j0. RowMajor / Transposed / Nchw go
+// through store_vals; kEpiGlu pairs gate columns c..c+63 with up columns
+// c+64..c+127 of every 128-column block.
+template <typename T, int BN>
+__device__ __forceinline__ void epilogue_tile(const TcParams& p, uint32_t tbase, int64_t gi, int j0) {
+  if (p.epilogue == kEpiGlu) {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 128) {
+#pragma unroll 1
+      for (int h = 0; h < 64; h += 32) {
+        uint32_t rg[32], ru[32];
+        tmem_ld_32x32b_x32(tbase + c + h, rg);
+        tmem_ld_32x32b_x32(tbase + c + 64 + h, ru);
+        tmem_ld_wait();
+        const int64_t oc = (static_cast<int64_t>(j0) + c) / 2 + h;
+        if (gi < p.rows_a && oc < p.glu_cols) {
+          T* dst = static_cast<T*>(p.out) + gi * p.ldo + oc;
+          if (p.out_vec && (p.ldo % 8) == 0 && oc + 32 <= p.glu_cols) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              Vec16<T> pack;
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                pack.e[e] = glu_val<T>(__uint_as_float(rg[q * 8 + e]), __uint_as_float(ru[q * 8 + e]));
+              store16(dst + q * 8, pack);
+            }
+          } else {
+            for (int k = 0; k < 32 && oc + k < p.glu_cols; ++k)
+              dst[k] = glu_val<T>(__uint_as_float(rg[k]), __uint_as_float(ru[k]));
+          }
+        }
+      }
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tbase + c, r);
+    tmem_ld_wait();
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
+    if (j0 + c < p.rows_b) store_vals<T>(p, gi, j0 + c, v, 32);
+  }
+}
+
 template <typename T, int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tcgen05_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -279,46 +328,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         epilogue_bar();
       }
-    } else if (!aborted && p.splits == 1 && p.epilogue == kEpiGlu) {
-      // this thread's token row; columns hold 64-wide gate/up blocks
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 128) {
-#pragma unroll 1
-        for (int h = 0; h < 64; h += 32) {
-          uint32_t rg[32], ru[32];
-          tmem_ld_32x32b_x32(tbase + c + h, rg);
-          tmem_ld_32x32b_x32(tbase + c + 64 + h, ru);
-          tmem_ld_wait();
-          const int64_t oc = (static_cast<int64_t>(j0) + c) / 2 + h;
-          if (gi < p.rows_a && oc < p.glu_cols) {
-            T* dst = static_cast<T*>(p.out) + gi * p.ldo + oc;
-            if (p.out_vec && (p.ldo % 8) == 0 && oc + 32 <= p.glu_cols) {
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                Vec16<T> pack;
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                  pack.e[e] = glu_val<T>(__uint_as_float(rg[q * 8 + e]), __uint_as_float(ru[q * 8 + e]));
-                store16(dst + q * 8, pack);
-              }
-            } else {
-              for (int k = 0; k < 32 && oc + k < p.glu_cols; ++k)
-                dst[k] = glu_val<T>(__uint_as_float(rg[k]), __uint_as_float(ru[k]));
-            }
-          }
-        }
-      }
     } else if (!aborted && p.splits == 1) {
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + c, r);
-        tmem_ld_wait();
-        float v[32];
-#pragma unroll
-        for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
-        if (j0 + c < p.rows_b) store_vals<T>(p, gi, j0 + c, v, 32);
-      }
+      epilogue_tile<T, BN>(p, tbase, gi, j0);
     } else if (p.splits > 1) {
       // Split-K: stage this CTA's fp32 partial tile in its own shared memory
       // (the operand ring is idle: every load was consumed before acc_full).
@@ -407,6 +418,164 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// ---- persistent tcgen05 GEMM (prefill-sized problems) --------------------------
+// One CTA per SM walks tiles blockIdx.x, +gridDim.x, ... (grouped raster). The
+// accumulator is double-buffered in tensor memory (2 x 256 columns = all 512):
+// while the epilogue warps drain tile n from one buffer, the MMA warp already
+// accumulates tile n+1 into the other, and the producer streams its operands,
+// so tile epilogues no longer stall the tensor pipe. acc_full[b] (MMA ->
+// epilogue, tcgen05.commit) and acc_empty[b] (4 epilogue warps -> MMA) hand the
+// buffers over; the operand ring runs across tile boundaries.
+template <int STAGES>
+struct PersistentLayout {
+  static constexpr int BN = 256;
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kBytes = kBarOffset + (2 * STAGES + 4) * 8 + 16 + 1024;
+};
+
+template <typename T, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    tcgen05_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                   const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
+  using L = PersistentLayout<STAGES>;
+  constexpr int BN = L::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = p.tiles_i * p.tiles_j;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrive per epilogue warp
+    }
+    flags[0] = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      pdl_wait();
+      pdl_trigger();
+      int it = 0;
+      bool stop = false;
+      for (int tile = blockIdx.x; tile < tiles && !stop; tile += gridDim.x) {
+        int ti, tj;
+        tile_coords(tile, p.tiles_i, p.tiles_j, ti, tj);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1)) {
+            set_device_error(p.err, kDevErrGemmTimeout);
+            flags[0] = 1;
+          }
+          if (flags[0]) {
+            stop = true;
+            break;
+          }
+          uint8_t* sa = smem + s * L::kStageBytes;
+          mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+          tma_load_2d(sa, &tmap_a, kb * kBK, ti * kBM, &full[s]);
+          tma_load_2d(sa + L::kABytes, &tmap_b, kb * kBK, tj * BN, &full[s]);
+          ++it;
+        }
+      }
+      // No bulk copy may still be writing shared memory when the CTA exits.
+      for (int j = max(0, it - STAGES); j < it; ++j) mbar_wait(&full[j % STAGES], (j / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, BN);
+      int it = 0, lt = 0;
+      bool stop = false;
+      for (int tile = blockIdx.x; tile < tiles && !stop; tile += gridDim.x, ++lt) {
+        const int buf = lt & 1;
+        if (!mbar_wait(&acc_empty[buf], ((lt >> 1) & 1) ^ 1) || flags[0]) {
+          set_device_error(p.err, kDevErrGemmTimeout);
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem_base + static_cast<uint32_t>(buf * BN);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph)) {
+            set_device_error(p.err, kDevErrGemmTimeout);
+            flags[0] = 1;
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
+          const uint64_t adesc = umma_desc_sw128(a_addr);
+          const uint64_t bdesc = umma_desc_sw128(a_addr + L::kABytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+          ++it;
+        }
+        umma_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
+      const int buf = lt & 1;
+      if (!mbar_wait(&acc_full[buf], (lt >> 1) & 1)) {
+        set_device_error(p.err, kDevErrGemmTimeout);
+        flags[0] = 1;
+      }
+      tc_fence_after();
+      epilogue_bar();  // every epilogue warp sees the same abort flag
+      if (flags[0]) break;
+      int ti, tj;
+      tile_coords(tile, p.tiles_i, p.tiles_j, ti, tj);
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      epilogue_tile<T, BN>(p, tbase, static_cast<int64_t>(ti) * kBM + row, tj * BN);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
   }
 }
 
@@ -529,6 +698,27 @@ dli_status launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcParam
   launch_pdl_cluster(kernel, grid, dim3(kGemmThreads), L::kBytes, stream,
                      static_cast<unsigned>(splits), ma, mb, p);
   return check_launch("tcgen05 gemm");
+}
+
+template <typename T>
+dli_status launch_tc_persistent(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p,
+                                cudaStream_t stream) {
+  using L = PersistentLayout<4>;
+  auto kernel = tcgen05_gemm_persistent_kernel<T, 4>;
+  const dli_status st = ensure_smem(reinterpret_cast<const void*>(kernel), L::kBytes, "tcgen05 gemm");
+  if (st != DLI_OK) return st;
+  const int tiles = p.tiles_i * p.tiles_j;
+  dim3 grid(static_cast<unsigned>(std::min(tiles, sm_count())));
+  launch_pdl(kernel, grid, dim3(kGemmThreads), L::kBytes, stream, ma, mb, p);
+  return check_launch("tcgen05 gemm");
+}
+
+// Persistent double-buffered kernel for many-tile, un-split, row-per-thread
+// epilogues (prefill projections, conv); DLI_SM100_GEMM_PERSISTENT=0 disables it.
+bool use_persistent(const GemmPlan& plan, int epilogue) {
+  static const bool on = tuning_knob("GEMM_PERSISTENT", 1) != 0;
+  return on && plan.bn == 256 && plan.splits == 1 && epilogue != kEpiTransposed && epilogue != kEpiGluT &&
+         static_cast<int64_t>(plan.tiles_i) * plan.tiles_j > sm_count();
 }
 
 template <typename T>
@@ -697,6 +887,8 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
   p.const_a = const_a ? 1 : 0;
   p.const_b = const_b ? 1 : 0;
   p.glu_cols = static_cast<int>(glu_cols);
+  if (use_persistent(plan, epilogue))
+    return bf16 ? launch_tc_persistent<__nv_bfloat16>(ma, mb, p, stream) : launch_tc_persistent<__half>(ma, mb, p, stream);
   if (bf16) return launch_tc_bn<__nv_bfloat16>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
   return launch_tc_bn<__half>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
 }
