@@ -37,7 +37,6 @@ namespace dli_sm100 {
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr int kVpt = 4;                    // 16-byte vectors per thread
 constexpr int64_t kHeaderAlign = 4096;
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;
 
@@ -112,7 +111,10 @@ __device__ __forceinline__ uint4 wait_ll4(const uint64_t* p, uint32_t e, uint64_
                     static_cast<uint32_t>(w3));
 }
 
-template <typename T>
+// VPT 16-byte vectors per thread: the host picks the smallest VPT that fits the
+// row in 512 threads, so as many threads as possible issue the peer stores (one
+// thread's remote stores drain slowly; the push is throughput-bound per thread).
+template <typename T, int kVpt>
 __global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
     ExchangeParams p, const T* __restrict__ delta, const T* residual /* may alias residual_out */,
     const T* __restrict__ w, T* __restrict__ normed, T* residual_out) {
@@ -343,8 +345,7 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm(
   if (ranks_in_launch > 1 && rank_stride % V != 0)
     return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": rank_stride must be a multiple of 16 bytes");
   const int64_t lanes = hidden / V;
-  const int64_t threads = std::max<int64_t>(64, ceil_div(ceil_div(lanes, kVpt), 32) * 32);
-  if (threads > 512) return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": hidden too large");
+  if (ceil_div(lanes, 4) > 512) return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": hidden too large");
   for (const void* ptr : {delta, residual, w, static_cast<const void*>(normed), static_cast<const void*>(residual_out)})
     if (!aligned(ptr, 16)) return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": 16-byte aligned tensors expected");
 
@@ -366,32 +367,47 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm(
   p.err = device_error_word();
 
   // Every CTA of the launch must be resident at once: rank 0's CTA r may wait
-  // for rank 1's CTA r, in this launch (several ranks on one device) or on a peer.
-  int per_sm = 0;
-  dli_status st = dispatch_float(dtype, name, [&](auto tag) {
-    using T = decltype(tag);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, allreduce_add_rms_norm_kernel<T>,
-                                                  static_cast<int>(threads), 0);
-  });
-  if (st != DLI_OK) return st;
-  if (static_cast<int64_t>(per_sm) * sm_count() < rows * ranks_in_launch)
-    return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": more rows than resident CTAs");
+  // for rank 1's CTA r, in this launch (several ranks on one device) or on a
+  // peer. Fewest vectors per thread (most threads storing to the peers) first;
+  // more per thread when that many CTAs would not all be resident.
+  int vpt = 0;
+  int64_t threads = 0;
+  dli_status st = DLI_OK;
+  for (const int cand : {1, 2, 4}) {
+    const int64_t th = std::max<int64_t>(64, ceil_div(ceil_div(lanes, cand), 32) * 32);
+    if (th > 512) continue;
+    int per_sm = 0;
+    st = dispatch_float(dtype, name, [&](auto tag) {
+      using T = decltype(tag);
+      auto kern = cand == 1 ? allreduce_add_rms_norm_kernel<T, 1>
+                            : (cand == 2 ? allreduce_add_rms_norm_kernel<T, 2> : allreduce_add_rms_norm_kernel<T, 4>);
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, static_cast<int>(th), 0);
+    });
+    if (st != DLI_OK) return st;
+    if (static_cast<int64_t>(per_sm) * sm_count() >= rows * ranks_in_launch) {
+      vpt = cand;
+      threads = th;
+      break;
+    }
+  }
+  if (vpt == 0) return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": more rows than resident CTAs");
   const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(ranks_in_launch));
   st = dispatch_float(dtype, name, [&](auto tag) {
     using T = decltype(tag);
+    auto kern = vpt == 1 ? allreduce_add_rms_norm_kernel<T, 1>
+                         : (vpt == 2 ? allreduce_add_rms_norm_kernel<T, 2> : allreduce_add_rms_norm_kernel<T, 4>);
+    const T* d = static_cast<const T*>(delta);
+    const T* res = static_cast<const T*>(residual);
+    const T* wt = static_cast<const T*>(w);
+    T* nm = static_cast<T*>(normed);
+    T* ro = static_cast<T*>(residual_out);
     if (ranks_in_launch == 1) {
-      launch_pdl(allreduce_add_rms_norm_kernel<T>, grid, dim3(static_cast<unsigned>(threads)), 0, as_stream(stream), p,
-                 (const T*)delta, (const T*)residual, (const T*)w, (T*)normed, (T*)residual_out);
+      launch_pdl(kern, grid, dim3(static_cast<unsigned>(threads)), 0, as_stream(stream), p, d, res, wt, nm, ro);
     } else {
       // one cooperative launch over all ranks of the group: co-resident CTAs
-      const T* d = static_cast<const T*>(delta);
-      const T* res = static_cast<const T*>(residual);
-      const T* wt = static_cast<const T*>(w);
-      T* nm = static_cast<T*>(normed);
-      T* ro = static_cast<T*>(residual_out);
       void* args[] = {&p, &d, &res, &wt, &nm, &ro};
-      cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(allreduce_add_rms_norm_kernel<T>), grid,
-                                  dim3(static_cast<unsigned>(threads)), args, 0, as_stream(stream));
+      cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kern), grid, dim3(static_cast<unsigned>(threads)),
+                                  args, 0, as_stream(stream));
     }
   });
   if (st != DLI_OK) return st;
