@@ -10,10 +10,11 @@ N(0, 0.02) of the named architecture (no checkpoints: synthetic data).
   python bench.py --impl reference ...     # the reference's CPU path (PyTorch eager)
 
 Multi-GPU (launched by torchrun, one rank per GPU): tensor parallelism over
-tp = min(N, max TP the head counts allow, 4 for 7B) with an NCCL all_reduce
-after o_proj and down_proj; N / tp data-parallel groups split the batch
-(strong scaling: total work fixed). Times are CUDA events on each rank, max
-over ranks.
+tp = min(N, max TP the head counts allow, 4 for 7B) with the all-reduce after
+o_proj and down_proj fused into the next RMSNorm (NVLink exchange kernel for
+decode rows, NCCL for prefill) and a vocabulary-split LM head; N / tp
+data-parallel groups split the batch (strong scaling: total work fixed). Times
+are CUDA events on each rank, max over ranks.
 
 Printed JSON (rank 0): value = decode tok/s of the whole job; prefill tok/s,
 e2e (decode through the public API with host ids in and out every token),
