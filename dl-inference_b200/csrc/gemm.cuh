@@ -38,8 +38,8 @@ GemmPlan plan_tn_gemm(int64_t rows_a, int64_t rows_b, int64_t k, dli_dtype dtype
 // `ldo` is the output row stride (elements); `ohw` is used by kEpiNchw.
 // `const_a` / `const_b` mark an operand that no kernel writes (weights): its
 // first tiles are fetched before the kernel waits on the previous kernel.
-// Split-K plans need a workspace whose ticket words are zero on entry (the
-// kernel leaves them zero).
+// Split-K plans reduce inside a thread-block cluster and need no workspace
+// (the arguments are kept for plans that would).
 dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, void* out,
                                int64_t rows_a, int64_t rows_b, int64_t k, int64_t lda,
                                int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,

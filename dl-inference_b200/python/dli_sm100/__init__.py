@@ -153,8 +153,7 @@ def linear(x, w, bias=None, out=None):
         raise ValueError("linear: weight K mismatch")
     out = out if out is not None else torch.empty(*x.shape[:-1], n, dtype=x.dtype, device=x.device)
     L = lib()
-    ws_bytes = L.dli_sm100_linear_workspace_size(m, n, k, _dt(x))
-    # split-K tickets must be zero on entry (the kernel leaves them zero)
+    ws_bytes = L.dli_sm100_linear_workspace_size(m, n, k, _dt(x))  # 0 in this build (cluster split-K)
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
     check(L.dli_sm100_linear(_ptr(x), _ptr(w), _ptr(bias), _ptr(out), m, n, k, _dt(x), _ptr(ws),
                              ws_bytes, _stream()), "linear")

@@ -1,5 +1,6 @@
 """Tensor parallelism on two GPUs: the sharded Qwen2 graph with the plugin's
-NCCL all_reduce operator, against the same model on one GPU.
+tensor-parallel operators (fused all-reduce + RMSNorm, vocab-parallel argmax),
+against the same model on one GPU.
 
 Each of two spawned ranks (one per GPU, NCCL process group, 127.0.0.1
 rendezvous) runs a tp=2 Qwen2Runner on its half of the weights, and a tp=1
@@ -8,7 +9,7 @@ down_proj runs as the fused NVLink exchange kernel for decode-sized rows and as
 NCCL all_reduce + add_rms_norm for prefill; the LM head is split by vocabulary
 and the greedy pick exchanges (value, id) candidates (each rank's logits are
 compared with its slice of the single-GPU logits). Prefill logits, eager decode
-logits and CUDA-graph decode ids (the graph captures the NCCL all_reduce) are
+logits and CUDA-graph decode ids (the graph captures the exchange kernels) are
 compared: bf16 with a different summation order across ranks, so logits within
 2e-2 relative Frobenius error and at least 90% of teacher-forced greedy ids
 equal; free-running CUDA-graph generation on two GPUs must equal eager
