@@ -180,6 +180,13 @@ def cpu_baseline(shape, batch: int, prompt: int, seconds: float = 20.0) -> dict:
             "ms_per_step": step_s * 1e3}
 
 
+def workload_config(model: str, batch: int, prompt: int, dsteps: int) -> dict:
+    """The `config` keys both arms report for the same workload."""
+    return {"workload": f"qwen2-{model}: prefill {batch}x{prompt} + {dsteps} greedy decode steps",
+            "model": f"Qwen2-{model.upper()}-shape", "global_batch": batch, "seq_len": prompt,
+            "decode_steps": dsteps}
+
+
 def run_reference_arm(args, world: int, rank: int):
     from dli_export import qwen2 as Q
 
@@ -189,6 +196,7 @@ def run_reference_arm(args, world: int, rank: int):
     shape = getattr(Q, name)
     batch = args.batch or batch
     prompt = args.prompt or prompt
+    dsteps = args.decode or dsteps
     vals = []
     per = max(3.0, 60.0 / max(1, args.steps + args.warmup))
     for i in range(args.warmup + args.steps):
@@ -201,7 +209,9 @@ def run_reference_arm(args, world: int, rank: int):
             "ms_per_step": statistics.median(v["ms_per_step"] for v in vals),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init N(0,0.02) weights, seeded)",
-            "config": {"workload": f"qwen2-{args.model} decode, batch {batch}, {prompt}-token context"},
+            "config": workload_config(args.model, batch, prompt, dsteps) | {
+                "parallelism": "none (host cores)",
+                "reference_sample": f"decode at a {prompt}-token context, one decoder layer timed and scaled"},
             "cpu_baseline": {k: vals[-1][k] for k in ("kind", "cores", "sample")} | {"value": value,
                                                                                      "unit": "tok/s (decode)"},
             "e2e": {"value": value, "unit": "tok/s (decode)", "h2d_bytes_per_step": 0,
@@ -411,9 +421,8 @@ def main() -> int:
             "ms_per_step": (pre_ms + dec_ms) / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random-init N(0,0.02) weights of the named architecture, uniform token ids; seeded)",
-            "config": {"workload": f"qwen2-{args.model}: prefill {batch}x{prompt} + {dsteps} greedy decode steps",
-                       "model": f"Qwen2-{args.model.upper()}-shape", "global_batch": batch,
-                       "seq_len": prompt, "decode_steps": dsteps, "parallelism": f"tp{tp}" + (f"xdp{dp}" if dp > 1 else ""),
+            "config": workload_config(args.model, batch, prompt, dsteps) | {
+                       "parallelism": f"tp{tp}" + (f"xdp{dp}" if dp > 1 else ""),
                        "l2": "inputs larger than L2 (weights stream from HBM every step)",
                        "kv_capacity": capacity},
             "prefill": {"value": prefill_tok_s, "unit": "tok/s (prefill)", "ms_per_step": pre_ms / args.steps},
