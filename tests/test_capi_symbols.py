@@ -41,3 +41,18 @@ def test_abi_version_and_queries_without_gpu():
     # workspace queries are pure host arithmetic
     assert lib.dli_sm100_linear_workspace_size(64, 1024, 4096, 0) == 0  # fp32: no scratch
     assert lib.dli_sm100_attention_workspace_size(1, 4, 4, 8, 8, 7, 2) == 0  # head_dim 7: fallback
+
+
+def test_tp_exchange_buffer_size_is_host_arithmetic():
+    """Exchange buffer bytes: a 4096-aligned header of per-row epochs (all-reduce and
+    argmax), then 2 slots x tp x max_rows rows of 8-byte words carrying 4 payload
+    bytes each, then 2 slots x tp x max_rows argmax candidates of two words."""
+    lib = dli_sm100.lib()
+    tp, rows, elems = 2, 64, 3584
+    header = 4096  # 2 * 64 * 4 bytes of epochs, rounded up to 4096
+    words = 2 * tp * rows * (elems * 2 // 4) * 8
+    argmax = 2 * tp * rows * 2 * 8
+    assert lib.dli_sm100_tp_exchange_bytes(tp, rows, elems, 2) == header + words + argmax
+    assert lib.dli_sm100_tp_exchange_bytes(4, 256, 8192, 0) == 4096 + 2 * 4 * 256 * 8192 * 8 + 2 * 4 * 256 * 16
+    assert lib.dli_sm100_tp_exchange_bytes(9, 64, 3584, 2) == 0  # more than 8 ranks
+    assert lib.dli_sm100_tp_exchange_bytes(2, 64, 3584, 1) == 0  # int64 is not an exchange dtype
