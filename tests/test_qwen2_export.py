@@ -184,3 +184,24 @@ def _run_tp(oracles, ids, pos, ref):
     np.testing.assert_allclose(logits, ref, rtol=1e-4, atol=1e-5)
     for env in envs:
         np.testing.assert_array_equal(env["next_ids"], np.argmax(ref, -1))
+
+
+def test_vocab_parallel_lm_head_shards_recompose():
+    """Under tensor parallelism the LM head is split by vocabulary rows (rank r holds
+    ids [r*V/tp, (r+1)*V/tp)); tied embeddings keep the full table for the lookup.
+    A vocabulary that does not divide evenly keeps a replicated head and argmax."""
+    import dataclasses
+
+    st = random_state(TINY, dtype=torch.float32, seed=4)
+    full = transform_weights(st, TINY, 1, 0)
+    shards = [transform_weights(st, TINY, 2, r) for r in range(2)]
+    torch.testing.assert_close(torch.cat([s["lm_head"] for s in shards]), full["lm_head"])
+    tied = dataclasses.replace(TINY, tie_embeddings=True)
+    st_t = random_state(tied, dtype=torch.float32, seed=4)
+    st_t.pop("lm_head.weight", None)
+    sh = transform_weights(st_t, tied, 2, 1)
+    assert sh["embed"].shape[0] == tied.vocab and sh["lm_head"].shape[0] == tied.vocab // 2
+    torch.testing.assert_close(sh["lm_head"], st_t["model.embed_tokens.weight"][tied.vocab // 2:])
+    odd = dataclasses.replace(TINY, vocab=51)
+    assert [n["op"] for n in build_graph(odd, capacity=32, tp_size=2)["nodes"]][-1] == "argmax"
+    assert transform_weights(random_state(odd, dtype=torch.float32), odd, 2, 0)["lm_head"].shape[0] == 51
