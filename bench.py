@@ -1,4 +1,4 @@
-"""Qwen2 serving benchmark of the sm_100a plugin (BASELINE config: Qwen2-7B shape).
+"""Qwen2 serving benchmark of the sm_100a plugin (default workload: the Qwen2-7B shape).
 
 One "step" = one generation request batch: a causal prefill of B x S prompt
 tokens followed by D greedy decode steps over the KV cache, all through the
@@ -332,6 +332,13 @@ def main() -> int:
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     pre_ms, dec_ms = t.tolist()
+    # A kernel whose bounded wait ran out (or that met an out-of-range index)
+    # returns early and sets the device error word: such a run is not a measurement.
+    try:
+        dli_sm100.check_device_error()
+        device_error = None
+    except RuntimeError as exc:
+        device_error = str(exc)
     total_seqs = b_local * dp
     decode_tok_s = total_seqs * dsteps * args.steps / (dec_ms / 1e3)
     prefill_tok_s = total_seqs * prompt * args.steps / (pre_ms / 1e3)
@@ -446,6 +453,7 @@ def main() -> int:
             "cpu_baseline": cpu,
             "gpu_launches": launches,
             "launches_per_decode_step": launches_decode,
+            "device_error": device_error,
         }
         print(json.dumps(line))
     # graphs holding NCCL launches go before the communicator, which goes before the process group
@@ -457,7 +465,7 @@ def main() -> int:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    return 0
+    return 1 if device_error else 0
 
 
 if __name__ == "__main__":

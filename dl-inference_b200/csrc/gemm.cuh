@@ -45,7 +45,7 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
                                int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,
                                dli_dtype dtype, const GemmPlan& plan, void* workspace,
                                size_t workspace_bytes, cudaStream_t stream, bool const_a,
-                               bool const_b, int64_t glu_cols = 0);
+                               bool const_b, int64_t glu_cols = 0, bool out_f32 = false);
 
 // SIMT fallback (any float dtype, any alignment): out[M,N] = A[M,K] . B + bias,
 // with B given as [N,K] (b_kmajor) or [K,N].

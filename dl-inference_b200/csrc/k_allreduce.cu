@@ -347,7 +347,10 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm(
   const int64_t lanes = hidden / V;
   if (ceil_div(lanes, 4) > 512) return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": hidden too large");
   for (const void* ptr : {delta, residual, w, static_cast<const void*>(normed), static_cast<const void*>(residual_out)})
-    if (!aligned(ptr, 16)) return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": 16-byte aligned tensors expected");
+    // A per-rank property, so a hard error: DLI_ERR_UNSUPPORTED is reserved for
+    // shape checks, which give the same answer on every rank of the group (a
+    // caller that falls back to a library all-reduce on it stays in step).
+    if (!aligned(ptr, 16)) return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": 16-byte aligned tensors expected");
 
   ExchangeParams p{};
   for (int i = 0; i < tp; ++i) {

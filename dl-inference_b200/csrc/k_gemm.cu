@@ -60,6 +60,7 @@ struct TcParams {
   int const_a;  // operand A is read-only weights: its first tiles load before pdl_wait
   int const_b;  // same for operand B
   int glu_cols; // SwiGLU epilogues: valid output columns (the intermediate size)
+  int out_f32;  // RowMajor / Transposed: the output is float32 (operands stay T)
   const void* bias;
   void* out;
   unsigned* err;
@@ -83,6 +84,16 @@ __device__ __forceinline__ void store_vals(const TcParams& p, int64_t gi, int jc
   const T* bias = static_cast<const T*>(p.bias);
   T* out = static_cast<T*>(p.out);
   if (gi >= p.rows_a) return;
+  if (p.out_f32) {  // fp32 output (logits): the accumulator is stored unrounded
+    float* outf = static_cast<float*>(p.out);
+    const bool tr = p.epilogue == kEpiTransposed;
+    const float bt = (tr && bias) ? to_f32(bias[gi]) : 0.f;
+    for (int k = 0; k < n && jc + k < p.rows_b; ++k) {
+      const float bv = tr ? bt : (bias ? to_f32(bias[jc + k]) : 0.f);
+      outf[tr ? static_cast<int64_t>(jc + k) * p.ldo + gi : gi * p.ldo + jc + k] = v[k] + bv;
+    }
+    return;
+  }
   if (p.epilogue == kEpiRowMajor) {
     T* dst = out + gi * p.ldo + jc;
     if (n == 32 && p.out_vec && jc + 32 <= p.rows_b && (p.ldo % 8) == 0) {
@@ -858,8 +869,10 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
                                int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,
                                dli_dtype dtype, const GemmPlan& plan, void* workspace,
                                size_t workspace_bytes, cudaStream_t stream, bool const_a,
-                               bool const_b, int64_t glu_cols) {
+                               bool const_b, int64_t glu_cols, bool out_f32) {
   if (!plan.tcgen05) return fail(DLI_ERR_UNSUPPORTED, "gemm: shape not served by tcgen05");
+  if (out_f32 && epilogue != kEpiRowMajor && epilogue != kEpiTransposed)
+    return fail(DLI_ERR_UNSUPPORTED, "gemm: float32 output only for plain row-major/transposed epilogues");
   if (!aligned(a, 16) || !aligned(b, 16) || lda % 8 != 0 || ldb % 8 != 0)
     return fail(DLI_ERR_UNSUPPORTED, "gemm: TMA needs 16-byte aligned operands and row strides");
   (void)workspace;
@@ -887,6 +900,7 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
   p.const_a = const_a ? 1 : 0;
   p.const_b = const_b ? 1 : 0;
   p.glu_cols = static_cast<int>(glu_cols);
+  p.out_f32 = out_f32 ? 1 : 0;
   if (use_persistent(plan, epilogue))
     return bf16 ? launch_tc_persistent<__nv_bfloat16>(ma, mb, p, stream) : launch_tc_persistent<__half>(ma, mb, p, stream);
   if (bf16) return launch_tc_bn<__nv_bfloat16>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
@@ -945,6 +959,27 @@ extern "C" dli_status dli_sm100_linear(const void* x, const void* w, const void*
                                workspace, workspace_bytes, as_stream(stream), false, true);
   }
   return run_gemm_simt(x, w, bias, y, m, n, k, true, dtype, as_stream(stream));
+}
+
+extern "C" dli_status dli_sm100_linear_ex(const void* x, const void* w, const void* bias, void* y, int64_t m,
+                                          int64_t n, int64_t k, dli_dtype dtype, dli_dtype out_dtype,
+                                          void* stream) {
+  if (out_dtype == dtype) return dli_sm100_linear(x, w, bias, y, m, n, k, dtype, nullptr, 0, stream);
+  if (m < 0 || n <= 0 || k <= 0) return fail(DLI_ERR_INVALID_ARGUMENT, "linear_ex: bad sizes");
+  if ((dtype != DLI_DTYPE_BF16 && dtype != DLI_DTYPE_F16) || out_dtype != DLI_DTYPE_F32)
+    return fail(DLI_ERR_UNSUPPORTED, "linear_ex: only bfloat16/float16 operands with a float32 output");
+  if (m == 0) return ok();
+  if (!x || !w || !y) return fail(DLI_ERR_INVALID_ARGUMENT, "linear_ex: null pointer");
+  if (!aligned(x, 16) || !aligned(w, 16) || k % 8 != 0)
+    return fail(DLI_ERR_UNSUPPORTED, "linear_ex: 16-byte aligned operands and K % 8 == 0 expected");
+  const bool swap = m <= kSwapRows;
+  const GemmPlan plan = swap ? plan_tn_gemm(n, m, k, dtype, true) : plan_tn_gemm(m, n, k, dtype, true);
+  if (!plan.tcgen05) return fail(DLI_ERR_UNSUPPORTED, "linear_ex: shape not served by tcgen05");
+  if (swap)
+    return run_tn_gemm_tcgen05(w, x, bias, y, n, m, k, k, k, n, kEpiTransposed, 0, dtype, plan, nullptr, 0,
+                               as_stream(stream), true, false, 0, true);
+  return run_tn_gemm_tcgen05(x, w, bias, y, m, n, k, k, k, n, kEpiRowMajor, 0, dtype, plan, nullptr, 0,
+                             as_stream(stream), false, true, 0, true);
 }
 
 extern "C" dli_status dli_sm100_linear_silu_mul(const void* x, const void* w_glu, void* y, int64_t m,

@@ -102,7 +102,7 @@ class LinearOp final : public dli::Operator {
 
  public:
   std::string type() const override { return "linear"; }
-  void compute(const Inputs& in, const Outputs& out, const Attributes&, ExecutionContext& ctx) const override {
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
     arity(in, out, 2, 3, 1, type());
     floatInputs(in, in.size(), type());
     const Tensor& x = *in[0];
@@ -115,8 +115,19 @@ class LinearOp final : public dli::Operator {
     const std::int64_t m = dli::product(x.shape(), 0, x.rank() - 1);
     auto shape = x.shape();
     shape.back() = n;
-    *out[0] = Tensor::cuda(x.dtype(), shape, x.deviceId());
+    // Additive attribute: out_dtype = "float32" keeps the fp32 accumulator of a
+    // bfloat16/float16 linear (LM-head logits ranked by argmax).
+    const DType out_dt = attrs.contains("out_dtype")
+                             ? dli::dtypeFromString(attrs.require<std::string>("out_dtype"))
+                             : x.dtype();
+    *out[0] = Tensor::cuda(out_dt, shape, x.deviceId());
     const dli_dtype dt = cdt(x.dtype());
+    if (out_dt != x.dtype()) {
+      check(dli_sm100_linear_ex(dli::ptr(x), dli::ptr(w), in.size() == 3 ? dli::ptr(*in[2]) : nullptr,
+                                out[0]->deviceData(), m, n, k, dt, cdt(out_dt), ctx.cuda_stream),
+            type());
+      return;
+    }
     const std::size_t need = dli_sm100_linear_workspace_size(m, n, k, dt);
     if (need > wsBytes(ws_) || (ws_.defined() && ws_.device().index() != x.deviceId()))
       ws_ = at::zeros({static_cast<std::int64_t>(need)},
@@ -680,8 +691,9 @@ const Exchange* findExchange(void* comm) {
 // The tensor-parallel form of add_rms_norm. With an exchange buffer registered
 // for the run's communicator and rows that fit it, one fused kernel does the
 // all-reduce over NVLink peer memory and the norm; otherwise (prefill-sized
-// rows, no buffer) an NCCL all_reduce followed by add_rms_norm. Both branches
-// depend only on shapes, so every rank of the group takes the same one.
+// rows, no buffer) an NCCL all_reduce followed by add_rms_norm. The kernel
+// answers DLI_ERR_UNSUPPORTED for shape reasons only, so every rank of the group
+// takes the same branch; a per-rank problem (alignment) is a thrown error.
 class AllReduceAddRmsNormOp final : public dli::Operator {
  public:
   std::string type() const override { return "all_reduce_add_rms_norm"; }

@@ -48,6 +48,18 @@ class Qwen2Runner:
         out = self.engine.run(self.graph, {"input_ids": input_ids, "positions": positions})
         return out["logits"], out["next_ids"]
 
+    def check_device_error(self) -> None:
+        """Raises RuntimeError when a kernel of this process reported an error
+        through the device error word: a bounded wait that ran out (a
+        tensor-parallel peer that never arrived, a tensor-core pipeline stall) or
+        an out-of-range id or position. Such a kernel returns early, so the
+        outputs of the run are not valid. Synchronises the current stream. After
+        an exchange timeout every rank must reset its exchange buffer
+        (dli_sm100_tp_exchange_reset) before the group runs again."""
+        import dli_sm100
+
+        dli_sm100.check_device_error()
+
     def reset(self) -> None:
         """Forgets cached sequences (rows are rewritten by position, so nothing to clear)."""
         self.engine.kv_cache_reset()
@@ -114,4 +126,5 @@ class Qwen2Runner:
                 out[:, t] = nxt
                 ids = nxt.view(b, 1)
                 pos = pos + 1
+        self.check_device_error()
         return out

@@ -183,11 +183,15 @@ def transform_weights(state: dict[str, torch.Tensor], shape: Qwen2Shape, tp_size
 
 
 def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: str = "qwen2",
-                weights_file: str = "", with_argmax: bool = True, fused_glu: bool = True) -> dict[str, Any]:
+                weights_file: str = "", with_argmax: bool = True, fused_glu: bool = True,
+                logits_dtype: str | None = "float32") -> dict[str, Any]:
     """dli.graph.v1 dict for one rank. Inputs: input_ids [B,S] int64, positions [B]
     int64, rotary_cos/rotary_sin, and the weights of transform_weights() (made
     with the same `fused_glu`: one linear_silu_mul node instead of linear +
-    silu_mul; the fused operator serves bfloat16/float16)."""
+    silu_mul; the fused operator serves bfloat16/float16). `logits_dtype` sets
+    the LM head's output type: "float32" keeps the fp32 accumulator, so greedy
+    ids are not decided among logits that rounding to bf16 made equal; None
+    writes the weights' dtype."""
     hq, hkv, d = shape.q_heads // tp_size, shape.kv_heads // tp_size, shape.head_dim
     nodes: list[dict[str, Any]] = []
 
@@ -230,7 +234,8 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
     node("norm", add_norm, [resid, delta, "norm"], ["normed", "h_out"], {"eps": eps})
     node("last_token", "last_token", ["normed"], ["last_hidden"])
     # with a vocab-parallel LM head, `logits` is this rank's slice of the vocabulary
-    node("lm_head", "linear", ["last_hidden", "lm_head"], ["logits"])
+    node("lm_head", "linear", ["last_hidden", "lm_head"], ["logits"],
+         {"out_dtype": logits_dtype} if logits_dtype else None)
     outputs = ["logits"]
     if with_argmax:
         node("greedy", "tp_argmax" if vocab_parallel(shape, tp_size) else "argmax", ["logits"], ["next_ids"])

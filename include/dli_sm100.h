@@ -78,6 +78,15 @@ dli_status dli_sm100_linear(const void* x, const void* w, const void* bias, void
                             int64_t n, int64_t k, dli_dtype dtype, void* workspace,
                             size_t workspace_bytes, void* stream);
 
+/* linear with a wider output type: y[M,N] (out_dtype) = x[M,K] · w[N,K]^T (+ bias[N]),
+ * x, w and bias in `dtype`. Serves BF16/F16 operands with an F32 output (the
+ * fp32 accumulator stored without rounding to bf16), used for the LM-head logits
+ * that greedy decoding takes the argmax of; out_dtype == dtype is
+ * dli_sm100_linear. Additive: the reference's linear (python/dli_ops/aot/linear/
+ * template.cc:14-34) always writes its input dtype, fp32. */
+dli_status dli_sm100_linear_ex(const void* x, const void* w, const void* bias, void* y, int64_t m,
+                               int64_t n, int64_t k, dli_dtype dtype, dli_dtype out_dtype, void* stream);
+
 /* Fused gate/up projection + SwiGLU (additive; the reference graph runs
  * linear -> silu -> mul): y[M, inter] = silu(x · Wg^T) * (x · Wu^T), rounded like
  * the unfused nodes (each linear output, the silu output and the product in
@@ -299,7 +308,14 @@ dli_status dli_sm100_tp_exchange_reset(void* buffer, size_t bytes, void* stream)
  *   rows <= max_rows, hidden <= row_elems, hidden * element size a multiple of 16
  * residual_out may alias residual. DLI_ERR_UNSUPPORTED when the shape does not
  * fit the exchange buffer or the launch cannot be resident at once (callers
- * then fall back to a library all-reduce + dli_sm100_add_rms_norm). */
+ * then fall back to a library all-reduce + dli_sm100_add_rms_norm); these depend
+ * on shapes only, so every rank reaches the same answer. A tensor that is not
+ * 16-byte aligned is DLI_ERR_INVALID_ARGUMENT (a per-rank property: falling back
+ * on it would leave this rank in a library collective its peers never join).
+ * After a wait ran out (DLI_ERR_DEVICE from dli_sm100_check_device_error) the
+ * buffers hold words of an abandoned exchange: every rank must zero its buffer
+ * with dli_sm100_tp_exchange_reset, and the group must synchronise, before the
+ * next exchange call. */
 /* Greedy pick over a vocabulary split across the group (vocab-parallel LM head):
  * rank i holds logits[rows, width] for ids [i*width, (i+1)*width). out_ids[r] =
  * the id of the largest logit of row r over all ranks, lowest id on ties (the

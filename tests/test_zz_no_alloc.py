@@ -6,7 +6,9 @@ instead of a caller workspace.
 
 Checked through the C ABI against dli_sm100_attention_kvcache (the entry point
 with a caller workspace) on two calls in a row with different inputs, so
-leftovers of the first call in the shared array cannot leak into the second.
+leftovers of the first call in the shared array cannot leak into the second,
+and against the CPU oracle (float64) at the same shape, with ragged cache
+positions, some so short that most key splits of their sequence are empty.
 The case decodes two tokens per sequence at the 7B head shape: 2 x 7 query
 rows per KV head take the split-KV kernel whose partials need scratch (single
 tokens take the cluster kernel, which needs none);
@@ -20,6 +22,7 @@ import pytest
 import torch
 
 import dli_sm100 as C
+from oracle import ops as O
 
 pytestmark = pytest.mark.gpu
 
@@ -57,6 +60,35 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
         torch.cuda.synchronize()
         err = ((got.float() - ref.float()).norm() / ref.float().norm()).item()
         assert err <= TOL, (seed, err)
+    C.check_device_error()
+
+
+def _oracle(q, ck, cv, positions):
+    """float64 oracle over the cache: sequence b sees keys [0, positions[b] + S), bottom-right causal."""
+    b, s = q.shape[:2]
+    outs = []
+    for i in range(b):
+        n = int(positions[i]) + s
+        qi = q[i:i + 1].permute(0, 2, 1, 3).double().cpu().numpy()
+        outs.append(torch.from_numpy(O.attention(qi, ck[i:i + 1, :, :n].double().cpu().numpy(),
+                                                 cv[i:i + 1, :, :n].double().cpu().numpy(),
+                                                 causal=True)).permute(0, 2, 1, 3))
+    return torch.cat(outs, 0)
+
+
+def test_noalloc_matches_oracle_with_empty_splits():
+    short = [0, 1, 3, 7, 15, 63, 64, 65, 127, 200]
+    for seed, positions in ((3, short + [(i * 997) % 2557 for i in range(22)]),
+                            (4, [(i * 1231) % 2557 for i in range(22)] + short[::-1])):
+        q, ck, cv, _ = _case(seed)
+        pos = torch.tensor(positions, device="cuda", dtype=torch.int64)
+        got = _noalloc(q, ck, cv, pos)
+        torch.cuda.synchronize()
+        ref = _oracle(q, ck, cv, positions)
+        err = ((got.double().cpu() - ref).norm() / ref.norm()).item()
+        assert err <= TOL, (seed, err)
+        rows = (got.double().cpu() - ref).flatten(2).norm(dim=-1) / ref.flatten(2).norm(dim=-1)
+        assert rows.max().item() <= 3 * TOL, (seed, rows.max().item())
     C.check_device_error()
 
 
