@@ -33,6 +33,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "fmha.cuh"
 #include "tcgen05.cuh"
 
 namespace dli_sm100 {
@@ -1097,6 +1098,38 @@ dli_status run_attention(AttnArgs& args, dli_dtype dtype, int64_t max_kv, void* 
                   aligned(args.v, 16) && aligned(args.out, 4);
   if (tc) {
     const DecodePlan plan = plan_decode(args.batch, args.hkv, args.group, args.seq_q, max_kv, args.head_dim);
+    if (!plan.decode) {
+      // prefill: the tcgen05 kernel (TMEM accumulators, TMA K/V) when the layout allows
+      FmhaArgs f{};
+      f.q = args.q;
+      f.k = args.k;
+      f.v = args.v;
+      f.out = args.out;
+      f.q_sb = args.q_sb;
+      f.q_sh = args.q_sh;
+      f.q_ss = args.q_ss;
+      f.o_sb = args.o_sb;
+      f.o_sh = args.o_sh;
+      f.o_ss = args.o_ss;
+      f.k_sb = args.k_sb;
+      f.k_sh = args.k_sh;
+      f.batch = args.batch;
+      f.hq = args.hq;
+      f.hkv = args.hkv;
+      f.seq_q = args.seq_q;
+      f.dense_kv = args.seq_k;
+      f.head_dim = args.head_dim;
+      f.positions = args.positions;
+      f.scale_log2 = args.scale_log2;
+      f.causal = args.causal;
+      if (fmha_supported(f, dtype)) {
+        const dli_status st = run_fmha_prefill(f, dtype, stream);
+        if (st != DLI_ERR_UNSUPPORTED) return st;
+      }
+      if (fmha_required())
+        return fail(DLI_ERR_UNSUPPORTED, "attention: the tcgen05 prefill kernel cannot serve this layout "
+                                         "(DLI_SM100_ATTN_FMHA=2)");
+    }
     if (plan.decode && !plan.cluster && plan.splits > 1) {
       if (workspace == nullptr || workspace_bytes < plan.workspace)
         return fail(DLI_ERR_WORKSPACE, "attention: workspace too small (need " +

@@ -74,6 +74,22 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// 4-D tiled load of the box at coordinates (c0 innermost .. c3) into shared memory.
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, int32_t c0,
+                                            int32_t c1, int32_t c2, int32_t c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads of them (operands a tcgen05.mma takes from shared memory).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ---- tcgen05 ----------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -127,6 +143,22 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// Stores 32 consecutive 32-bit columns of the warp's 32 TMEM lanes (thread i -> lane i).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  __syncwarp();
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+      "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 
 // ---- thread-block clusters -----------------------------------------------------
 // Full cluster barrier: every thread of every CTA of the cluster arrives
@@ -167,11 +199,33 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand stored with the
+// 128-byte swizzle: rows of 128 B hold 64 consecutive 16-bit MN elements for one
+// K index, 8 consecutive K rows form a 1024 B swizzle atom. `lbo` is the byte
+// distance between 64-element MN chunks (used when N or M exceeds 64), `sbo` the
+// byte distance between groups of 8 K rows (1024 when the rows are packed).
+// This is the layout a 2-D TMA box {64 MN elements, K rows} writes with
+// SWIZZLE_128B, e.g. V[keys][D] as the B operand of O = P V.
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16: f32 accumulator, A/B format (0 = f16,
 // 1 = bf16), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(bool bf16, int m, int n) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+// Same with operand B MN-major (the "transpose B" bit 16): B is given as K rows
+// of N consecutive elements instead of N rows of K.
+__host__ __device__ constexpr uint32_t umma_idesc_f16_bmn(bool bf16, int m, int n) {
+  return umma_idesc_f16(bf16, m, n) | (1u << 16);
 }
 
 }  // namespace dli_sm100
