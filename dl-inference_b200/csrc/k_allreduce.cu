@@ -30,6 +30,7 @@
 // live at fixed offsets, so calls with different row counts never overlap, and
 // a word left from epoch e-2 never matches epoch e.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -114,10 +115,45 @@ __device__ __forceinline__ uint4 wait_ll4(const uint64_t* p, uint32_t e, uint64_
 // VPT 16-byte vectors per thread: the host picks the smallest VPT that fits the
 // row in 512 threads, so as many threads as possible issue the peer stores (one
 // thread's remote stores drain slowly; the push is throughput-bound per thread).
-template <typename T, int kVpt>
+// Residual vectors: R = T (the residual stream in the model's type, rounded
+// after the add) or R = float with a 16-bit T (the residual stream kept in fp32).
+template <typename T, typename R>
+__device__ __forceinline__ void load_res(const R* ptr, float (&f)[Vec16<T>::N]) {
+  constexpr int V = Vec16<T>::N;
+  if constexpr (std::is_same<T, R>::value) {
+    const Vec16<T> v = load16(ptr);
+#pragma unroll
+    for (int j = 0; j < V; ++j) f[j] = to_f32(v.e[j]);
+  } else {
+#pragma unroll
+    for (int q = 0; q < V / 4; ++q) {
+      const float4 x = reinterpret_cast<const float4*>(ptr)[q];
+      f[4 * q] = x.x;
+      f[4 * q + 1] = x.y;
+      f[4 * q + 2] = x.z;
+      f[4 * q + 3] = x.w;
+    }
+  }
+}
+template <typename T, typename R>
+__device__ __forceinline__ void store_res(R* ptr, const float (&f)[Vec16<T>::N]) {
+  constexpr int V = Vec16<T>::N;
+  if constexpr (std::is_same<T, R>::value) {
+    Vec16<T> v;
+#pragma unroll
+    for (int j = 0; j < V; ++j) v.e[j] = from_f32<T>(f[j]);
+    store16(ptr, v);
+  } else {
+#pragma unroll
+    for (int q = 0; q < V / 4; ++q)
+      reinterpret_cast<float4*>(ptr)[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+  }
+}
+
+template <typename T, typename R, int kVpt>
 __global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
-    ExchangeParams p, const T* __restrict__ delta, const T* residual /* may alias residual_out */,
-    const T* __restrict__ w, T* __restrict__ normed, T* residual_out) {
+    ExchangeParams p, const T* __restrict__ delta, const R* residual /* may alias residual_out */,
+    const T* __restrict__ w, T* __restrict__ normed, R* residual_out) {
   constexpr int V = Vec16<T>::N;
   __shared__ float scratch[32];
   __shared__ uint32_t s_epoch;
@@ -188,16 +224,16 @@ __global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
   for (int i = 0; i < kVpt; ++i) {
     const int64_t c = threadIdx.x + static_cast<int64_t>(i) * blockDim.x;
     if (c < lanes) {
-      Vec16<T> res = load16(residual + off + c * V);
+      float res[V];
+      load_res<T, R>(residual + off + c * V, res);
 #pragma unroll
       for (int j = 0; j < V; ++j) {
-        const float sum = to_f32(from_f32<T>(acc[i][j]));  // the all-reduced value in T
-        const T h = from_f32<T>(to_f32(res.e[j]) + sum);
-        res.e[j] = h;
-        acc[i][j] = to_f32(h);
+        const float sum = round_through<T>(acc[i][j]);  // the all-reduced value in T
+        const float h = res[j] + sum;
+        acc[i][j] = std::is_same<T, R>::value ? round_through<T>(h) : h;
         ss += acc[i][j] * acc[i][j];
       }
-      store16(residual_out + off + c * V, res);
+      store_res<T, R>(residual_out + off + c * V, acc[i]);
     }
   }
   const float total = block_sum(ss, scratch);
@@ -327,7 +363,20 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm(
     const void* delta, const void* residual, const void* w, void* normed, void* residual_out,
     int64_t rank_stride, int64_t rows, int64_t hidden, float eps, int64_t timeout_ns, dli_dtype dtype,
     void* stream) {
+  return dli_sm100_allreduce_add_rms_norm_ex(buffers, tp, rank, ranks_in_launch, max_rows, row_elems, delta,
+                                             residual, w, normed, residual_out, rank_stride, rows, hidden, eps,
+                                             timeout_ns, dtype, dtype, stream);
+}
+
+extern "C" dli_status dli_sm100_allreduce_add_rms_norm_ex(
+    void* const* buffers, int tp, int rank, int ranks_in_launch, int64_t max_rows, int64_t row_elems,
+    const void* delta, const void* residual, const void* w, void* normed, void* residual_out,
+    int64_t rank_stride, int64_t rows, int64_t hidden, float eps, int64_t timeout_ns, dli_dtype dtype,
+    dli_dtype residual_dtype, void* stream) {
   const char* name = "allreduce_add_rms_norm";
+  const bool res32 = residual_dtype != dtype;
+  if (res32 && (residual_dtype != DLI_DTYPE_F32 || (dtype != DLI_DTYPE_BF16 && dtype != DLI_DTYPE_F16)))
+    return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": a float32 residual needs bfloat16/float16 tensors");
   if (buffers == nullptr || tp < 1 || tp > kMaxRanks || rank < 0 || ranks_in_launch < 1 ||
       rank + ranks_in_launch > tp || (ranks_in_launch > 1 && rank != 0))
     return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": bad rank arguments");
@@ -382,8 +431,8 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm(
     int per_sm = 0;
     st = dispatch_float(dtype, name, [&](auto tag) {
       using T = decltype(tag);
-      auto kern = cand == 1 ? allreduce_add_rms_norm_kernel<T, 1>
-                            : (cand == 2 ? allreduce_add_rms_norm_kernel<T, 2> : allreduce_add_rms_norm_kernel<T, 4>);
+      auto kern = cand == 1 ? allreduce_add_rms_norm_kernel<T, T, 1>
+                            : (cand == 2 ? allreduce_add_rms_norm_kernel<T, T, 2> : allreduce_add_rms_norm_kernel<T, T, 4>);
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, static_cast<int>(th), 0);
     });
     if (st != DLI_OK) return st;
@@ -395,15 +444,16 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm(
   }
   if (vpt == 0) return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": more rows than resident CTAs");
   const dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(ranks_in_launch));
-  st = dispatch_float(dtype, name, [&](auto tag) {
-    using T = decltype(tag);
-    auto kern = vpt == 1 ? allreduce_add_rms_norm_kernel<T, 1>
-                         : (vpt == 2 ? allreduce_add_rms_norm_kernel<T, 2> : allreduce_add_rms_norm_kernel<T, 4>);
+  auto go = [&](auto ttag, auto rtag) {
+    using T = decltype(ttag);
+    using R = decltype(rtag);
+    auto kern = vpt == 1 ? allreduce_add_rms_norm_kernel<T, R, 1>
+                         : (vpt == 2 ? allreduce_add_rms_norm_kernel<T, R, 2> : allreduce_add_rms_norm_kernel<T, R, 4>);
     const T* d = static_cast<const T*>(delta);
-    const T* res = static_cast<const T*>(residual);
+    const R* res = static_cast<const R*>(residual);
     const T* wt = static_cast<const T*>(w);
     T* nm = static_cast<T*>(normed);
-    T* ro = static_cast<T*>(residual_out);
+    R* ro = static_cast<R*>(residual_out);
     if (ranks_in_launch == 1) {
       launch_pdl(kern, grid, dim3(static_cast<unsigned>(threads)), 0, as_stream(stream), p, d, res, wt, nm, ro);
     } else {
@@ -412,6 +462,11 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm(
       cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kern), grid, dim3(static_cast<unsigned>(threads)),
                                   args, 0, as_stream(stream));
     }
+  };
+  st = dispatch_float(dtype, name, [&](auto tag) {
+    using T = decltype(tag);
+    if (res32) go(T{}, float{});
+    else go(T{}, T{});
   });
   if (st != DLI_OK) return st;
   return check_launch(name);

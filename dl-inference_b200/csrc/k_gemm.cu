@@ -127,13 +127,12 @@ __device__ __forceinline__ void store_vals(const TcParams& p, int64_t gi, int jc
   }
 }
 
-// SwiGLU of one gate/up accumulator pair, rounded like the unfused graph
-// (linear output in T, silu output in T, product in T).
+// SwiGLU of one gate/up accumulator pair: silu(g) * u from the fp32
+// accumulators, rounded to T once (the unfused graph rounds the gate and up
+// outputs, the silu and the product: four bf16 roundings instead of one).
 template <typename T>
 __device__ __forceinline__ T glu_val(float g, float u) {
-  const float gt = round_through<T>(g), ut = round_through<T>(u);
-  const float sg = round_through<T>(gt / (1.0f + expf(-gt)));
-  return from_f32<T>(sg * ut);
+  return from_f32<T>(g / (1.0f + expf(-g)) * u);
 }
 
 // kEpiGluT: n (<= 32) consecutive tokens j0.. of gate row `grow` (0..63) of tile ti.

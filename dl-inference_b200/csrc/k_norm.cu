@@ -75,6 +75,64 @@ __global__ void rms_norm_kernel(const T* x /* may alias residual_out */,
   }
 }
 
+// Residual add + RMSNorm with the residual stream kept in float32 while the
+// delta, the weight and the normalised output are T (bf16/f16): the running
+// sum of a deep model then carries no 16-bit rounding from layer to layer.
+// s = residual + delta in fp32 (stored unrounded), normed = T(T(s * inv) * w).
+template <typename T>
+__global__ void add_rms_norm_res32_kernel(const float* residual /* may alias residual_out */,
+                                          const T* __restrict__ delta, const T* __restrict__ w,
+                                          T* __restrict__ out, float* residual_out, int64_t rows,
+                                          int64_t hidden, float eps, bool vec) {
+  DLI_PDL_ENTRY();
+  __shared__ float scratch[32];
+  constexpr int V = Vec16<T>::N;  // 8 elements: 16 bytes of T, 32 bytes of residual
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* xr = residual + r * hidden;
+    const T* dr = delta + r * hidden;
+    float* rr = residual_out + r * hidden;
+    float ss = 0.f;
+    if (vec) {
+      for (int64_t c = threadIdx.x * V; c < hidden; c += blockDim.x * V) {
+        const Vec16<T> d = load16(dr + c);
+        float4 a0 = *reinterpret_cast<const float4*>(xr + c);
+        float4 a1 = *reinterpret_cast<const float4*>(xr + c + 4);
+        a0.x += to_f32(d.e[0]); a0.y += to_f32(d.e[1]); a0.z += to_f32(d.e[2]); a0.w += to_f32(d.e[3]);
+        a1.x += to_f32(d.e[4]); a1.y += to_f32(d.e[5]); a1.z += to_f32(d.e[6]); a1.w += to_f32(d.e[7]);
+        *reinterpret_cast<float4*>(rr + c) = a0;
+        *reinterpret_cast<float4*>(rr + c + 4) = a1;
+        ss += a0.x * a0.x + a0.y * a0.y + a0.z * a0.z + a0.w * a0.w;
+        ss += a1.x * a1.x + a1.y * a1.y + a1.z * a1.z + a1.w * a1.w;
+      }
+    } else {
+      for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) {
+        const float f = xr[c] + to_f32(dr[c]);
+        rr[c] = f;
+        ss += f * f;
+      }
+    }
+    const float total = block_sum(ss, scratch);
+    const float inv = rsqrtf(total / static_cast<float>(hidden) + eps);
+    T* dst = out + r * hidden;
+    if (vec) {
+      for (int64_t c = threadIdx.x * V; c < hidden; c += blockDim.x * V) {
+        const float4 a0 = *reinterpret_cast<const float4*>(rr + c);
+        const float4 a1 = *reinterpret_cast<const float4*>(rr + c + 4);
+        const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const Vec16<T> g = load16(w + c);
+        Vec16<T> o;
+#pragma unroll
+        for (int j = 0; j < V; ++j) o.e[j] = from_f32<T>(round_through<T>(a[j] * inv) * to_f32(g.e[j]));
+        store16(dst + c, o);
+      }
+    } else {
+      for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x)
+        dst[c] = from_f32<T>(round_through<T>(rr[c] * inv) * to_f32(w[c]));
+    }
+    __syncthreads();  // scratch reuse by the next row
+  }
+}
+
 template <bool kFused>
 dli_status launch(const void* x, const void* delta, const void* w, void* out, void* residual_out,
                   int64_t rows, int64_t hidden, float eps, dli_dtype dtype, void* stream,
@@ -114,4 +172,34 @@ extern "C" dli_status dli_sm100_add_rms_norm(const void* residual, const void* d
                                              void* stream) {
   return launch<true>(residual, delta, w, normed, residual_out, rows, hidden, eps, dtype, stream,
                       "add_rms_norm");
+}
+
+extern "C" dli_status dli_sm100_add_rms_norm_ex(const void* residual, const void* delta, const void* w,
+                                                void* normed, void* residual_out, int64_t rows,
+                                                int64_t hidden, float eps, dli_dtype dtype,
+                                                dli_dtype residual_dtype, void* stream) {
+  const char* name = "add_rms_norm_ex";
+  if (residual_dtype == dtype)
+    return dli_sm100_add_rms_norm(residual, delta, w, normed, residual_out, rows, hidden, eps, dtype, stream);
+  if (residual_dtype != DLI_DTYPE_F32 || (dtype != DLI_DTYPE_BF16 && dtype != DLI_DTYPE_F16))
+    return fail(DLI_ERR_UNSUPPORTED, std::string(name) + ": a float32 residual with bfloat16/float16 tensors");
+  if (rows < 0 || hidden <= 0) return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": bad sizes");
+  if (rows == 0) return ok();
+  if (!residual || !delta || !w || !normed || !residual_out)
+    return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": null pointer");
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, sm_count() * 16));
+  const bool vec = hidden % 8 == 0 && aligned(residual, 32) && aligned(residual_out, 32) && aligned(delta, 16) &&
+                   aligned(w, 16) && aligned(normed, 16);
+  const int64_t lanes = vec ? hidden / 8 : hidden;
+  const int threads = lanes >= 512 ? 512 : (lanes >= 256 ? 256 : (lanes >= 128 ? 128 : 32));
+  if (dtype == DLI_DTYPE_BF16)
+    launch_pdl(add_rms_norm_res32_kernel<__nv_bfloat16>, grid, threads, 0, as_stream(stream),
+               static_cast<const float*>(residual), static_cast<const __nv_bfloat16*>(delta),
+               static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(normed),
+               static_cast<float*>(residual_out), rows, hidden, eps, vec);
+  else
+    launch_pdl(add_rms_norm_res32_kernel<__half>, grid, threads, 0, as_stream(stream),
+               static_cast<const float*>(residual), static_cast<const __half*>(delta), static_cast<const __half*>(w),
+               static_cast<__half*>(normed), static_cast<float*>(residual_out), rows, hidden, eps, vec);
+  return check_launch(name);
 }

@@ -83,6 +83,18 @@ void floatInputs(const Inputs& in, std::size_t n, const std::string& op) {
   }
 }
 
+// (residual, delta, weight) of the add + RMSNorm operators: delta and weight
+// share one float dtype; the residual has that dtype too, or is float32 (a
+// residual stream kept in fp32 around a bfloat16/float16 model).
+void residualInputs(const Inputs& in, const std::string& op) {
+  dli::requireCudaInputs(in, op);
+  for (const Tensor* t : in) dli::requireFloat(*t, op);
+  dli::requireSameDtype(*in[1], *in[2], op);
+  if (in[0]->dtype() != in[1]->dtype() &&
+      !(in[0]->dtype() == DType::Float32 && (in[1]->dtype() == DType::BFloat16 || in[1]->dtype() == DType::Float16)))
+    throw std::invalid_argument(op + ": residual must match delta or be float32 around a 16-bit delta");
+}
+
 template <typename Op>
 void reg(dli::OperatorRegistry* r, const char* name) {
   r->registerFactory(name, [] { return std::make_unique<Op>(); });
@@ -440,23 +452,26 @@ class TransposeOp final : public dli::Operator {
 // Additive fused operators (batched Qwen2 graphs)
 // ---------------------------------------------------------------------------
 
-// add_rms_norm: (residual, delta, weight) -> (normed, residual + delta).
+// add_rms_norm: (residual, delta, weight) -> (normed, residual + delta). normed
+// has delta's dtype, the new residual the residual's (float32 when the graph
+// keeps its residual stream in fp32).
 class AddRmsNormOp final : public dli::Operator {
  public:
   std::string type() const override { return "add_rms_norm"; }
   void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
     arity(in, out, 3, 3, 2, type());
-    floatInputs(in, 3, type());
+    residualInputs(in, type());
     const Tensor& r = *in[0];
-    if (in[1]->shape() != r.shape()) throw std::invalid_argument("add_rms_norm residual/delta shape mismatch");
+    const Tensor& d = *in[1];
+    if (d.shape() != r.shape()) throw std::invalid_argument("add_rms_norm residual/delta shape mismatch");
     const std::int64_t hidden = r.shape().back();
     if (static_cast<std::int64_t>(in[2]->numel()) != hidden) throw std::invalid_argument("add_rms_norm weight size mismatch");
     const float eps = static_cast<float>(dli::attrDouble(attrs, "eps", 1e-6));
-    *out[0] = Tensor::cuda(r.dtype(), r.shape(), r.deviceId());
+    *out[0] = Tensor::cuda(d.dtype(), r.shape(), r.deviceId());
     *out[1] = Tensor::cuda(r.dtype(), r.shape(), r.deviceId());
-    check(dli_sm100_add_rms_norm(dli::ptr(r), dli::ptr(*in[1]), dli::ptr(*in[2]), out[0]->deviceData(),
-                                 out[1]->deviceData(), static_cast<std::int64_t>(r.numel()) / hidden, hidden, eps,
-                                 cdt(r.dtype()), ctx.cuda_stream),
+    check(dli_sm100_add_rms_norm_ex(dli::ptr(r), dli::ptr(d), dli::ptr(*in[2]), out[0]->deviceData(),
+                                    out[1]->deviceData(), static_cast<std::int64_t>(r.numel()) / hidden, hidden, eps,
+                                    cdt(d.dtype()), cdt(r.dtype()), ctx.cuda_stream),
           type());
   }
 };
@@ -627,6 +642,10 @@ class CastOp final : public dli::Operator {
     const Tensor& x = *in[0];
     const DType to = dli::dtypeFromString(attrs.require<std::string>("dtype"));
     if (!dli::isFloating(to)) throw std::invalid_argument("cast target must be a float dtype");
+    if (to == x.dtype()) {  // nothing to convert: the output is the input
+      *out[0] = x;
+      return;
+    }
     *out[0] = Tensor::cuda(to, x.shape(), x.deviceId());
     check(dli_sm100_cast(dli::ptr(x), cdt(x.dtype()), out[0]->deviceData(), cdt(to),
                          static_cast<std::int64_t>(x.numel()), ctx.cuda_stream),
@@ -699,7 +718,7 @@ class AllReduceAddRmsNormOp final : public dli::Operator {
   std::string type() const override { return "all_reduce_add_rms_norm"; }
   void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
     arity(in, out, 3, 3, 2, type());
-    floatInputs(in, 3, type());
+    residualInputs(in, type());
     const Tensor& r = *in[0];
     const Tensor& d = *in[1];
     if (d.shape() != r.shape()) throw std::invalid_argument("all_reduce_add_rms_norm residual/delta shape mismatch");
@@ -708,19 +727,19 @@ class AllReduceAddRmsNormOp final : public dli::Operator {
       throw std::invalid_argument("all_reduce_add_rms_norm weight size mismatch");
     const std::int64_t rows = static_cast<std::int64_t>(r.numel()) / hidden;
     const float eps = static_cast<float>(dli::attrDouble(attrs, "eps", 1e-6));
-    *out[0] = Tensor::cuda(r.dtype(), r.shape(), r.deviceId());
+    *out[0] = Tensor::cuda(d.dtype(), r.shape(), r.deviceId());
     *out[1] = Tensor::cuda(r.dtype(), r.shape(), r.deviceId());
     const void* delta = dli::ptr(d);
     Tensor summed;
     if (ctx.tp_size > 1) {
       if (ctx.communicator == nullptr) throw std::invalid_argument(type() + ": no communicator for tp_size > 1");
       const Exchange* ex = findExchange(ctx.communicator);
-      if (ex != nullptr && ex->tp == ctx.tp_size && ex->rank == ctx.tp_rank && ex->dtype == cdt(r.dtype()) &&
+      if (ex != nullptr && ex->tp == ctx.tp_size && ex->rank == ctx.tp_rank && ex->dtype == cdt(d.dtype()) &&
           rows <= ex->max_rows && hidden <= ex->row_elems) {
-        const dli_status st = dli_sm100_allreduce_add_rms_norm(
+        const dli_status st = dli_sm100_allreduce_add_rms_norm_ex(
             ex->ptrs.data(), ex->tp, ex->rank, 1, ex->max_rows, ex->row_elems, delta, dli::ptr(r),
             dli::ptr(*in[2]), out[0]->deviceData(), out[1]->deviceData(), 0, rows, hidden, eps, 0,
-            cdt(r.dtype()), ctx.cuda_stream);
+            cdt(d.dtype()), cdt(r.dtype()), ctx.cuda_stream);
         if (st == DLI_OK) return;
         if (st != DLI_ERR_UNSUPPORTED) check(st, type());
       }
@@ -737,8 +756,9 @@ class AllReduceAddRmsNormOp final : public dli::Operator {
       throw std::runtime_error(type() + ": plugin built without NCCL");
 #endif
     }
-    check(dli_sm100_add_rms_norm(dli::ptr(r), delta, dli::ptr(*in[2]), out[0]->deviceData(), out[1]->deviceData(),
-                                 rows, hidden, eps, cdt(r.dtype()), ctx.cuda_stream),
+    check(dli_sm100_add_rms_norm_ex(dli::ptr(r), delta, dli::ptr(*in[2]), out[0]->deviceData(),
+                                    out[1]->deviceData(), rows, hidden, eps, cdt(d.dtype()), cdt(r.dtype()),
+                                    ctx.cuda_stream),
           type());
   }
 };

@@ -184,14 +184,19 @@ def transform_weights(state: dict[str, torch.Tensor], shape: Qwen2Shape, tp_size
 
 def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: str = "qwen2",
                 weights_file: str = "", with_argmax: bool = True, fused_glu: bool = True,
-                logits_dtype: str | None = "float32") -> dict[str, Any]:
+                logits_dtype: str | None = "float32",
+                residual_dtype: str | None = "float32") -> dict[str, Any]:
     """dli.graph.v1 dict for one rank. Inputs: input_ids [B,S] int64, positions [B]
     int64, rotary_cos/rotary_sin, and the weights of transform_weights() (made
     with the same `fused_glu`: one linear_silu_mul node instead of linear +
     silu_mul; the fused operator serves bfloat16/float16). `logits_dtype` sets
     the LM head's output type: "float32" keeps the fp32 accumulator, so greedy
     ids are not decided among logits that rounding to bf16 made equal; None
-    writes the weights' dtype."""
+    writes the weights' dtype. `residual_dtype` = "float32" keeps the residual
+    stream (embedding output + every block's output) in fp32: a cast after the
+    embedding starts it and each add_rms_norm adds the block's bf16 output to it
+    unrounded, so a 16-bit model does not round its running sum once per layer
+    (None keeps the residual in the weights' dtype)."""
     hq, hkv, d = shape.q_heads // tp_size, shape.kv_heads // tp_size, shape.head_dim
     nodes: list[dict[str, Any]] = []
 
@@ -204,10 +209,13 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
     add_norm = "all_reduce_add_rms_norm" if tp_size > 1 else "add_rms_norm"
     node("embed_tokens", "embedding", ["input_ids", "embed"], ["h0"])
     resid, delta = "h0", None
+    if residual_dtype:
+        node("residual_stream", "cast", ["h0"], ["h0_res"], {"dtype": residual_dtype})
+        resid = "h0_res"
     for i in range(shape.layers):
         L = f"layers.{i}"
         if delta is None:
-            node(f"{L}.input_layernorm", "rms_norm", [resid, f"{L}.ln_in"], [f"{L}.x"], {"eps": eps})
+            node(f"{L}.input_layernorm", "rms_norm", ["h0", f"{L}.ln_in"], [f"{L}.x"], {"eps": eps})
         else:
             node(f"{L}.input_layernorm", add_norm, [resid, delta, f"{L}.ln_in"],
                  [f"{L}.x", f"{L}.h_in"], {"eps": eps})

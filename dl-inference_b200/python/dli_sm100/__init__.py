@@ -47,6 +47,7 @@ SIGNATURES = {
     "dli_sm100_conv2d": (N, [P, P, P, P] + [I] * 11 + [D, P, Z, P]),
     "dli_sm100_rms_norm": (N, [P, P, P, I, I, F, D, P]),
     "dli_sm100_add_rms_norm": (N, [P, P, P, P, P, I, I, F, D, P]),
+    "dli_sm100_add_rms_norm_ex": (N, [P, P, P, P, P, I, I, F, D, D, P]),
     "dli_sm100_batch_norm2d": (N, [P, P, P, P, P, P, I, I, I, F, D, P]),
     "dli_sm100_softmax": (N, [P, P, I, I, D, P]),
     "dli_sm100_rotary_embedding": (N, [P, P, P, P, P, P] + [I] * 8 + [P, I, D, P]),
@@ -72,6 +73,7 @@ SIGNATURES = {
     "dli_sm100_tp_exchange_bytes": (Z, [D, I, I, D]),
     "dli_sm100_tp_exchange_reset": (N, [P, Z, P]),
     "dli_sm100_allreduce_add_rms_norm": (N, [P, D, D, D, I, I, P, P, P, P, P, I, I, I, F, I, D, P]),
+    "dli_sm100_allreduce_add_rms_norm_ex": (N, [P, D, D, D, I, I, P, P, P, P, P, I, I, I, F, I, D, D, P]),
     "dli_sm100_allgather_argmax": (N, [P, D, D, D, I, I, D, P, I, I, I, P, I, D, P]),
 }
 
@@ -224,13 +226,15 @@ def rms_norm(x, w, eps=1e-6):
 
 
 def add_rms_norm(residual, delta, w, eps=1e-6, residual_out=None):
+    """(normed, residual + delta). A float32 residual with a bf16/f16 delta keeps
+    the residual stream in fp32 (dli_sm100_add_rms_norm_ex); normed has delta's dtype."""
     _contig(residual, delta, w)
     hidden = residual.shape[-1]
-    normed = torch.empty_like(residual)
+    normed = torch.empty_like(delta)
     residual_out = residual_out if residual_out is not None else torch.empty_like(residual)
-    check(lib().dli_sm100_add_rms_norm(_ptr(residual), _ptr(delta), _ptr(w), _ptr(normed),
-                                       _ptr(residual_out), residual.numel() // hidden, hidden, eps,
-                                       _dt(residual), _stream()), "add_rms_norm")
+    check(lib().dli_sm100_add_rms_norm_ex(_ptr(residual), _ptr(delta), _ptr(w), _ptr(normed),
+                                          _ptr(residual_out), residual.numel() // hidden, hidden, eps,
+                                          _dt(delta), _dt(residual), _stream()), "add_rms_norm")
     return normed, residual_out
 
 
@@ -257,11 +261,11 @@ class ExchangeGroup:
         _contig(residual, delta, w)
         tp, rows, hidden = delta.shape
         ranks = tp if ranks is None else ranks
-        normed, residual_out = torch.empty_like(residual), torch.empty_like(residual)
-        st = lib().dli_sm100_allreduce_add_rms_norm(
+        normed, residual_out = torch.empty_like(delta), torch.empty_like(residual)
+        st = lib().dli_sm100_allreduce_add_rms_norm_ex(
             self._ptrs, self.tp, 0, ranks, self.max_rows, self.row_elems, _ptr(delta), _ptr(residual),
             _ptr(w), _ptr(normed), _ptr(residual_out), rows * hidden, rows, hidden, eps, timeout_ns,
-            _dt(delta), _stream())
+            _dt(delta), _dt(residual), _stream())
         check(st, "allreduce_add_rms_norm")
         return normed, residual_out
 

@@ -88,9 +88,9 @@ dli_status dli_sm100_linear_ex(const void* x, const void* w, const void* bias, v
                                int64_t n, int64_t k, dli_dtype dtype, dli_dtype out_dtype, void* stream);
 
 /* Fused gate/up projection + SwiGLU (additive; the reference graph runs
- * linear -> silu -> mul): y[M, inter] = silu(x · Wg^T) * (x · Wu^T), rounded like
- * the unfused nodes (each linear output, the silu output and the product in
- * dtype). w_glu holds Wg and Wu interleaved in 64-row blocks: rows
+ * linear -> silu -> mul): y[M, inter] = silu(x · Wg^T) * (x · Wu^T), computed in
+ * fp32 from the two fp32 accumulators and rounded to dtype once (the unfused
+ * nodes round each linear output, the silu output and the product). w_glu holds Wg and Wu interleaved in 64-row blocks: rows
  * [128b, 128b+64) are gate rows [64b, 64b+64) and rows [128b+64, 128b+128) the
  * matching up rows, 2*ceil(inter/64)*64 rows of K in all, the rows past `inter`
  * zero. BF16/F16 only (DLI_ERR_UNSUPPORTED otherwise): one tcgen05 GEMM whose
@@ -131,6 +131,17 @@ dli_status dli_sm100_rms_norm(const void* x, const void* w, void* out, int64_t r
 dli_status dli_sm100_add_rms_norm(const void* residual, const void* delta, const void* w,
                                   void* normed, void* residual_out, int64_t rows, int64_t hidden,
                                   float eps, dli_dtype dtype, void* stream);
+
+/* add_rms_norm with the residual stream in a wider type: residual and
+ * residual_out are `residual_dtype` (F32), delta, w and normed are `dtype`
+ * (BF16/F16). residual_out = residual + delta in fp32, unrounded; normed as
+ * dli_sm100_add_rms_norm. residual_out may alias residual. Additive (the
+ * reference's graphs run add then rms_norm in fp32, export.py:385,428): keeping
+ * the running sum of a 16-bit model in fp32 removes a rounding per layer from
+ * the logits. residual_dtype == dtype is dli_sm100_add_rms_norm. */
+dli_status dli_sm100_add_rms_norm_ex(const void* residual, const void* delta, const void* w,
+                                     void* normed, void* residual_out, int64_t rows, int64_t hidden,
+                                     float eps, dli_dtype dtype, dli_dtype residual_dtype, void* stream);
 
 /* batch_norm2d (inference): out = (x - mean[c]) * rsqrt(var[c] + eps) * weight[c] + bias[c].
  * Replaces python/dli_ops/aot/batch_norm2d/kernel.py:5-28, template.cc:1-33. */
@@ -337,6 +348,17 @@ dli_status dli_sm100_allreduce_add_rms_norm(void* const* buffers, int tp, int ra
                                             void* residual_out, int64_t rank_stride, int64_t rows,
                                             int64_t hidden, float eps, int64_t timeout_ns, dli_dtype dtype,
                                             void* stream);
+/* dli_sm100_allreduce_add_rms_norm with the residual stream in float32:
+ * residual and residual_out are `residual_dtype` (F32) while delta, w and
+ * normed are `dtype` (BF16/F16); the all-reduced delta is rounded to dtype (the
+ * value an all-reduce returns) and added to the fp32 residual without rounding,
+ * as dli_sm100_add_rms_norm_ex does. residual_dtype == dtype is the call above. */
+dli_status dli_sm100_allreduce_add_rms_norm_ex(void* const* buffers, int tp, int rank, int ranks_in_launch,
+                                               int64_t max_rows, int64_t row_elems, const void* delta,
+                                               const void* residual, const void* w, void* normed,
+                                               void* residual_out, int64_t rank_stride, int64_t rows,
+                                               int64_t hidden, float eps, int64_t timeout_ns, dli_dtype dtype,
+                                               dli_dtype residual_dtype, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

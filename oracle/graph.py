@@ -79,6 +79,8 @@ class GraphOracle:
             return [getattr(O, op)(*x)]
         if op == "reshape":
             return [np.asarray(x[0]).reshape(O.reshape_shape(np.asarray(x[0]).shape, a["shape"]))]
+        if op == "cast":  # float64 throughout: a dtype change is the identity here
+            return [np.asarray(x[0], dtype=np.float64)]
         raise KeyError(f"oracle graph interpreter: unsupported op {op}")
 
     def _qkv_rotary_cache(self, x, a):

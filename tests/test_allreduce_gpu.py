@@ -65,6 +65,29 @@ def test_fused_allreduce_matches_sum_then_add_rms_norm(tp, rows, hidden):
     C.check_device_error()
 
 
+@pytest.mark.parametrize("tp", [2, 4])
+def test_fp32_residual_stream(tp):
+    """bf16 partials around a float32 residual (the exported graphs' residual
+    stream): residual_out = residual + bf16(sum of partials) in fp32, bit for bit
+    as dli_sm100_add_rms_norm_ex computes it, identical on every rank."""
+    rows, hidden = 32, 3584
+    group = C.ExchangeGroup(tp, max_rows=64, row_elems=4096, dtype=torch.bfloat16)
+    for seed in range(2):
+        residual, delta, w = _case(tp, rows, hidden, torch.bfloat16, 20 + seed)
+        # an fp32 residual (below bf16 resolution), replicated on every rank
+        noise = 1e-3 * torch.randn(rows, hidden, device="cuda")
+        residual = (residual[0].float() + noise).unsqueeze(0).expand(tp, rows, hidden).contiguous()
+        normed, res_out = group.allreduce_add_rms_norm(residual, delta, w, eps=1e-6)
+        ref_n, ref_r = _expected(residual, delta, w, 1e-6)
+        torch.cuda.synchronize()
+        assert res_out.dtype == torch.float32 and normed.dtype == torch.bfloat16
+        for k in range(tp):
+            assert torch.equal(res_out[k], ref_r), (seed, k)
+            assert torch.equal(normed[k], normed[0]), (seed, k)
+        torch.testing.assert_close(normed[0].float(), ref_n.float(), rtol=1e-2, atol=1e-2)
+    C.check_device_error()
+
+
 def test_fp32_and_changing_row_counts():
     tp = 4
     group = C.ExchangeGroup(tp, max_rows=128, row_elems=4096, dtype=torch.float32)

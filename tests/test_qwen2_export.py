@@ -43,7 +43,7 @@ def test_interleaved_rotary_on_permuted_rows_equals_rotate_half():
 
 
 def test_graph_structure_per_layer():
-    g = build_graph(TINY, capacity=64, tp_size=1, fused_glu=False)
+    g = build_graph(TINY, capacity=64, tp_size=1, fused_glu=False, residual_dtype=None)
     ops = [n["op"] for n in g["nodes"]]
     assert ops[0] == "embedding"
     layer0 = ["rms_norm", "linear", "qkv_rotary_cache", "attention_kvcache", "linear", "add_rms_norm",
@@ -57,6 +57,15 @@ def test_graph_structure_per_layer():
     fused = [n for n in gf["nodes"] if n["op"] == "linear_silu_mul"]
     assert len(fused) == TINY.layers and "silu_mul" not in [n["op"] for n in gf["nodes"]]
     assert fused[0]["attrs"]["intermediate"] == TINY.intermediate
+    # fp32 residual stream (default): a cast after the embedding starts it; the
+    # first norm still reads the embedding output, every add+norm the fp32 chain
+    cast = [n for n in gf["nodes"] if n["op"] == "cast"]
+    assert len(cast) == 1 and cast[0]["inputs"] == ["h0"] and cast[0]["attrs"]["dtype"] == "float32"
+    first_add = next(n for n in gf["nodes"] if n["op"] == "add_rms_norm")
+    assert first_add["inputs"][0] == "h0_res"
+    assert gf["nodes"][2]["op"] == "rms_norm" and gf["nodes"][2]["inputs"][0] == "h0"
+    lm = next(n for n in gf["nodes"] if n["name"] == "lm_head")
+    assert lm["attrs"]["out_dtype"] == "float32"
     assert g["inputs"] == ["input_ids", "positions"] and g["outputs"] == ["logits", "next_ids"]
     g2 = build_graph(TINY, capacity=64, tp_size=2)
     ops2 = [n["op"] for n in g2["nodes"]]
