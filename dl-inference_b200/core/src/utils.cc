@@ -1,76 +1,84 @@
 #include "dli/utils.h"
 
-#include <sstream>
+#include <algorithm>
+#include <functional>
+#include <numeric>
 #include <stdexcept>
+#include <type_traits>
+#include <variant>
 
 namespace dli {
 
 std::int64_t product(const std::vector<std::int64_t>& shape, std::size_t begin, std::size_t end) {
-  if (end == static_cast<std::size_t>(-1) || end > shape.size()) end = shape.size();
-  std::int64_t p = 1;
-  for (std::size_t i = begin; i < end; ++i) p *= shape[i];
-  return p;
+  end = std::min(end, shape.size());
+  if (begin >= end) return 1;
+  return std::accumulate(shape.begin() + static_cast<std::ptrdiff_t>(begin),
+                         shape.begin() + static_cast<std::ptrdiff_t>(end), std::int64_t{1},
+                         std::multiplies<std::int64_t>());
 }
 
-unsigned ceilDiv(std::int64_t a, std::int64_t b) { return static_cast<unsigned>((a + b - 1) / b); }
-
 std::string formatShape(const std::vector<std::int64_t>& shape) {
-  std::ostringstream out;
-  out << '[';
-  for (std::size_t i = 0; i < shape.size(); ++i) out << (i ? "," : "") << shape[i];
-  out << ']';
-  return out.str();
+  std::string text = "[";
+  const char* sep = "";
+  for (const std::int64_t d : shape) {
+    text += sep;
+    text += std::to_string(d);
+    sep = ", ";
+  }
+  return text + "]";
 }
 
 void requireCudaInputs(const std::vector<const Tensor*>& inputs, const std::string& op) {
-  for (const Tensor* t : inputs)
-    if (t == nullptr || !t->isCuda()) throw std::invalid_argument(op + " expects CUDA tensors");
+  const bool all_cuda =
+      std::all_of(inputs.begin(), inputs.end(), [](const Tensor* t) { return t != nullptr && t->isCuda(); });
+  if (!all_cuda) throw std::invalid_argument(op + " expects CUDA tensors");
 }
 
 void requireFloat(const Tensor& tensor, const std::string& op) {
-  if (!isFloating(tensor.dtype()))
-    throw std::invalid_argument(op + " expects float32, bfloat16 or float16");
+  if (isFloating(tensor.dtype())) return;
+  throw std::invalid_argument(op + " expects float32, bfloat16 or float16, got " + toString(tensor.dtype()));
 }
 
 void requireSameDtype(const Tensor& a, const Tensor& b, const std::string& op) {
-  if (a.dtype() != b.dtype())
-    throw std::invalid_argument(op + " expects matching dtypes (" + toString(a.dtype()) + " vs " +
-                                toString(b.dtype()) + ")");
+  if (a.dtype() == b.dtype()) return;
+  throw std::invalid_argument(op + " expects one dtype for its tensors, got " + toString(a.dtype()) + " and " +
+                              toString(b.dtype()));
 }
 
 double attrDouble(const Attributes& attrs, const std::string& name, double fallback) {
-  if (!attrs.contains(name)) return fallback;
-  if (std::holds_alternative<std::int64_t>(attrs.values().at(name)))
-    return static_cast<double>(attrs.require<std::int64_t>(name));
-  return attrs.require<double>(name);
+  const auto it = attrs.values().find(name);
+  if (it == attrs.values().end()) return fallback;
+  return std::visit(
+      [&name](const auto& v) -> double {
+        using V = std::decay_t<decltype(v)>;
+        if constexpr (std::is_same_v<V, double> || std::is_same_v<V, std::int64_t>) {
+          return static_cast<double>(v);
+        } else {
+          throw std::invalid_argument("attribute has unexpected type: " + name);
+        }
+      },
+      it->second);
 }
 
 std::vector<std::int64_t> attrInts(const Attributes& attrs, const std::string& name,
                                    std::vector<std::int64_t> fallback) {
-  if (!attrs.contains(name)) return fallback;
-  return attrs.require<std::vector<std::int64_t>>(name);
+  return attrs.contains(name) ? attrs.require<std::vector<std::int64_t>>(name) : std::move(fallback);
 }
 
 void* ptr(const Tensor& tensor) { return const_cast<void*>(tensor.deviceData()); }
 
 std::vector<std::int64_t> reshapeShape(const std::vector<std::int64_t>& input,
                                        std::vector<std::int64_t> target) {
-  std::int64_t known = 1;
-  int infer = -1;
-  for (std::size_t i = 0; i < target.size(); ++i) {
-    if (target[i] == -1) {
-      if (infer != -1) throw std::invalid_argument("reshape has multiple inferred dimensions");
-      infer = static_cast<int>(i);
-    } else if (target[i] <= 0) {
-      throw std::invalid_argument("reshape dimension must be positive or -1");
-    } else {
-      known *= target[i];
-    }
-  }
+  const auto wildcards = std::count(target.begin(), target.end(), std::int64_t{-1});
+  if (wildcards > 1) throw std::invalid_argument("reshape has multiple inferred dimensions");
+  if (std::any_of(target.begin(), target.end(), [](std::int64_t d) { return d == 0 || d < -1; }))
+    throw std::invalid_argument("reshape dimension must be positive or -1");
   const std::int64_t numel = product(input);
-  if (infer != -1) {
-    if (numel % known != 0) throw std::invalid_argument("reshape inferred dimension is not integral");
-    target[static_cast<std::size_t>(infer)] = numel / known;
+  if (wildcards == 1) {
+    // the product of the fixed entries is minus the product with the -1 included
+    const std::int64_t fixed = -product(target);
+    if (numel % fixed != 0) throw std::invalid_argument("reshape inferred dimension is not integral");
+    *std::find(target.begin(), target.end(), std::int64_t{-1}) = numel / fixed;
   }
   if (product(target) != numel) throw std::invalid_argument("reshape changes element count");
   return target;

@@ -102,6 +102,13 @@ __device__ __forceinline__ uint32_t pack_pair(float lo, float hi) {
   }
 }
 
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // Every lane waits (so each observes the completed phase), then the warp agrees.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   const bool done = mbar_wait(bar, parity);
@@ -308,19 +315,23 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
       // mask: keys < lim are visible to this row
       const int key0 = j * BN;
       const bool full_block = key0 + BN <= kv_len && (!p.causal || key0 + BN - 1 <= m0 + off);
-      float mx = -INFINITY;
-      if (full_block) {
-#pragma unroll
-        for (int i = 0; i < BN; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
-      } else {
+      if (!full_block) {
         const int lim = p.causal ? min(kv_len, qrow + off + 1) : kv_len;
 #pragma unroll
-        for (int i = 0; i < BN; ++i) {
-          const float v = key0 + i < lim ? __uint_as_float(sr[i]) : -INFINITY;
-          sr[i] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
-        }
+        for (int i = 0; i < BN; ++i)
+          if (key0 + i >= lim) sr[i] = __float_as_uint(-INFINITY);
       }
+      // row maximum over 8 independent chains (short dependency chains: one
+      // warp per scheduler, so latency is not hidden by other warps)
+      float mc[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mc[k] = max3(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1]), -INFINITY);
+#pragma unroll
+      for (int i = 16; i < BN; i += 16)
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mc[k] = max3(mc[k], __uint_as_float(sr[i + 2 * k]), __uint_as_float(sr[i + 2 * k + 1]));
+      const float mx = max3(max3(mc[0], mc[1], mc[2]), max3(mc[3], mc[4], mc[5]), fmaxf(mc[6], mc[7]));
       const float m_blk = mx * p.scale_log2;
       float alpha = 1.f;
       bool rescale_row = false;
@@ -355,15 +366,15 @@ __global__ void __launch_bounds__(kFmhaThreads, 1)
       // P = exp2(S * scale - m) (masked keys: exp2(-inf) = 0)
       const float neg = m_used == -INFINITY ? 0.f : -m_used;
       uint32_t pk[BN / 2];
-      float rs = 0.f;
+      float rs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < BN; i += 2) {
         const float p0 = ex2(fmaf(__uint_as_float(sr[i]), p.scale_log2, neg));
         const float p1 = ex2(fmaf(__uint_as_float(sr[i + 1]), p.scale_log2, neg));
-        rs += p0 + p1;
+        rs[(i / 2) & 7] += p0 + p1;
         pk[i / 2] = pack_pair<T>(p0, p1);
       }
-      l += rs;
+      l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
       // P V_{j-1} must have consumed the P tile before it is rewritten
       if (j > 0 && !waited) {
         if (!warp_wait(o_done, (j - 1) & 1, abort_flag)) {

@@ -6,7 +6,8 @@ Each case builds its inputs once (every case's operands exceed the 126 MB L2,
 or it states otherwise), runs 3 warm-up launches and N timed launches through the
 C ABI, and prints one JSON line with the mean launch time (CUDA events) and the
 algorithmic bytes / FLOPs of one launch. Cases use the Qwen2-7B decode/prefill
-shapes of the benchmark (batch 32, 2048-token prompts).
+shapes of the benchmark (batch 32, 2048-token prompts). The attention prefill
+cases are tensor-bound; their operands may fit in L2.
 """
 from __future__ import annotations
 
@@ -67,6 +68,8 @@ CASES = {
     "attn_decode": _attn_decode,
     "attn_decode_tp4": lambda: _attn_decode(hq=7, hkv=1),
     "attn_prefill": _attn_prefill,
+    "attn_prefill_b32": lambda: _attn_prefill(b=32, s=2048),          # the benchmark's prefill launch
+    "attn_prefill_0_5b": lambda: _attn_prefill(b=8, hq=14, hkv=2, d=64, s=512),
 }
 
 

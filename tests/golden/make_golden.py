@@ -1,9 +1,9 @@
 """Regenerates the golden fixtures in tests/golden/*.npz from the reference itself.
 
-Run in a container where the reference checkout exists (default
-/root/reference, or $DLI_REFERENCE_ROOT):
+Run where a checkout of the reference exists, naming its root:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <dl-inference checkout>
+    DLI_REFERENCE_ROOT=<dl-inference checkout> python tests/golden/make_golden.py
 
 For every dli.graph.v1 operator this script executes the reference's own Triton
 kernel (python/dli_ops/aot/<op>/kernel.py) on CPU through the Triton
@@ -38,7 +38,8 @@ os.environ["TRITON_INTERPRET"] = "1"
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = Path(os.environ.get("DLI_REFERENCE_ROOT", "/root/reference"))
+REF_ARG = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DLI_REFERENCE_ROOT", "")
+REF = Path(REF_ARG)
 AOT = REF / "python" / "dli_ops" / "aot"
 OUT = Path(__file__).resolve().parent
 
@@ -367,8 +368,9 @@ def save() -> None:
 
 
 def main() -> int:
-    if not AOT.exists():
-        print(f"reference checkout not found at {REF}", file=sys.stderr)
+    if not REF_ARG or not AOT.exists():
+        print(f"reference checkout not found at {REF_ARG!r}: pass its root as the first argument "
+              "or in DLI_REFERENCE_ROOT", file=sys.stderr)
         return 1
     capture_reference_tests()
     random_cases()

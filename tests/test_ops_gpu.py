@@ -140,7 +140,7 @@ def test_linear_tcgen05_model_shapes(m, n, k, dtype):
 
 
 def test_linear_fp32_config1():
-    """x[64,1024] . W[4096,1024]^T + b in fp32, rel-err <= 1e-4."""
+    """The single-linear workload: x[64,1024] . W[4096,1024]^T + b in fp32, rel-err <= 1e-4."""
     import dli_sm100 as C
 
     g = torch.Generator().manual_seed(0)
