@@ -12,6 +12,7 @@
 
 #include "dli/engine.h"
 #include "dli/graph.h"
+#include "dli/profile.h"
 #include "dli/weights.h"
 
 namespace py = pybind11;
@@ -75,16 +76,18 @@ PYBIND11_MODULE(_dli_native, m) {
           py::arg("path"), py::return_value_policy::reference_internal)
       .def(
           "run",
-          [](dli::Engine& e, const dli::Graph& g, const py::dict& inputs) {
+          [](dli::Engine& e, const dli::Graph& g, const py::dict& inputs, dli::ProfileSession* profile) {
             auto tensors = fromPython(inputs);
             dli::TensorMap out;
+            dli::RunOptions options;
+            options.profiler = profile;
             {
               py::gil_scoped_release release;
-              out = e.run(g, std::move(tensors));
+              out = e.run(g, std::move(tensors), options);
             }
             return toPython(out);
           },
-          py::arg("graph"), py::arg("inputs"))
+          py::arg("graph"), py::arg("inputs"), py::arg("profile") = nullptr)
       .def(
           "set_constants",
           [](dli::Engine& e, const py::dict& tensors) { e.setConstants(fromPython(tensors)); },
@@ -114,6 +117,30 @@ PYBIND11_MODULE(_dli_native, m) {
           },
           py::arg("comm"), py::arg("rank"), py::arg("size"))
       .def("clear_plans", &dli::Engine::clearPlans);
+
+  py::class_<dli::ProfileSession>(m, "ProfileSession")
+      .def(py::init([](bool cpu, bool gpu, bool record_shapes, std::size_t max_events) {
+             dli::ProfileConfig c;
+             c.cpu = cpu;
+             c.gpu = gpu;
+             c.record_shapes = record_shapes;
+             c.max_events = max_events;
+             return std::make_unique<dli::ProfileSession>(c);
+           }),
+           py::arg("cpu") = true, py::arg("gpu") = true, py::arg("record_shapes") = false,
+           py::arg("max_events") = 1000000)
+      .def(
+          "finalize",
+          [](dli::ProfileSession& p) {
+            py::gil_scoped_release release;
+            p.finalize();
+          })
+      .def("reserve", &dli::ProfileSession::reserve, py::arg("pairs"))
+      .def_property_readonly("finalized", &dli::ProfileSession::finalized)
+      .def("to_json", &dli::ProfileSession::toJson)
+      .def("write_json", &dli::ProfileSession::writeJson, py::arg("path"))
+      .def_property_readonly("num_events", [](const dli::ProfileSession& p) { return p.events().size(); })
+      .def_property_readonly("num_runs", [](const dli::ProfileSession& p) { return p.runs().size(); });
 
   m.def(
       "load_weights",

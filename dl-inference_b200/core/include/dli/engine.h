@@ -24,6 +24,13 @@ namespace dli {
 
 using TensorMap = std::map<std::string, Tensor>;
 
+class ProfileSession;
+
+// Per-run options (the reference's profiling design, .codex/profiling_design.md:141-160).
+struct RunOptions {
+  ProfileSession* profiler = nullptr;  // non-owning; times every node of the run when set
+};
+
 class Engine {
  public:
   Engine();
@@ -36,7 +43,7 @@ class Engine {
   KVCache& kvCache() { return kv_cache_; }
   const KVCache& kvCache() const { return kv_cache_; }
 
-  TensorMap run(const Graph& graph, TensorMap inputs);
+  TensorMap run(const Graph& graph, TensorMap inputs, const RunOptions& options = {});
 
   // Tensors bound to graph input names for every later run (e.g. weights), so a
   // run only passes what changes per call. Inputs passed to run() win.

@@ -20,6 +20,8 @@
 
 namespace dli {
 
+class ProfileSession;
+
 struct ExecutionContext {
   KVCache* kv_cache = nullptr;
   void* cuda_stream = nullptr;   // cudaStream_t every launch of this run goes to
@@ -27,6 +29,7 @@ struct ExecutionContext {
   void* communicator = nullptr;  // tensor-parallel communicator (ncclComm_t) or null
   int tp_rank = 0;
   int tp_size = 1;
+  ProfileSession* profiler = nullptr;  // the run's profiling session, if any
 };
 
 class Operator {

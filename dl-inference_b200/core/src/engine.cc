@@ -1,5 +1,7 @@
 #include "dli/engine.h"
 
+#include "dli/profile.h"
+
 #include <c10/cuda/CUDAStream.h>
 
 #include <algorithm>
@@ -102,7 +104,7 @@ Engine::Plan& Engine::planFor(const Graph& graph) {
   return ref;
 }
 
-TensorMap Engine::run(const Graph& graph, TensorMap inputs) {
+TensorMap Engine::run(const Graph& graph, TensorMap inputs, const RunOptions& options) {
   Plan& plan = planFor(graph);
   std::vector<Tensor> slots(plan.slot_names.size());
   for (const auto& [slot, tensor] : plan.constant_slots) slots[slot] = *tensor;
@@ -131,6 +133,9 @@ TensorMap Engine::run(const Graph& graph, TensorMap inputs) {
   ctx.communicator = comm_;
   ctx.tp_rank = tp_rank_;
   ctx.tp_size = tp_size_;
+  ProfileSession* prof = options.profiler;
+  ctx.profiler = prof;
+  const std::int64_t run_id = prof ? prof->beginRun() : -1;
 
   std::vector<const Tensor*> in;
   std::vector<Tensor> out_storage;
@@ -147,11 +152,27 @@ TensorMap Engine::run(const Graph& graph, TensorMap inputs) {
     out_storage.assign(step.out.size(), Tensor());
     out.clear();
     for (auto& t : out_storage) out.push_back(&t);
-    step.op->compute(in, out, step.node->attributes, ctx);
+    if (prof == nullptr) {
+      step.op->compute(in, out, step.node->attributes, ctx);
+    } else {
+      // a node is CUDA-backed when any of its inputs lives on the GPU
+      const bool cuda = device >= 0 && std::any_of(in.begin(), in.end(), [](const Tensor* t) { return t->isCuda(); });
+      const int node_index = static_cast<int>(&step - plan.steps.data());
+      const std::int64_t ev = prof->beginOperator(run_id, node_index, *step.node, cuda, ctx.device, ctx.cuda_stream, in);
+      try {
+        step.op->compute(in, out, step.node->attributes, ctx);
+      } catch (...) {
+        prof->endOperator(ev, false, out);
+        prof->endRun(run_id, false);
+        throw;
+      }
+      prof->endOperator(ev, true, out);
+    }
     for (std::size_t i = 0; i < step.out.size(); ++i) slots[step.out[i]] = std::move(out_storage[i]);
     for (const int s : step.release) slots[s] = Tensor();
   }
 
+  if (prof != nullptr) prof->endRun(run_id, true);
   TensorMap result;
   if (graph.outputs.empty()) {
     for (std::size_t i = 0; i < slots.size(); ++i)

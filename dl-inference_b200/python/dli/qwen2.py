@@ -40,12 +40,13 @@ class Qwen2Runner:
         self._graphs: dict[int, tuple] = {}
 
     # -- plain engine calls -------------------------------------------------------
-    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor):
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, profile=None):
         """input_ids [B,S] int64, positions [B] int64 (cache row of the first token).
         Returns (logits of the last token, next ids). With tensor parallelism over a
         vocabulary that divides evenly, the logits are this rank's slice of the
-        vocabulary (ids [rank*V/tp, (rank+1)*V/tp)); the next ids are global."""
-        out = self.engine.run(self.graph, {"input_ids": input_ids, "positions": positions})
+        vocabulary (ids [rank*V/tp, (rank+1)*V/tp)); the next ids are global.
+        `profile` (a dli.ProfileSession) times every node of the run."""
+        out = self.engine.run(self.graph, {"input_ids": input_ids, "positions": positions}, profile=profile)
         return out["logits"], out["next_ids"]
 
     def check_device_error(self) -> None:
@@ -65,6 +66,27 @@ class Qwen2Runner:
         self.engine.kv_cache_reset()
 
     # -- CUDA-graph decode ----------------------------------------------------------
+    def profile_decode_step(self, batch: int, profile) -> None:
+        """Captures one decode step with every node between CUDA-event markers,
+        replays it once and leaves the session holding that replay's per-node
+        device times (call profile.finalize() next). The step runs at the last
+        cache row, like the warm-up of the decode graph, so live sequences are
+        not disturbed. The markers make the step slower than the decode graph."""
+        ids = torch.zeros(batch, 1, dtype=torch.int64, device=self.device)
+        pos = torch.full((batch,), self.capacity - 1, dtype=torch.int64, device=self.device)
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            self.forward(ids, pos)
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        profile.reserve(len(self.graph.node_ops()))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.forward(ids, pos, profile=profile)
+        g.replay()
+        torch.cuda.synchronize(self.device)
+        del g
+
     def _capture(self, batch: int):
         # Warm-up and capture write one cache row per sequence; the last row is only
         # read after a later step has rewritten it, so live sequences are not disturbed.
