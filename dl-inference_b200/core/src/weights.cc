@@ -11,6 +11,12 @@
 #include <sstream>
 #include <stdexcept>
 
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <array>
+
 #include "json.h"
 
 namespace dli {
@@ -37,6 +43,63 @@ struct Mapping {
   }
 };
 
+void cudaCheck(cudaError_t err, const char* what) {
+  if (err != cudaSuccess) throw std::runtime_error(std::string("weights: ") + what + ": " + cudaGetErrorString(err));
+}
+
+// Host-to-device upload through a ring of pinned staging buffers: the mapped
+// file pages are copied into one buffer while the DMA engine drains the
+// previous ones (one cudaMemcpyAsync per chunk on a private stream), so file
+// reads and PCIe/C2C transfers overlap and every byte crosses host memory once.
+class DeviceUploader {
+ public:
+  static constexpr std::size_t kChunk = std::size_t(32) << 20;
+  static constexpr int kSlots = 4;
+
+  explicit DeviceUploader(int device) : guard_(static_cast<c10::DeviceIndex>(device)) {
+    cudaCheck(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+    for (int i = 0; i < kSlots; ++i) {
+      cudaCheck(cudaHostAlloc(&slot_[i], kChunk, cudaHostAllocDefault), "cudaHostAlloc");
+      cudaCheck(cudaEventCreateWithFlags(&done_[i], cudaEventDisableTiming), "cudaEventCreate");
+    }
+  }
+  ~DeviceUploader() {
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (int i = 0; i < kSlots; ++i) {
+      if (done_[i]) cudaEventDestroy(done_[i]);
+      if (slot_[i]) cudaFreeHost(slot_[i]);
+    }
+    if (stream_) cudaStreamDestroy(stream_);
+  }
+  DeviceUploader(const DeviceUploader&) = delete;
+  DeviceUploader& operator=(const DeviceUploader&) = delete;
+
+  void upload(void* dst, const char* src, std::size_t n) {
+    for (std::size_t off = 0; off < n; off += kChunk) {
+      const std::size_t len = std::min(kChunk, n - off);
+      const int s = next_++ % kSlots;
+      if (used_[s]) cudaCheck(cudaEventSynchronize(done_[s]), "cudaEventSynchronize");  // slot drained
+      std::memcpy(slot_[s], src + off, len);
+      cudaCheck(cudaMemcpyAsync(static_cast<char*>(dst) + off, slot_[s], len, cudaMemcpyHostToDevice, stream_),
+                "cudaMemcpyAsync");
+      cudaCheck(cudaEventRecord(done_[s], stream_), "cudaEventRecord");
+      used_[s] = true;
+      bytes_ += len;
+    }
+  }
+  void finish() { cudaCheck(cudaStreamSynchronize(stream_), "cudaStreamSynchronize"); }
+  std::size_t bytes() const { return bytes_; }
+
+ private:
+  c10::cuda::CUDAGuard guard_;
+  cudaStream_t stream_ = nullptr;
+  std::array<void*, kSlots> slot_{};
+  std::array<cudaEvent_t, kSlots> done_{};
+  std::array<bool, kSlots> used_{};
+  unsigned next_ = 0;
+  std::size_t bytes_ = 0;
+};
+
 }  // namespace
 
 TensorMap loadWeights(const std::string& manifest_path, DeviceType device, int device_id) {
@@ -57,6 +120,10 @@ TensorMap loadWeights(const std::string& manifest_path, DeviceType device, int d
 
   Mapping map(data.string());
   TensorMap result;
+  // declared after `result`: on an error the uploader drains its stream before
+  // the tensors it writes into are released
+  std::unique_ptr<DeviceUploader> uploader;
+  if (device != DeviceType::Cpu) uploader = std::make_unique<DeviceUploader>(device_id);
   for (const auto& [name, meta] : tensors.o) {
     if (meta.type != json::Value::Type::Object)
       throw std::invalid_argument("weights tensor metadata must be an object: " + name);
@@ -73,12 +140,21 @@ TensorMap loadWeights(const std::string& manifest_path, DeviceType device, int d
     }
     if (expect != nbytes)
       throw std::invalid_argument("weights tensor byte count does not match dtype and shape: " + name);
-    const auto opts = at::TensorOptions().dtype(torchDType(dtype)).device(at::kCPU);
-    at::Tensor host = at::empty(shape, opts);
-    if (nbytes) std::memcpy(host.data_ptr(), static_cast<const char*>(map.base) + offset, nbytes);
-    if (device == DeviceType::Cpu) result.emplace(name, Tensor(host));
-    else result.emplace(name, Tensor(host.to(at::Device(at::kCUDA, device_id))));
+    const char* src = static_cast<const char*>(map.base) + offset;
+    if (device == DeviceType::Cpu) {
+      at::Tensor host = at::empty(shape, at::TensorOptions().dtype(torchDType(dtype)).device(at::kCPU));
+      if (nbytes) std::memcpy(host.data_ptr(), src, nbytes);
+      result.emplace(name, Tensor(host));
+    } else {
+      // straight from the mapped file to the device tensor, no pageable copy
+      at::Tensor dev = at::empty(shape, at::TensorOptions().dtype(torchDType(dtype)).device(at::kCUDA, device_id));
+      if (nbytes) uploader->upload(dev.data_ptr(), src, nbytes);
+      result.emplace(name, Tensor(dev));
+    }
   }
+  // the device tensors are complete before they are returned (the caching
+  // allocator's streams never saw the private upload stream)
+  if (uploader) uploader->finish();
   return result;
 }
 

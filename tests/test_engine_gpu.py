@@ -121,3 +121,25 @@ def test_exported_files_run_through_load_weights(tmp_path):
     out = e.run(dli.Graph.from_json_file(str(gpath)), inputs)
     assert out["logits"].shape == (3, 1000) and out["next_ids"].shape == (3,)
     assert torch.equal(out["next_ids"], out["logits"].float().argmax(-1))
+
+
+def test_load_weights_to_device_matches_host_copy(tmp_path):
+    """The device loader (mapped file -> pinned staging ring -> device) gives the
+    bytes the host loader gives, for tensors larger than one staging chunk (the
+    ring wraps several times) and for small and empty ones."""
+    from dli_export.qwen2 import write_weights
+
+    g = torch.Generator().manual_seed(4)
+    tensors = {"big": torch.randn(9, 1 << 22, generator=g).to(torch.bfloat16),   # 72 MB
+               "mid": torch.randn(3000, 777, generator=g),
+               "ids": torch.arange(17, dtype=torch.int64),
+               "empty": torch.zeros(0, 8),
+               "half": torch.randn(5, 3, generator=g).half()}
+    path = write_weights(tensors, tmp_path, "w")
+    on_host = dli.load_weights(str(path), "cpu")
+    on_dev = dli.load_weights(str(path), "cuda")
+    assert set(on_dev) == set(tensors)
+    for name, t in tensors.items():
+        d = on_dev[name]
+        assert d.is_cuda and d.dtype == t.dtype and d.shape == t.shape, name
+        assert torch.equal(d.cpu(), on_host[name]) and torch.equal(d.cpu(), t), name
