@@ -6,7 +6,7 @@ dli.Engine running the exported dli.graph.v1 graph with the sm_100a plugin
 (decode replayed from a captured CUDA graph). Weights are random-init
 N(0, 0.02) of the named architecture (no checkpoints: synthetic data).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--model 7b|0.5b|72b]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--model 7b|0.5b|72b|linear|alexnet]
   python bench.py --impl reference ...     # the reference's CPU path (PyTorch eager)
 
 Multi-GPU (launched by torchrun, one rank per GPU): tensor parallelism over
@@ -47,6 +47,11 @@ MODELS = {
     "0.5b": ("QWEN2_0_5B", 8, 512, 256, 2),
     "72b": ("QWEN2_72B", 64, 4096, 512, 8),
 }
+# single-GPU operator / CNN workloads (replicas only under torchrun)
+SMALL = {
+    "linear": "single linear x[64,1024] . W[4096,1024]^T + b, fp32",
+    "alexnet": "AlexNet-style CNN forward, batch 64, 3x32x32, fp16",
+}
 
 
 def parse_args():
@@ -55,7 +60,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("sm100", "reference"), default="sm100")
-    ap.add_argument("--model", choices=sorted(MODELS), default="7b")
+    ap.add_argument("--model", choices=sorted(MODELS) + sorted(SMALL), default="7b")
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--prompt", type=int, default=None)
     ap.add_argument("--decode", type=int, default=None)
@@ -187,6 +192,189 @@ def workload_config(model: str, batch: int, prompt: int, dsteps: int) -> dict:
             "decode_steps": dsteps}
 
 
+# ---------------------------------------------------------------------------------
+# Single-GPU operator / CNN workloads: the single fp32 linear and the AlexNet-style CNN
+# ---------------------------------------------------------------------------------
+
+def _small_case(model: str, device):
+    """(engine graph dict, output name, constants, input, flops, algorithmic bytes, unit label)."""
+    import torch
+
+    if model == "linear":
+        g = torch.Generator(device=device).manual_seed(0)
+        x = torch.randn(64, 1024, device=device, generator=g)
+        w = torch.randn(4096, 1024, device=device, generator=g) * 0.02
+        b = torch.randn(4096, device=device, generator=g) * 0.02
+        graph = {"format": "dli.graph.v1", "model_type": "single_linear", "inputs": ["x"], "outputs": ["y"],
+                 "nodes": [{"name": "fc", "op": "linear", "inputs": ["x", "w", "b"], "outputs": ["y"], "attrs": {}}]}
+        nbytes = 4 * (4096 * 1024 + 64 * 1024 + 64 * 4096 + 4096)
+        return graph, "y", {"w": w, "b": b}, x, 2.0 * 64 * 1024 * 4096, nbytes, "calls/s"
+    from dli_export.cnn import alexnet_flops, alexnet_graph, alexnet_params
+
+    graph, out = alexnet_graph(64)
+    p, x = alexnet_params(torch.float16, 64, seed=0, device=device)
+    nbytes = 2 * (sum(t.numel() for t in p.values()) + x.numel() + 64 * 10)
+    return graph, out, p, x, alexnet_flops(64), nbytes, "images/s"
+
+
+def run_small(args, world: int, rank: int, local: int) -> int:
+    import torch
+    import torch.distributed as dist
+
+    import dli
+    import dli_sm100
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    graph, out_name, consts, x, flops, nbytes, unit = _small_case(args.model, dev)
+    units_per_step = 1 if args.model == "linear" else x.shape[0]
+    engine = dli.Engine()
+    engine.load_library(dli.PLUGIN_PATH)
+    engine.set_constants(consts)
+    g = dli.Graph.from_json(json.dumps(graph))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > the 126 MB L2
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return engine.run(g, {"x": x})[out_name]
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    n0 = dli_sm100.launch_count()
+    evs = []
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            flush.zero_()  # L2 flushed between timed steps, outside the timed span
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            step()
+            b.record(stream)
+            evs.append((a, b))
+        torch.cuda.synchronize()
+    launches = dli_sm100.launch_count() - n0
+    ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    try:
+        dli_sm100.check_device_error()
+        device_error = None
+    except RuntimeError as exc:
+        device_error = str(exc)
+    # e2e: input from pinned host memory, result read back, every step
+    host_x = x.cpu().pin_memory()
+    y0 = step()
+    host_y = torch.empty(y0.shape, dtype=y0.dtype, pin_memory=True)
+    e2e_ms = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        xd = host_x.to(dev, non_blocking=True)
+        host_y.copy_(engine.run(g, {"x": xd})[out_name], non_blocking=True)
+        b.record(stream)
+        stream.synchronize()
+        if i >= args.warmup:
+            e2e_ms.append(a.elapsed_time(b))
+    e2e = sum(e2e_ms) / len(e2e_ms)
+    pk = peaks()
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = small_cpu_baseline(args.model, seconds=15.0)
+        cpu.pop("ms_per_step", None)
+    if rank == 0:
+        tflops = flops / (ms / 1e3) / 1e12
+        gbs = nbytes / (ms / 1e3) / 1e9
+        fp32 = args.model == "linear"
+        line = {
+            "metric": f"{args.model} throughput ({unit})", "value": world * units_per_step / (ms / 1e3),
+            "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32" if fp32 else "f16",
+            "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) weights)",
+            "config": {"workload": SMALL[args.model], "model": args.model, "global_batch": 64 * world,
+                       "parallelism": f"replicas{world}" if world > 1 else "none",
+                       "l2": "flushed between timed steps (256 MB write outside the timed span)"},
+            "e2e": {"value": world * units_per_step / (e2e / 1e3), "unit": unit,
+                    "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
+                    "d2h_bytes_per_step": host_y.numel() * host_y.element_size(), "ms": e2e,
+                    "path": "dli.Engine.run with the input copied from pinned host memory and the output read back"},
+            "roofline": ({"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                          "frac": gbs / pk["hbm_gbs"], "traffic": None, "algorithmic_bytes": nbytes,
+                          "flops": flops, "TFLOP/s": tflops, "peak_source": pk["source"],
+                          "note": "fp32 runs on CUDA cores (exact fp32); the weight stream is the HBM floor"}
+                         if fp32 else
+                         {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                          "frac": tflops / pk["bf16_tflops"], "traffic": None, "flops": flops,
+                          "peak_source": pk["source"],
+                          "note": "whole forward (13 nodes) against the dense fp16/bf16 peak; launch-bound at batch 64"}),
+            "clocks": clocks.summary(), "cpu_baseline": cpu, "gpu_launches": launches,
+            "device_error": device_error,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 1 if device_error else 0
+
+
+def small_cpu_baseline(model: str, seconds: float = 15.0) -> dict:
+    """The reference's CPU path for these workloads: the linear as the aten::linear
+    node dispatches it (torch.nn.functional.linear, fp32) and the CNN as a PyTorch
+    eager forward (fp32 on the host: 16-bit convolutions are not a host fast path)."""
+    import torch
+
+    threads = torch.get_num_threads()
+    graph, out, consts, x, flops, _, unit = _small_case(model, "cpu")
+    if model == "linear":
+        fn = lambda: torch.nn.functional.linear(x, consts["w"], consts["b"])  # noqa: E731
+        per = 1
+        what = f"torch.nn.functional.linear fp32 [64,1024]x[4096,1024]^T + b on {threads} host threads"
+    else:
+        from dli_export.cnn import alexnet_forward
+
+        p32 = {k: v.float() for k, v in consts.items()}
+        x32 = x.float()
+        fn = lambda: alexnet_forward(p32, x32)  # noqa: E731
+        per = x.shape[0]
+        what = f"AlexNet-style forward, PyTorch eager fp32, batch 64, on {threads} host threads"
+    with torch.no_grad():
+        fn()
+        n, t0 = 0, time.perf_counter()
+        while n < 2 or time.perf_counter() - t0 < seconds:
+            fn()
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+    return {"value": per / dt, "unit": unit, "cores": threads, "kind": "reference",
+            "sample": f"{what}: {n} calls", "ms_per_step": dt * 1e3}
+
+
+def run_small_reference(args, world: int, rank: int) -> int:
+    if rank != 0:
+        return 0
+    vals = [small_cpu_baseline(args.model, seconds=max(2.0, 40.0 / (args.steps + args.warmup)))
+            for _ in range(args.warmup + args.steps)][args.warmup:]
+    value = statistics.median(v["value"] for v in vals)
+    unit = vals[0]["unit"]
+    line = {"metric": f"{args.model} throughput ({unit})", "impl": "reference", "value": value, "unit": unit,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": statistics.median(v["ms_per_step"] for v in vals), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) inputs, N(0,0.02) weights)",
+            "config": {"workload": SMALL[args.model], "model": args.model, "global_batch": 64,
+                       "parallelism": "none (host cores)"},
+            "cpu_baseline": {k: vals[-1][k] for k in ("kind", "cores", "sample")} | {"value": value, "unit": unit},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
 def run_reference_arm(args, world: int, rank: int):
     from dli_export import qwen2 as Q
 
@@ -229,6 +417,10 @@ def main() -> int:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.model in SMALL:
+        if args.impl == "reference":
+            return run_small_reference(args, world, rank)
+        return run_small(args, world, rank, local)
     if args.impl == "reference":
         return run_reference_arm(args, world, rank)
 

@@ -32,59 +32,22 @@ import model_parity
 
 pytestmark = pytest.mark.gpu
 
-CONVS = [(3, 64, True), (64, 192, True), (192, 384, False), (384, 256, False), (256, 256, True)]
-FCS = [(4096, 4096, True), (4096, 4096, True), (4096, 10, False)]
-
-
 def _alexnet_graph():
-    nodes, x = [], "x"
+    from dli_export.cnn import alexnet_graph
 
-    def node(op, inputs, attrs=None):
-        nonlocal x
-        out = f"t{len(nodes)}"
-        nodes.append({"name": out, "op": op, "inputs": inputs, "outputs": [out], "attrs": attrs or {}})
-        x = out
-
-    for i, (_, _, pool) in enumerate(CONVS):
-        node("conv2d", [x, f"conv{i}.w", f"conv{i}.b"], {"stride": [1, 1], "padding": [1, 1]})
-        node("relu", [x])
-        if pool:
-            node("max_pool2d", [x], {"kernel_size": [2, 2], "stride": [2, 2]})
-    node("reshape", [x], {"shape": [64, 4096]})
-    for i, (_, _, act) in enumerate(FCS):
-        node("linear", [x, f"fc{i}.w", f"fc{i}.b"])
-        if act:
-            node("relu", [x])
-    return {"format": "dli.graph.v1", "model_type": "alexnet_style", "inputs": ["x"], "outputs": [x],
-            "nodes": nodes}, x
+    return alexnet_graph(64)
 
 
 def _alexnet_params(dtype):
-    g = torch.Generator().manual_seed(0)
-    p = {}
-    for i, (c, oc, _) in enumerate(CONVS):
-        p[f"conv{i}.w"] = (torch.randn(oc, c, 3, 3, generator=g) * 0.02).to(dtype)
-        p[f"conv{i}.b"] = (torch.randn(oc, generator=g) * 0.02).to(dtype)
-    for i, (k, n, _) in enumerate(FCS):
-        p[f"fc{i}.w"] = (torch.randn(n, k, generator=g) * 0.02).to(dtype)
-        p[f"fc{i}.b"] = (torch.randn(n, generator=g) * 0.02).to(dtype)
-    x = torch.randn(64, 3, 32, 32, generator=g).to(dtype)
-    return p, x
+    from dli_export.cnn import alexnet_params
+
+    return alexnet_params(dtype, 64, seed=0)
 
 
 def _alexnet_reference(p, x):
-    F = torch.nn.functional
-    h = x.double()
-    for i, (_, _, pool) in enumerate(CONVS):
-        h = F.relu(F.conv2d(h, p[f"conv{i}.w"].double(), p[f"conv{i}.b"].double(), padding=1))
-        if pool:
-            h = F.max_pool2d(h, 2)
-    h = h.reshape(64, 4096)
-    for i, (_, _, act) in enumerate(FCS):
-        h = F.linear(h, p[f"fc{i}.w"].double(), p[f"fc{i}.b"].double())
-        if act:
-            h = F.relu(h)
-    return h
+    from dli_export.cnn import alexnet_forward
+
+    return alexnet_forward({k: v.double() for k, v in p.items()}, x.double())
 
 
 @pytest.mark.parametrize("dtype,tol", [(torch.float16, 1e-2), (torch.float32, 1e-4)], ids=["f16", "f32"])
