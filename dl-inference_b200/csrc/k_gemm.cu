@@ -644,6 +644,184 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ---- exact fp32 GEMM on CUDA cores, split-K over a thread-block cluster ----------
+// out[M,N] = A[M,K] . B + bias with B as [N,K] (linear) or [K,N] (matmul), fp32
+// FFMA in the reference's accumulation precision (its tl.dot runs fp32 as TF32,
+// 1e-3 relative; this kernel is exact fp32). CTA tile 64 x 128, 256 threads of
+// 4 x 8 outputs, K in 16-deep slices double-buffered in shared memory (16-byte
+// global loads). Skinny problems (decode-sized M) split K over S <= 8 CTAs that
+// form one thread-block cluster: each stages its fp32 partial tile in its own
+// shared memory, and after a cluster barrier CTA r sums rows r*64/S.. of all S
+// partials in rank order through distributed shared memory (deterministic, no
+// workspace, no second launch).
+constexpr int kF32BM = 64, kF32BN = 128, kF32BK = 16, kF32Threads = 256;
+constexpr int kF32AStride = kF32BM + 4, kF32BStride = kF32BN + 4;
+constexpr int kF32StageFloats = kF32BK * (kF32AStride + kF32BStride);
+constexpr int kF32RedStride = kF32BN + 4;
+constexpr int kF32SmemBytes =
+    (2 * kF32StageFloats > kF32BM * kF32RedStride ? 2 * kF32StageFloats : kF32BM * kF32RedStride) * 4;
+
+struct F32GemmArgs {
+  const float* a;
+  const float* b;
+  const float* bias;
+  float* out;
+  int m, n, k;
+  int tiles_n;   // tiles along N (grid.x = tiles_n * tiles_m)
+  int splits;    // cluster size along grid.y
+  int kchunk;    // K elements per split (a multiple of kF32BK)
+};
+
+template <bool kBKMajor>
+__global__ void __launch_bounds__(kF32Threads)
+    gemm_f32_cluster_kernel(const F32GemmArgs p) {
+  DLI_PDL_ENTRY();
+  extern __shared__ __align__(16) float f32_smem[];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;  // 16 x 16 threads: 8 columns x 4 rows each
+  const int tile_n = blockIdx.x % p.tiles_n, tile_m = blockIdx.x / p.tiles_n;
+  const int m0 = tile_m * kF32BM, n0 = tile_n * kF32BN;
+  const int split = blockIdx.y;
+  const int k_begin = split * p.kchunk;
+  const int k_end = min(p.k, k_begin + p.kchunk);
+
+  float acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+  // register staging of the next K slice (global -> registers -> shared)
+  float4 ra, rb[2];
+  auto fetch = [&](int k0) {
+    {  // A: 64 rows x 16 k, one float4 per thread
+      const int r = tid >> 2, kq = (tid & 3) * 4;
+      const int gr = m0 + r, gk = k0 + kq;
+      ra = (gr < p.m && gk < k_end) ? *reinterpret_cast<const float4*>(p.a + static_cast<int64_t>(gr) * p.k + gk)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int idx = tid + h * kF32Threads;
+      if constexpr (kBKMajor) {  // B [N,K]: 128 rows x 16 k
+        const int r = idx >> 2, kq = (idx & 3) * 4;
+        const int gn = n0 + r, gk = k0 + kq;
+        rb[h] = (gn < p.n && gk < k_end) ? *reinterpret_cast<const float4*>(p.b + static_cast<int64_t>(gn) * p.k + gk)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+      } else {  // B [K,N]: 16 k rows x 128 columns
+        const int kr = idx >> 5, nq = (idx & 31) * 4;
+        const int gk = k0 + kr, gn = n0 + nq;
+        rb[h] = (gk < k_end && gn < p.n) ? *reinterpret_cast<const float4*>(p.b + static_cast<int64_t>(gk) * p.n + gn)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  };
+  auto stash = [&](int buf) {
+    float* as = f32_smem + buf * kF32StageFloats;
+    float* bs = as + kF32BK * kF32AStride;
+    {
+      const int r = tid >> 2, kq = (tid & 3) * 4;
+      as[(kq + 0) * kF32AStride + r] = ra.x;
+      as[(kq + 1) * kF32AStride + r] = ra.y;
+      as[(kq + 2) * kF32AStride + r] = ra.z;
+      as[(kq + 3) * kF32AStride + r] = ra.w;
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int idx = tid + h * kF32Threads;
+      if constexpr (kBKMajor) {
+        const int r = idx >> 2, kq = (idx & 3) * 4;
+        bs[(kq + 0) * kF32BStride + r] = rb[h].x;
+        bs[(kq + 1) * kF32BStride + r] = rb[h].y;
+        bs[(kq + 2) * kF32BStride + r] = rb[h].z;
+        bs[(kq + 3) * kF32BStride + r] = rb[h].w;
+      } else {
+        const int kr = idx >> 5, nq = (idx & 31) * 4;
+        *reinterpret_cast<float4*>(bs + kr * kF32BStride + nq) = rb[h];
+      }
+    }
+  };
+
+  const int slices = (k_end - k_begin + kF32BK - 1) / kF32BK;
+  if (slices > 0) {
+    fetch(k_begin);
+    stash(0);
+  }
+  __syncthreads();
+  for (int s = 0; s < slices; ++s) {
+    const int buf = s & 1;
+    if (s + 1 < slices) fetch(k_begin + (s + 1) * kF32BK);  // loads in flight during the FFMAs
+    const float* as = f32_smem + buf * kF32StageFloats;
+    const float* bs = as + kF32BK * kF32AStride;
+#pragma unroll
+    for (int kk = 0; kk < kF32BK; ++kk) {
+      const float4 av = *reinterpret_cast<const float4*>(as + kk * kF32AStride + ty * 4);
+      const float4 b0 = *reinterpret_cast<const float4*>(bs + kk * kF32BStride + tx * 8);
+      const float4 b1 = *reinterpret_cast<const float4*>(bs + kk * kF32BStride + tx * 8 + 4);
+      const float a4[4] = {av.x, av.y, av.z, av.w};
+      const float b8[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a4[i], b8[j], acc[i][j]);
+    }
+    if (s + 1 < slices) stash(buf ^ 1);
+    __syncthreads();
+  }
+
+  auto store = [&](int row, int col0, const float* v) {
+    if (row >= p.m) return;
+    float* dst = p.out + static_cast<int64_t>(row) * p.n + col0;
+    if (col0 + 8 <= p.n && (p.n & 3) == 0) {
+      float4 o0 = make_float4(v[0], v[1], v[2], v[3]), o1 = make_float4(v[4], v[5], v[6], v[7]);
+      if (p.bias) {
+        const float4 c0 = *reinterpret_cast<const float4*>(p.bias + col0);
+        const float4 c1 = *reinterpret_cast<const float4*>(p.bias + col0 + 4);
+        o0.x += c0.x; o0.y += c0.y; o0.z += c0.z; o0.w += c0.w;
+        o1.x += c1.x; o1.y += c1.y; o1.z += c1.z; o1.w += c1.w;
+      }
+      *reinterpret_cast<float4*>(dst) = o0;
+      *reinterpret_cast<float4*>(dst + 4) = o1;
+    } else {
+      for (int j = 0; j < 8 && col0 + j < p.n; ++j) dst[j] = v[j] + (p.bias ? p.bias[col0 + j] : 0.f);
+    }
+  };
+
+  if (p.splits == 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) store(m0 + ty * 4 + i, n0 + tx * 8, acc[i]);
+    return;
+  }
+  // split-K: partial tile into this CTA's shared memory, then a cluster reduction
+  float* red = f32_smem;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float* row = red + (ty * 4 + i) * kF32RedStride + tx * 8;
+    *reinterpret_cast<float4*>(row) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    *reinterpret_cast<float4*>(row + 4) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+  }
+  cluster_sync();
+  const int S = p.splits;
+  const int rows_per = (kF32BM + S - 1) / S;
+  const uint32_t red_local = static_cast<uint32_t>(__cvta_generic_to_shared(red));
+  // rank `split` sums rows [split*rows_per, ...) of every rank's partial, 8 columns per thread
+  for (int q = tid; q < rows_per * (kF32BN / 8); q += kF32Threads) {
+    const int rr = split * rows_per + q / (kF32BN / 8);
+    const int c8 = (q % (kF32BN / 8)) * 8;
+    if (rr >= kF32BM) continue;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < S; ++r) {
+      const uint32_t off = static_cast<uint32_t>((rr * kF32RedStride + c8) * 4);
+      const float4 x0 = ld_dsmem_f4(mapa_shared(red_local + off, r));
+      const float4 x1 = ld_dsmem_f4(mapa_shared(red_local + off + 16, r));
+      v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
+      v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+    }
+    store(m0 + rr, n0 + c8, v);
+  }
+  cluster_sync();  // every rank's shared memory stays alive until all reads are done
+}
+
 // ---- host helpers ---------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -906,9 +1084,41 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
   return launch_tc_bn<__half>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
 }
 
+// Cluster split-K fp32 GEMM: true when it served the call (fp32, 16-byte aligned
+// operands, K and the [K,N] row stride multiples of 4 elements).
+bool try_gemm_f32(const void* a, const void* b, const void* bias, void* out, int64_t m, int64_t n, int64_t k,
+                  bool b_kmajor, cudaStream_t stream, dli_status* status) {
+  static const bool on = tuning_knob("GEMM_F32", 1) != 0;
+  if (!on || k % 4 != 0 || (!b_kmajor && n % 4 != 0) || !aligned(a, 16) || !aligned(b, 16) || !aligned(out, 16) ||
+      (bias && !aligned(bias, 16)) || m > (1 << 30) || n > (1 << 30) || k > (1 << 30))
+    return false;
+  const int64_t tiles = ceil_div(n, kF32BN) * ceil_div(m, kF32BM);
+  if (tiles > 0x7fffffff) return false;
+  // splits: enough CTAs for two per SM, each split keeping >= 256 K elements
+  const int64_t target = 2 * static_cast<int64_t>(sm_count());
+  int splits = static_cast<int>(std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(target, tiles))));
+  splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(splits, k / 256)));
+  const int kchunk = static_cast<int>(ceil_div(ceil_div(k, splits), kF32BK) * kF32BK);
+  splits = static_cast<int>(ceil_div(k, kchunk));
+  F32GemmArgs args{static_cast<const float*>(a), static_cast<const float*>(b), static_cast<const float*>(bias),
+                   static_cast<float*>(out), static_cast<int>(m), static_cast<int>(n), static_cast<int>(k),
+                   static_cast<int>(ceil_div(n, kF32BN)), splits, kchunk};
+  auto kern = b_kmajor ? gemm_f32_cluster_kernel<true> : gemm_f32_cluster_kernel<false>;
+  *status = ensure_smem(reinterpret_cast<const void*>(kern), kF32SmemBytes, "fp32 gemm");
+  if (*status != DLI_OK) return true;
+  launch_pdl_cluster(kern, dim3(static_cast<unsigned>(tiles), static_cast<unsigned>(splits)), dim3(kF32Threads),
+                     kF32SmemBytes, stream, static_cast<unsigned>(splits), args);
+  *status = check_launch("fp32 gemm");
+  return true;
+}
+
 dli_status run_gemm_simt(const void* a, const void* b, const void* bias, void* out, int64_t m,
                          int64_t n, int64_t k, bool b_kmajor, dli_dtype dtype,
                          cudaStream_t stream) {
+  if (dtype == DLI_DTYPE_F32) {
+    dli_status st = DLI_OK;
+    if (try_gemm_f32(a, b, bias, out, m, n, k, b_kmajor, stream, &st)) return st;
+  }
   if (ceil_div(m, kSimtTile) > 65535) return fail(DLI_ERR_UNSUPPORTED, "gemm: too many rows for SIMT path");
   dim3 grid(static_cast<unsigned>(ceil_div(n, kSimtTile)), static_cast<unsigned>(ceil_div(m, kSimtTile)));
   dli_status st = dispatch_float(dtype, "gemm", [&](auto tag) {

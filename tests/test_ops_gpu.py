@@ -153,6 +153,34 @@ def test_linear_fp32_config1():
     assert np.abs(y.cpu().double().numpy() - ref).max() <= 1e-4 * np.abs(ref).max()
 
 
+@pytest.mark.parametrize("m,n,k", [(64, 4096, 1024), (32, 4608, 3584), (32, 3584, 18944), (1, 10, 4096),
+                                   (70, 130, 52), (4096, 256, 64), (3, 7, 5), (129, 1000, 260)])
+def test_linear_fp32_split_k_shapes(m, n, k):
+    """Exact-fp32 linear at decode-sized, ragged and odd-K shapes (the cluster
+    split-K FFMA kernel, or the scalar kernel where K is not a multiple of 4)."""
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n + k)
+    x = torch.randn(m, k, device="cuda", generator=g)
+    w = torch.randn(n, k, device="cuda", generator=g) * 0.02
+    b = torch.randn(n, device="cuda", generator=g) * 0.02
+    y = C.linear(x, w, b)
+    y2 = C.linear(x, w, b)
+    ref = torch.nn.functional.linear(x.double(), w.double(), b.double())
+    assert_close(y, ref, torch.float32, f"linear fp32 {m}x{n}x{k}")
+    assert torch.equal(y, y2)  # deterministic split-K reduction
+
+
+@pytest.mark.parametrize("m,n,k", [(70, 132, 52), (64, 4096, 1024), (33, 257, 4000), (5, 12, 3), (16, 512, 8192)])
+def test_matmul_fp32_shapes(m, n, k):
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(m + n * 3 + k)
+    a = torch.randn(m, k, device="cuda", generator=g)
+    b = torch.randn(k, n, device="cuda", generator=g) * 0.05
+    assert_close(C.matmul(a, b), a.double() @ b.double(), torch.float32, f"matmul fp32 {m}x{n}x{k}")
+
+
 def test_matmul_bf16_and_f32():
     import dli_sm100 as C
 
