@@ -605,7 +605,7 @@ def main() -> int:
     launches = args.steps * (launches_prefill + dsteps * launches_decode)
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:  # timed at N=1 only (all host threads)
         try:
             cpu = cpu_baseline(shape, total_seqs, prompt, seconds=20.0)
             cpu.pop("ms_per_step", None)
