@@ -24,7 +24,14 @@ struct GemmPlan {
   int kblocks = 0;
   bool tcgen05 = false;   // false -> SIMT fallback
   size_t workspace = 0;   // bytes of split-K scratch (partials + tile counters)
+  int streamk_ctas = 0;   // > 0: stream-K over this many CTAs (tcgen05_gemm_streamk_kernel)
 };
+
+// Turns a swap-AB decode plan (tile width <= 64) whose tiles do not fill whole
+// waves into a stream-K plan over every resident slot; sets streamk_ctas and
+// workspace (partial tiles + per-tile counters, zero-filled by the caller once
+// and left zeroed). Leaves other plans unchanged.
+GemmPlan plan_streamk(GemmPlan plan);
 
 // Occupancy of the tcgen05 GEMM with tile width bn and `stages` pipeline stages:
 // CTAs per SM for cluster <= 1, else resident clusters of `cluster` CTAs

@@ -61,6 +61,10 @@ struct TcParams {
   int const_b;  // same for operand B
   int glu_cols; // SwiGLU epilogues: valid output columns (the intermediate size)
   int out_f32;  // RowMajor / Transposed: the output is float32 (operands stay T)
+  // stream-K (tcgen05_gemm_streamk_kernel): partial tiles [ctas][2][128][BN] fp32
+  // and one arrival counter per tile, zero between calls
+  float* sk_part;
+  int* sk_count;
   const void* bias;
   void* out;
   unsigned* err;
@@ -589,6 +593,261 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ---- stream-K GEMM for decode-sized (swap-AB) problems ----------------------------
+// The (tile, K block) work units of a skinny GEMM are split evenly over P CTAs
+// (P = every resident slot of the GPU, two per SM), so every SM streams the same
+// number of weight bytes whatever the tile count: a CTA's contiguous unit range
+// may end inside one tile and start inside another. A CTA that covers a whole
+// tile stores it directly; a CTA holding part of a tile writes its fp32 partial
+// to the workspace and counts itself in; the last arrival sums the partials of
+// all contributors in CTA order (a fixed order, so the result is deterministic)
+// and stores the tile. No CTA waits for another, and no thread-block clusters
+// constrain where CTAs may run, so the next kernel's CTAs (programmatic
+// dependent launch) start on every SM as soon as this kernel's leave it.
+// Accumulators are double-buffered in TMEM: the MMA warp starts a CTA's next
+// segment while the epilogue drains the previous one.
+template <int BN, int STAGES>
+struct StreamKLayout {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kXchOffset = (kBarOffset + (2 * STAGES + 4) * 8 + 16 + 127) / 128 * 128;
+  static constexpr int kXchFloats = 64 * (BN + 1);  // SwiGLU: up rows handed to the gate rows
+  static constexpr int kBytes = kXchOffset + kXchFloats * 4 + 1024;
+  static constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+  static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KiB alignment");
+};
+
+// First work unit of CTA c when U units are split over P CTAs.
+__device__ __forceinline__ int64_t sk_begin(int64_t c, int64_t units, int64_t ctas) { return c * units / ctas; }
+// The CTA whose unit range holds unit u.
+__device__ __forceinline__ int sk_owner(int64_t u, int64_t units, int64_t ctas) {
+  int64_t c = u * ctas / units;
+  while (c + 1 < ctas && sk_begin(c + 1, units, ctas) <= u) ++c;
+  while (c > 0 && sk_begin(c, units, ctas) > u) --c;
+  return static_cast<int>(c);
+}
+
+template <typename T, int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    tcgen05_gemm_streamk_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
+  using L = StreamKLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort, [1] last arrival
+  float* xch = reinterpret_cast<float*>(smem + L::kXchOffset);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t units = static_cast<int64_t>(p.tiles_i) * p.tiles_j * p.kblocks;
+  const int64_t ctas = gridDim.x;
+  const int c = blockIdx.x;
+  const int64_t u_begin = sk_begin(c, units, ctas), u_end = sk_begin(c + 1, units, ctas);
+  const int first_tile = static_cast<int>(u_begin / p.kblocks);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    flags[0] = 0;
+    flags[1] = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // the weight tiles of the first stages do not depend on the previous kernel
+      int issued = 0;
+      const int pre = p.const_a ? static_cast<int>((u_end - u_begin < STAGES ? u_end - u_begin : STAGES)) : 0;
+      for (int it = 0; it < pre; ++it) {
+        const int64_t u = u_begin + it;
+        int ti, tj;
+        tile_coords(static_cast<int>(u / p.kblocks), p.tiles_i, p.tiles_j, ti, tj);
+        mbar_arrive_expect_tx(&full[it], L::kStageBytes);
+        tma_load_2d(smem + it * L::kStageBytes, &tmap_a, static_cast<int>(u % p.kblocks) * kBK, ti * kBM, &full[it]);
+      }
+      pdl_wait();
+      pdl_trigger();
+      for (int64_t u = u_begin; u < u_end; ++u) {
+        const int it = static_cast<int>(u - u_begin);
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        int ti, tj;
+        tile_coords(static_cast<int>(u / p.kblocks), p.tiles_i, p.tiles_j, ti, tj);
+        const int kx = static_cast<int>(u % p.kblocks) * kBK;
+        uint8_t* sa = smem + s * L::kStageBytes;
+        if (it < pre) {  // armed above: add the activations
+          tma_load_2d(sa + L::kABytes, &tmap_b, kx, tj * BN, &full[s]);
+          issued = it + 1;
+          continue;
+        }
+        if (!mbar_wait(&empty[s], ph ^ 1)) {
+          set_device_error(p.err, kDevErrGemmTimeout);
+          flags[0] = 1;
+        }
+        if (flags[0]) break;
+        mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+        tma_load_2d(sa, &tmap_a, kx, ti * kBM, &full[s]);
+        tma_load_2d(sa + L::kABytes, &tmap_b, kx, tj * BN, &full[s]);
+        issued = it + 1;
+      }
+      // No bulk copy may still be writing shared memory when the CTA exits.
+      for (int it = max(0, issued - STAGES); it < issued; ++it) mbar_wait(&full[it % STAGES], (it / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, BN);
+      int64_t u = u_begin;
+      for (int ls = 0; u < u_end && !flags[0]; ++ls) {
+        const int buf = ls & 1;
+        const int64_t seg_end = u_end < (u / p.kblocks + 1) * p.kblocks ? u_end : (u / p.kblocks + 1) * p.kblocks;
+        if (!mbar_wait(&acc_empty[buf], ((ls >> 1) & 1) ^ 1) || flags[0]) {
+          set_device_error(p.err, kDevErrGemmTimeout);
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem_base + static_cast<uint32_t>(buf * BN);
+        bool first = true;
+        for (; u < seg_end; ++u) {
+          const int it = static_cast<int>(u - u_begin);
+          const int s = it % STAGES;
+          if (!mbar_wait(&full[s], (it / STAGES) & 1)) {
+            set_device_error(p.err, kDevErrGemmTimeout);
+            flags[0] = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
+          const uint64_t adesc = umma_desc_sw128(a_addr);
+          const uint64_t bdesc = umma_desc_sw128(a_addr + L::kABytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (!first || kk > 0) ? 1u : 0u);
+          first = false;
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // TMEM lane = weight row of the tile
+    int64_t u = u_begin;
+    for (int ls = 0; u < u_end; ++ls) {
+      const int buf = ls & 1;
+      const int tile = static_cast<int>(u / p.kblocks);
+      const int64_t tile_u0 = static_cast<int64_t>(tile) * p.kblocks;
+      const int64_t seg_end = u_end < tile_u0 + p.kblocks ? u_end : tile_u0 + p.kblocks;
+      const bool whole = u == tile_u0 && seg_end == tile_u0 + p.kblocks;
+      u = seg_end;
+      if (!mbar_wait(&acc_full[buf], (ls >> 1) & 1)) {
+        set_device_error(p.err, kDevErrGemmTimeout);
+        flags[0] = 1;
+      }
+      tc_fence_after();
+      epilogue_bar();  // every epilogue warp sees the same abort flag
+      if (flags[0]) break;
+      float v[BN];
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
+#pragma unroll
+      for (int cc = 0; cc < BN; cc += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + cc, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[cc + k] = __uint_as_float(r[k]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);  // the MMA warp may reuse this buffer
+      if (!whole) {
+        // partial tile: publish it, count in, and the last contributor sums all of them
+        const int slot = tile == first_tile ? 0 : 1;
+        float* mine = p.sk_part + ((static_cast<int64_t>(c) * 2 + slot) * kBM + row) * BN;
+#pragma unroll
+        for (int cc = 0; cc < BN; cc += 4)
+          __stcg(reinterpret_cast<float4*>(mine + cc), make_float4(v[cc], v[cc + 1], v[cc + 2], v[cc + 3]));
+        __threadfence();
+        epilogue_bar();
+        const int c_first = sk_owner(tile_u0, units, ctas);
+        const int c_last = sk_owner(tile_u0 + p.kblocks - 1, units, ctas);
+        if (row == 0) flags[1] = atomicAdd(p.sk_count + tile, 1) == c_last - c_first;
+        epilogue_bar();
+        const bool last = flags[1] != 0;
+        if (!last) continue;
+        __threadfence();
+#pragma unroll
+        for (int k = 0; k < BN; ++k) v[k] = 0.f;
+        for (int cc2 = c_first; cc2 <= c_last; ++cc2) {  // CTA order: a fixed summation order
+          const int ctile = static_cast<int>(sk_begin(cc2, units, ctas) / p.kblocks);
+          const float* src = p.sk_part + ((static_cast<int64_t>(cc2) * 2 + (tile == ctile ? 0 : 1)) * kBM + row) * BN;
+#pragma unroll
+          for (int cc = 0; cc < BN; cc += 4) {
+            const float4 x = __ldcg(reinterpret_cast<const float4*>(src + cc));
+            v[cc] += x.x;
+            v[cc + 1] += x.y;
+            v[cc + 2] += x.z;
+            v[cc + 3] += x.w;
+          }
+        }
+        if (row == 0) p.sk_count[tile] = 0;  // ready for the next call (graph replays included)
+      }
+      // the finished tile
+      int ti, tj;
+      tile_coords(tile, p.tiles_i, p.tiles_j, ti, tj);
+      const int64_t gi = static_cast<int64_t>(ti) * kBM + row;
+      if (p.epilogue == kEpiGluT) {
+        if (quarter >= 2) {
+#pragma unroll
+          for (int k = 0; k < BN; ++k) xch[(row - 64) * (BN + 1) + k] = v[k];
+        }
+        epilogue_bar();
+        if (quarter < 2) {
+          const float* up = xch + row * (BN + 1);
+          store_glu_t<T>(p, ti, row, tj * BN, v, up, BN);
+        }
+        epilogue_bar();
+      } else {
+#pragma unroll
+        for (int cc = 0; cc < BN; cc += 32)
+          if (tj * BN + cc < p.rows_b) store_vals<T>(p, gi, tj * BN + cc, v + cc, 32);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
 // ---- SIMT fallback -----------------------------------------------------------
 constexpr int kSimtTile = 64;
 constexpr int kSimtK = 16;
@@ -901,6 +1160,21 @@ dli_status launch_tc_persistent(const CUtensorMap& ma, const CUtensorMap& mb, co
   return check_launch("tcgen05 gemm");
 }
 
+template <typename T, int BN, int STAGES>
+dli_status launch_tc_streamk(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p, int ctas,
+                             cudaStream_t stream) {
+  using L = StreamKLayout<BN, STAGES>;
+  auto kernel = tcgen05_gemm_streamk_kernel<T, BN, STAGES>;
+  const dli_status st = ensure_smem(reinterpret_cast<const void*>(kernel), L::kBytes, "tcgen05 gemm");
+  if (st != DLI_OK) return st;
+  launch_pdl(kernel, dim3(static_cast<unsigned>(ctas)), dim3(kGemmThreads), L::kBytes, stream, ma, mb, p);
+  return check_launch("tcgen05 gemm (stream-K)");
+}
+
+// Stream-K stage counts: two CTAs per SM (~110 KB each) at tile widths 32 and 64.
+constexpr int kStreamKStages32 = 5;
+constexpr int kStreamKStages64 = 3;
+
 // Persistent double-buffered kernel for many-tile, un-split, row-per-thread
 // epilogues (prefill projections, conv); DLI_SM100_GEMM_PERSISTENT=0 disables it.
 bool use_persistent(const GemmPlan& plan, int epilogue) {
@@ -1041,6 +1315,43 @@ GemmPlan plan_tn_gemm(int64_t rows_a, int64_t rows_b, int64_t k, dli_dtype dtype
   return plan;
 }
 
+GemmPlan plan_streamk(GemmPlan plan) {
+  static const bool on = tuning_knob("GEMM_STREAMK", 0) != 0;  // off: measured slower than cluster split-K
+  if (!on || !plan.tcgen05 || (plan.bn != 32 && plan.bn != 64) || plan.kblocks < 2) return plan;
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, int> occ_cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return plan;
+  }
+  int occ = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(dev, plan.bn);
+    auto it = occ_cache.find(key);
+    if (it != occ_cache.end()) {
+      occ = it->second;
+    } else {
+      const int bytes = plan.bn == 32 ? StreamKLayout<32, kStreamKStages32>::kBytes
+                                      : StreamKLayout<64, kStreamKStages64>::kBytes;
+      occ = query_occupancy(bytes, 1);
+      occ_cache[key] = occ;
+    }
+  }
+  if (occ <= 0) return plan;
+  const int64_t slots = static_cast<int64_t>(sm_count()) * std::min(occ, 2);
+  const int64_t tiles = static_cast<int64_t>(plan.tiles_i) * plan.tiles_j;
+  if (tiles % slots == 0) return plan;  // whole waves already: the data-parallel launch is balanced
+  const int64_t units = tiles * plan.kblocks;
+  const int64_t ctas = std::min<int64_t>(slots, units);
+  plan.streamk_ctas = static_cast<int>(ctas);
+  plan.splits = 1;
+  const size_t partial = static_cast<size_t>(ctas) * 2 * kBM * plan.bn * sizeof(float);
+  plan.workspace = (partial + static_cast<size_t>(tiles) * sizeof(int) + 255) / 256 * 256;
+  return plan;
+}
+
 dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, void* out,
                                int64_t rows_a, int64_t rows_b, int64_t k, int64_t lda,
                                int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,
@@ -1052,8 +1363,10 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
     return fail(DLI_ERR_UNSUPPORTED, "gemm: float32 output only for plain row-major/transposed epilogues");
   if (!aligned(a, 16) || !aligned(b, 16) || lda % 8 != 0 || ldb % 8 != 0)
     return fail(DLI_ERR_UNSUPPORTED, "gemm: TMA needs 16-byte aligned operands and row strides");
-  (void)workspace;
-  (void)workspace_bytes;
+  if (plan.streamk_ctas > 0 && (workspace == nullptr || workspace_bytes < plan.workspace ||
+                                epilogue == kEpiRowMajor || epilogue == kEpiNchw || epilogue == kEpiGlu))
+    return fail(DLI_ERR_WORKSPACE, "gemm: the stream-K plan needs a zero-filled workspace of " +
+                                       std::to_string(plan.workspace) + " bytes");
   const bool bf16 = dtype == DLI_DTYPE_BF16;
   CUtensorMap ma, mb;
   dli_status st = make_kmajor_map(&ma, a, rows_a, k, lda, kBM, bf16);
@@ -1078,6 +1391,16 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
   p.const_b = const_b ? 1 : 0;
   p.glu_cols = static_cast<int>(glu_cols);
   p.out_f32 = out_f32 ? 1 : 0;
+  if (plan.streamk_ctas > 0) {
+    p.sk_part = static_cast<float*>(workspace);
+    p.sk_count = reinterpret_cast<int*>(static_cast<char*>(workspace) +
+                                        static_cast<size_t>(plan.streamk_ctas) * 2 * kBM * plan.bn * sizeof(float));
+    if (plan.bn == 32)
+      return bf16 ? launch_tc_streamk<__nv_bfloat16, 32, kStreamKStages32>(ma, mb, p, plan.streamk_ctas, stream)
+                  : launch_tc_streamk<__half, 32, kStreamKStages32>(ma, mb, p, plan.streamk_ctas, stream);
+    return bf16 ? launch_tc_streamk<__nv_bfloat16, 64, kStreamKStages64>(ma, mb, p, plan.streamk_ctas, stream)
+                : launch_tc_streamk<__half, 64, kStreamKStages64>(ma, mb, p, plan.streamk_ctas, stream);
+  }
   if (use_persistent(plan, epilogue))
     return bf16 ? launch_tc_persistent<__nv_bfloat16>(ma, mb, p, stream) : launch_tc_persistent<__half>(ma, mb, p, stream);
   if (bf16) return launch_tc_bn<__nv_bfloat16>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
@@ -1141,12 +1464,20 @@ using namespace dli_sm100;
 namespace {
 // Activation rows at or below this count run swap-AB (weights on the MMA M side).
 constexpr int64_t kSwapRows = 128;
+
+// The tcgen05 plan of a linear: swap-AB decode problems take the stream-K plan
+// when the caller's workspace holds it (and the cluster split-K plan otherwise).
+GemmPlan linear_plan(int64_t m, int64_t n, int64_t k, dli_dtype dtype, size_t workspace_bytes, bool query) {
+  if (m > kSwapRows) return plan_tn_gemm(m, n, k, dtype, true);
+  const GemmPlan base = plan_tn_gemm(n, m, k, dtype, true);
+  const GemmPlan sk = plan_streamk(base);
+  return (sk.streamk_ctas > 0 && (query || workspace_bytes >= sk.workspace)) ? sk : base;
+}
 }  // namespace
 
 extern "C" size_t dli_sm100_linear_workspace_size(int64_t m, int64_t n, int64_t k, dli_dtype dtype) {
   if (m <= 0 || n <= 0 || k <= 0) return 0;
-  const bool swap = m <= kSwapRows;
-  const GemmPlan plan = swap ? plan_tn_gemm(n, m, k, dtype, true) : plan_tn_gemm(m, n, k, dtype, true);
+  const GemmPlan plan = linear_plan(m, n, k, dtype, 0, true);
   return plan.tcgen05 ? plan.workspace : 0;
 }
 
@@ -1158,7 +1489,7 @@ extern "C" dli_status dli_sm100_linear(const void* x, const void* w, const void*
   if (m == 0) return ok();
   if (!x || !w || !y) return fail(DLI_ERR_INVALID_ARGUMENT, "linear: null pointer");
   const bool swap = m <= kSwapRows;
-  const GemmPlan plan = swap ? plan_tn_gemm(n, m, k, dtype, true) : plan_tn_gemm(m, n, k, dtype, true);
+  const GemmPlan plan = linear_plan(m, n, k, dtype, workspace ? workspace_bytes : 0, false);
   const bool tma_ok = aligned(x, 16) && aligned(w, 16);
   if (plan.tcgen05 && tma_ok) {
     if (swap)
@@ -1172,8 +1503,9 @@ extern "C" dli_status dli_sm100_linear(const void* x, const void* w, const void*
 
 extern "C" dli_status dli_sm100_linear_ex(const void* x, const void* w, const void* bias, void* y, int64_t m,
                                           int64_t n, int64_t k, dli_dtype dtype, dli_dtype out_dtype,
-                                          void* stream) {
-  if (out_dtype == dtype) return dli_sm100_linear(x, w, bias, y, m, n, k, dtype, nullptr, 0, stream);
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (out_dtype == dtype)
+    return dli_sm100_linear(x, w, bias, y, m, n, k, dtype, workspace, workspace_bytes, stream);
   if (m < 0 || n <= 0 || k <= 0) return fail(DLI_ERR_INVALID_ARGUMENT, "linear_ex: bad sizes");
   if ((dtype != DLI_DTYPE_BF16 && dtype != DLI_DTYPE_F16) || out_dtype != DLI_DTYPE_F32)
     return fail(DLI_ERR_UNSUPPORTED, "linear_ex: only bfloat16/float16 operands with a float32 output");
@@ -1182,13 +1514,13 @@ extern "C" dli_status dli_sm100_linear_ex(const void* x, const void* w, const vo
   if (!aligned(x, 16) || !aligned(w, 16) || k % 8 != 0)
     return fail(DLI_ERR_UNSUPPORTED, "linear_ex: 16-byte aligned operands and K % 8 == 0 expected");
   const bool swap = m <= kSwapRows;
-  const GemmPlan plan = swap ? plan_tn_gemm(n, m, k, dtype, true) : plan_tn_gemm(m, n, k, dtype, true);
+  const GemmPlan plan = linear_plan(m, n, k, dtype, workspace ? workspace_bytes : 0, false);
   if (!plan.tcgen05) return fail(DLI_ERR_UNSUPPORTED, "linear_ex: shape not served by tcgen05");
   if (swap)
-    return run_tn_gemm_tcgen05(w, x, bias, y, n, m, k, k, k, n, kEpiTransposed, 0, dtype, plan, nullptr, 0,
-                               as_stream(stream), true, false, 0, true);
-  return run_tn_gemm_tcgen05(x, w, bias, y, m, n, k, k, k, n, kEpiRowMajor, 0, dtype, plan, nullptr, 0,
-                             as_stream(stream), false, true, 0, true);
+    return run_tn_gemm_tcgen05(w, x, bias, y, n, m, k, k, k, n, kEpiTransposed, 0, dtype, plan, workspace,
+                               workspace_bytes, as_stream(stream), true, false, 0, true);
+  return run_tn_gemm_tcgen05(x, w, bias, y, m, n, k, k, k, n, kEpiRowMajor, 0, dtype, plan, workspace,
+                             workspace_bytes, as_stream(stream), false, true, 0, true);
 }
 
 extern "C" dli_status dli_sm100_linear_silu_mul(const void* x, const void* w_glu, void* y, int64_t m,

@@ -105,10 +105,10 @@ void reg(dli::OperatorRegistry* r, const char* name) {
 // ---------------------------------------------------------------------------
 
 // linear: y = x . W^T (+ b); python/dli_ops/aot/linear/template.cc:14-34.
-// Split-K plans need a zero-initialised workspace that the kernel leaves zeroed;
-// the operator (one instance per graph node in the engine's plan) keeps one
-// such buffer and grows it when a larger plan needs more, so a decode step
-// replayed from a CUDA graph allocates nothing.
+// Stream-K decode plans need a zero-initialised workspace that the kernel
+// leaves zeroed; the operator (one instance per graph node in the engine's
+// plan) keeps one such buffer and grows it when a larger plan needs more, so a
+// decode step replayed from a CUDA graph allocates nothing.
 class LinearOp final : public dli::Operator {
   mutable at::Tensor ws_;
 
@@ -134,16 +134,17 @@ class LinearOp final : public dli::Operator {
                              : x.dtype();
     *out[0] = Tensor::cuda(out_dt, shape, x.deviceId());
     const dli_dtype dt = cdt(x.dtype());
-    if (out_dt != x.dtype()) {
-      check(dli_sm100_linear_ex(dli::ptr(x), dli::ptr(w), in.size() == 3 ? dli::ptr(*in[2]) : nullptr,
-                                out[0]->deviceData(), m, n, k, dt, cdt(out_dt), ctx.cuda_stream),
-            type());
-      return;
-    }
     const std::size_t need = dli_sm100_linear_workspace_size(m, n, k, dt);
     if (need > wsBytes(ws_) || (ws_.defined() && ws_.device().index() != x.deviceId()))
       ws_ = at::zeros({static_cast<std::int64_t>(need)},
                       at::TensorOptions().dtype(at::kByte).device(at::kCUDA, x.deviceId()));
+    if (out_dt != x.dtype()) {
+      check(dli_sm100_linear_ex(dli::ptr(x), dli::ptr(w), in.size() == 3 ? dli::ptr(*in[2]) : nullptr,
+                                out[0]->deviceData(), m, n, k, dt, cdt(out_dt), need ? wsPtr(ws_) : nullptr,
+                                need ? wsBytes(ws_) : 0, ctx.cuda_stream),
+            type());
+      return;
+    }
     check(dli_sm100_linear(dli::ptr(x), dli::ptr(w), in.size() == 3 ? dli::ptr(*in[2]) : nullptr,
                            out[0]->deviceData(), m, n, k, dt, need ? wsPtr(ws_) : nullptr,
                            need ? wsBytes(ws_) : 0, ctx.cuda_stream),

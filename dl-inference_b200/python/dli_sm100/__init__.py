@@ -40,7 +40,7 @@ SIGNATURES = {
     "dli_sm100_check_device_error": (N, [P]),
     "dli_sm100_linear_workspace_size": (Z, [I, I, I, D]),
     "dli_sm100_linear": (N, [P, P, P, P, I, I, I, D, P, Z, P]),
-    "dli_sm100_linear_ex": (N, [P, P, P, P, I, I, I, D, D, P]),
+    "dli_sm100_linear_ex": (N, [P, P, P, P, I, I, I, D, D, P, Z, P]),
     "dli_sm100_matmul": (N, [P, P, P, I, I, I, D, P]),
     "dli_sm100_linear_silu_mul": (N, [P, P, P, I, I, I, D, P]),
     "dli_sm100_conv2d_workspace_size": (Z, [I] * 11 + [D]),
@@ -156,7 +156,7 @@ def linear(x, w, bias=None, out=None):
         raise ValueError("linear: weight K mismatch")
     out = out if out is not None else torch.empty(*x.shape[:-1], n, dtype=x.dtype, device=x.device)
     L = lib()
-    ws_bytes = L.dli_sm100_linear_workspace_size(m, n, k, _dt(x))  # 0 in this build (cluster split-K)
+    ws_bytes = L.dli_sm100_linear_workspace_size(m, n, k, _dt(x))  # stream-K partials (zero-filled)
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
     check(L.dli_sm100_linear(_ptr(x), _ptr(w), _ptr(bias), _ptr(out), m, n, k, _dt(x), _ptr(ws),
                              ws_bytes, _stream()), "linear")
@@ -172,8 +172,11 @@ def linear_ex(x, w, bias=None, out_dtype=torch.float32):
     if w.shape[1] != k:
         raise ValueError("linear_ex: weight K mismatch")
     out = torch.empty(*x.shape[:-1], n, dtype=out_dtype, device=x.device)
-    check(lib().dli_sm100_linear_ex(_ptr(x), _ptr(w), _ptr(bias), _ptr(out), m, n, k, _dt(x),
-                                    DTYPE_CODES[out_dtype], _stream()), "linear_ex")
+    L = lib()
+    ws_bytes = L.dli_sm100_linear_workspace_size(m, n, k, _dt(x))
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=x.device) if ws_bytes else None
+    check(L.dli_sm100_linear_ex(_ptr(x), _ptr(w), _ptr(bias), _ptr(out), m, n, k, _dt(x),
+                                DTYPE_CODES[out_dtype], _ptr(ws), ws_bytes, _stream()), "linear_ex")
     return out
 
 

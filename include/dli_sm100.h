@@ -69,10 +69,15 @@ dli_status dli_sm100_check_device_error(void* stream);
  * (TMA-fed, TMEM accumulators, fp32 accumulate); F32 runs an exact-fp32 FFMA
  * kernel (the reference's tl.dot runs fp32 as TF32).
  * Decode-sized problems (few rows) stream the weight matrix once with the
- * weights on the MMA M side; when the tiles cannot fill the GPU, K is split over
- * a thread-block cluster and reduced through distributed shared memory, so this
- * build needs no workspace (linear_workspace_size() returns 0; the workspace
- * arguments are kept for callers written against a build that uses one). */
+ * weights on the MMA M side. When their tiles do not fill whole waves of the
+ * GPU, the (tile, K block) work is split evenly over every resident CTA
+ * (stream-K): partial tiles go through the workspace and the last contributor
+ * of a tile sums them in a fixed order (deterministic). The workspace of
+ * dli_sm100_linear_workspace_size() bytes must be zero-filled before its first
+ * use and is left zeroed by every call (so it can be reused, and replayed in a
+ * CUDA graph); calls sharing one workspace must not overlap on the GPU. Without
+ * a workspace (NULL / too small) K is split over thread-block clusters reduced
+ * through distributed shared memory instead. F32 needs no workspace. */
 size_t dli_sm100_linear_workspace_size(int64_t m, int64_t n, int64_t k, dli_dtype dtype);
 dli_status dli_sm100_linear(const void* x, const void* w, const void* bias, void* y, int64_t m,
                             int64_t n, int64_t k, dli_dtype dtype, void* workspace,
@@ -82,10 +87,11 @@ dli_status dli_sm100_linear(const void* x, const void* w, const void* bias, void
  * x, w and bias in `dtype`. Serves BF16/F16 operands with an F32 output (the
  * fp32 accumulator stored without rounding to bf16), used for the LM-head logits
  * that greedy decoding takes the argmax of; out_dtype == dtype is
- * dli_sm100_linear. Additive: the reference's linear (python/dli_ops/aot/linear/
+ * dli_sm100_linear. The workspace is dli_sm100_linear's (same size query). Additive: the reference's linear (python/dli_ops/aot/linear/
  * template.cc:14-34) always writes its input dtype, fp32. */
 dli_status dli_sm100_linear_ex(const void* x, const void* w, const void* bias, void* y, int64_t m,
-                               int64_t n, int64_t k, dli_dtype dtype, dli_dtype out_dtype, void* stream);
+                               int64_t n, int64_t k, dli_dtype dtype, dli_dtype out_dtype, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 /* Fused gate/up projection + SwiGLU (additive; the reference graph runs
  * linear -> silu -> mul): y[M, inter] = silu(x · Wg^T) * (x · Wu^T), computed in

@@ -139,6 +139,48 @@ def test_linear_tcgen05_model_shapes(m, n, k, dtype):
     assert torch.equal(y, y2)
 
 
+@pytest.mark.parametrize("m,n,k", [(32, 4608, 3584), (32, 3584, 3584), (32, 3584, 18944), (8, 1152, 896),
+                                   (32, 152064, 3584), (64, 1280, 8192), (3, 700, 136), (40, 1000, 1024)])
+def test_linear_stream_k_reuses_workspace(m, n, k):
+    """Decode-sized linears whose tiles do not fill whole waves run stream-K:
+    partial tiles through the caller's workspace, summed by the last contributor
+    in CTA order. Three calls on one workspace must agree bit for bit (the
+    per-tile counters return to zero after each call), match the no-workspace
+    cluster path within bf16 tolerance, and match an fp32 reference; the LM-head
+    shape also with float32 output."""
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    b = (torch.randn(n, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    L = C.lib()
+    need = L.dli_sm100_linear_workspace_size(m, n, k, C.DTYPE_CODES[torch.bfloat16])
+    ws = torch.zeros(max(need, 16), dtype=torch.uint8, device="cuda")
+    outs = []
+    for _ in range(3):
+        y = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        C.check(L.dli_sm100_linear(C._ptr(x), C._ptr(w), C._ptr(b), C._ptr(y), m, n, k, C.DTYPE_CODES[torch.bfloat16],
+                                   C._ptr(ws), need, C._stream()), "linear")
+        outs.append(y)
+    y_cluster = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    C.check(L.dli_sm100_linear(C._ptr(x), C._ptr(w), C._ptr(b), C._ptr(y_cluster), m, n, k,
+                               C.DTYPE_CODES[torch.bfloat16], None, 0, C._stream()), "linear")
+    C.check_device_error()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    ref = torch.nn.functional.linear(x.float(), w.float(), b.float())
+    assert_close(outs[0].float(), ref, torch.bfloat16, f"stream-K linear {m}x{n}x{k}")
+    assert_close(y_cluster.float(), ref, torch.bfloat16, f"cluster linear {m}x{n}x{k}")
+    if need:
+        counters = ws[need - ((n + 127) // 128 * 4 + 255) // 256 * 256:need]  # may include padding: all zero
+        assert int(counters.count_nonzero()) == 0
+    if n == 152064:
+        y32 = C.linear_ex(x, w, b, out_dtype=torch.float32)
+        y32b = C.linear_ex(x, w, b, out_dtype=torch.float32)
+        assert torch.equal(y32, y32b)
+        assert_close(y32, ref, torch.float16, "LM head fp32 logits")  # fp32 output: tighter than bf16
+
+
 def test_linear_fp32_config1():
     """The single-linear workload: x[64,1024] . W[4096,1024]^T + b in fp32, rel-err <= 1e-4."""
     import dli_sm100 as C
