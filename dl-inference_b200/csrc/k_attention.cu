@@ -924,6 +924,275 @@ __global__ void attn_fallback_kernel(const AttnArgs a) {
   }
 }
 
+// ---- fp32 tiles on CUDA cores (the reference's dtype) -------------------------------------
+// CTA = 16 query rows of one (sequence, query head) x one split of the keys;
+// 4 warps of 4 rows each. 32-key K/V blocks are double-buffered in shared memory
+// with cp.async; lane j scores key j against the warp's 4 rows (float4 reads of
+// the padded K rows, conflict-free), the online softmax runs per row across the
+// warp (shuffle max/sum, exp2), and for O += P V each lane owns D/32 output
+// columns while the 32 probabilities are broadcast by shuffles. When the rows
+// alone cannot fill the GPU (decode), the keys are split over up to 8 CTAs of
+// a thread-block cluster whose (m, l, O) are merged through distributed shared
+// memory in rank order: exact fp32, deterministic, no workspace. Rows past a
+// sequence's keys are never loaded (cp.async zero-fills them).
+constexpr int kF32Rows = 16, kF32Keys = 32;
+
+template <int D>
+struct F32AttnSmem {
+  static constexpr int kRow = D + 4;                   // padded K/V row (floats)
+  static constexpr int kQ = kF32Rows * D;              // [16][D]
+  static constexpr int kKV = 2 * 2 * kF32Keys * kRow;  // 2 stages x (K, V) x [32][D+4]
+  static constexpr int kState = kF32Rows * (D + 2);    // merge: O [16][D] + m, l per row
+  static constexpr int kFloats = kQ + kKV + kState;
+  static constexpr int kBytes = kFloats * 4;
+};
+
+template <int D>
+__global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
+  DLI_PDL_ENTRY();
+  using L = F32AttnSmem<D>;
+  constexpr int DL = D / 32;  // output columns per lane
+  extern __shared__ __align__(16) float f32s[];
+  float* sq = f32s;
+  float* skv = f32s + L::kQ;
+  float* st = skv + L::kKV;  // [16][D] O, then m[16], l[16]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, splits = gridDim.x;
+  const int m0 = blockIdx.y * kF32Rows;
+  const int bh = blockIdx.z;
+  const int h = bh % a.hq, b = bh / a.hq;
+  const int kvh = h / a.group;
+  const int kv_len = kv_len_of(a, b);
+  const int off = kv_len - a.seq_q;
+  const float* qbase = static_cast<const float*>(a.q) + b * a.q_sb + h * a.q_sh;
+  const float* kbase = static_cast<const float*>(a.k) + b * a.k_sb + kvh * a.k_sh;
+  const float* vbase = static_cast<const float*>(a.v) + b * a.k_sb + kvh * a.k_sh;
+
+  // Q rows (zero past the sequence)
+  for (int c = threadIdx.x; c < kF32Rows * D / 4; c += 128) {
+    const int r = c / (D / 4), d4 = (c % (D / 4)) * 4;
+    const int qs = m0 + r;
+    const float4 v = qs < a.seq_q ? *reinterpret_cast<const float4*>(qbase + static_cast<int64_t>(qs) * a.q_ss + d4)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4*>(sq + r * D + d4) = v;
+  }
+  int n_end = a.causal ? min(kv_len, m0 + kF32Rows + off) : kv_len;
+  n_end = max(n_end, 0);
+  const int nblocks = (n_end + kF32Keys - 1) / kF32Keys;
+  const int b0 = static_cast<int>(static_cast<int64_t>(split) * nblocks / splits);
+  const int b1 = static_cast<int>(static_cast<int64_t>(split + 1) * nblocks / splits);
+
+  auto load_block = [&](int blk, int stage) {
+    float* kt = skv + stage * 2 * kF32Keys * L::kRow;
+    float* vt = kt + kF32Keys * L::kRow;
+    const uint32_t ks = static_cast<uint32_t>(__cvta_generic_to_shared(kt));
+    const uint32_t vs = static_cast<uint32_t>(__cvta_generic_to_shared(vt));
+    for (int c = threadIdx.x; c < kF32Keys * D / 4; c += 128) {
+      const int r = c / (D / 4), d4 = (c % (D / 4)) * 4;
+      const int key = blk * kF32Keys + r;
+      const bool valid = key < n_end;
+      const int64_t src = static_cast<int64_t>(valid ? key : 0) * D + d4;
+      cp_async16(ks + (r * L::kRow + d4) * 4, kbase + src, valid);
+      cp_async16(vs + (r * L::kRow + d4) * 4, vbase + src, valid);
+    }
+    cp_async_commit();
+  };
+
+  float o[4][DL];
+  float m_row[4], l_row[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m_row[i] = -INFINITY;
+    l_row[i] = 0.f;
+#pragma unroll
+    for (int c = 0; c < DL; ++c) o[i][c] = 0.f;
+  }
+  const int r_base = warp * 4;
+  const bool warp_rows = m0 + r_base < a.seq_q;  // the warp has at least one live row
+  if (b0 < b1) load_block(b0, 0);
+  for (int blk = b0; blk < b1; ++blk) {
+    const int stage = (blk - b0) & 1;
+    if (blk + 1 < b1) {
+      load_block(blk + 1, stage ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float* kt = skv + stage * 2 * kF32Keys * L::kRow;
+    const float* vt = kt + kF32Keys * L::kRow;
+    if (warp_rows) {
+      // scores of key (blk*32 + lane) for the warp's 4 rows
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+      for (int d = 0; d < D; d += 4) {
+        const float4 kv = *reinterpret_cast<const float4*>(kt + lane * L::kRow + d);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 qv = *reinterpret_cast<const float4*>(sq + (r_base + i) * D + d);
+          sc[i] = fmaf(qv.x, kv.x, sc[i]);
+          sc[i] = fmaf(qv.y, kv.y, sc[i]);
+          sc[i] = fmaf(qv.z, kv.z, sc[i]);
+          sc[i] = fmaf(qv.w, kv.w, sc[i]);
+        }
+      }
+      const int key = blk * kF32Keys + lane;
+      float pr[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int qs = m0 + r_base + i;
+        const int lim = a.causal ? min(kv_len, qs + off + 1) : kv_len;
+        const float v = key < lim ? sc[i] * a.scale_log2 : -INFINITY;
+        const float mnew = fmaxf(m_row[i], warp_max(v));
+        const float alpha = mnew == -INFINITY ? 1.f : exp2f(m_row[i] - mnew);
+        pr[i] = mnew == -INFINITY ? 0.f : exp2f(v - mnew);
+        l_row[i] = l_row[i] * alpha + warp_sum(pr[i]);
+        m_row[i] = mnew;
+#pragma unroll
+        for (int c = 0; c < DL; ++c) o[i][c] *= alpha;
+      }
+      // O += P V: lane owns columns lane*DL .. lane*DL+DL-1
+#pragma unroll 4
+      for (int j = 0; j < kF32Keys; ++j) {
+        float vv[DL];
+#pragma unroll
+        for (int c = 0; c < DL; c += 4) {
+          const float4 x = *reinterpret_cast<const float4*>(vt + j * L::kRow + lane * DL + c);
+          vv[c] = x.x;
+          vv[c + 1] = x.y;
+          vv[c + 2] = x.z;
+          vv[c + 3] = x.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float pj = __shfl_sync(0xffffffffu, pr[i], j);
+#pragma unroll
+          for (int c = 0; c < DL; ++c) o[i][c] = fmaf(pj, vv[c], o[i][c]);
+        }
+      }
+    }
+    __syncthreads();  // the stage is refilled next iteration
+  }
+
+  auto store_row = [&](int r, const float* vals, float inv) {
+    const int qs = m0 + r;
+    if (qs >= a.seq_q) return;
+    float* dst = static_cast<float*>(a.out) + b * a.o_sb + h * a.o_sh + static_cast<int64_t>(qs) * a.o_ss;
+    for (int c = 0; c < DL; c += 4)
+      *reinterpret_cast<float4*>(dst + lane * DL + c) =
+          make_float4(vals[c] * inv, vals[c + 1] * inv, vals[c + 2] * inv, vals[c + 3] * inv);
+  };
+  if (splits == 1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) store_row(r_base + i, o[i], l_row[i] > 0.f ? 1.f / l_row[i] : 0.f);
+    return;
+  }
+  // split-KV: publish (m, l, O) and merge across the cluster in rank order
+  float* so = st;
+  float* sm = st + kF32Rows * D;
+  float* sl = sm + kF32Rows;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int c = 0; c < DL; c += 4)
+      *reinterpret_cast<float4*>(so + (r_base + i) * D + lane * DL + c) =
+          make_float4(o[i][c], o[i][c + 1], o[i][c + 2], o[i][c + 3]);
+    if (lane == 0) {
+      sm[r_base + i] = m_row[i];
+      sl[r_base + i] = l_row[i];
+    }
+  }
+  cluster_sync();
+  const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(st));
+  const int rows_per = (kF32Rows + splits - 1) / splits;
+  for (int r = split * rows_per + warp; r < min(kF32Rows, (split + 1) * rows_per); r += 4) {
+    float mm = -INFINITY;
+    for (int s = 0; s < splits; ++s) {
+      float v;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                   : "=f"(v)
+                   : "r"(mapa_shared(base + static_cast<uint32_t>((kF32Rows * D + r) * 4), s))
+                   : "memory");
+      mm = fmaxf(mm, v);
+    }
+    float acc[DL], ll = 0.f;
+#pragma unroll
+    for (int c = 0; c < DL; ++c) acc[c] = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      float ms, ls;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                   : "=f"(ms)
+                   : "r"(mapa_shared(base + static_cast<uint32_t>((kF32Rows * D + r) * 4), s))
+                   : "memory");
+      asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                   : "=f"(ls)
+                   : "r"(mapa_shared(base + static_cast<uint32_t>((kF32Rows * D + kF32Rows + r) * 4), s))
+                   : "memory");
+      const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - mm);
+      ll += ls * w;
+#pragma unroll
+      for (int c = 0; c < DL; c += 4) {
+        const float4 x = ld_dsmem_f4(mapa_shared(base + static_cast<uint32_t>((r * D + lane * DL + c) * 4), s));
+        acc[c] += w * x.x;
+        acc[c + 1] += w * x.y;
+        acc[c + 2] += w * x.z;
+        acc[c + 3] += w * x.w;
+      }
+    }
+    store_row(r, acc, ll > 0.f ? 1.f / ll : 0.f);
+  }
+  cluster_sync();  // every rank's shared memory stays alive until all reads are done
+}
+
+template <int D>
+dli_status launch_attn_f32(const AttnArgs& args, cudaStream_t stream) {
+  using L = F32AttnSmem<D>;
+  auto kern = attn_f32_kernel<D>;
+  const dli_status st = ensure_smem(reinterpret_cast<const void*>(kern), L::kBytes, "attention fp32");
+  if (st != DLI_OK) return st;
+  const int64_t tiles = ceil_div(args.seq_q, kF32Rows);
+  const int64_t rows = tiles * args.batch * args.hq;
+  const int64_t blocks = ceil_div(args.seq_k, kF32Keys);
+  // split the keys when the row tiles alone leave SMs idle (two CTAs per SM)
+  int splits = static_cast<int>(std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(2 * sm_count(), rows))));
+  splits = static_cast<int>(std::min<int64_t>(splits, std::max<int64_t>(1, blocks / 2)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(splits), static_cast<unsigned>(tiles),
+                     static_cast<unsigned>(static_cast<int64_t>(args.batch) * args.hq));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (splits > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  cudaLaunchKernelEx(&cfg, kern, args);
+  return check_launch("attention fp32");
+}
+
+bool f32_attention_ok(const AttnArgs& a) {
+  static const bool on = tuning_knob("ATTN_F32", 1) != 0;
+  if (!on || (a.head_dim != 64 && a.head_dim != 128)) return false;
+  if (static_cast<int64_t>(a.batch) * a.hq > 65535 || ceil_div(a.seq_q, kF32Rows) > 65535) return false;
+  for (const void* ptr : {a.q, a.k, a.v, static_cast<const void*>(a.out)})
+    if (!aligned(ptr, 16)) return false;
+  for (int64_t s : {a.q_sb, a.q_sh, a.q_ss, a.o_sb, a.o_sh, a.o_ss, a.k_sb, a.k_sh})
+    if (s % 4 != 0) return false;
+  return true;
+}
+
 // ---- host dispatch ----------------------------------------------------------------------
 struct DecodePlan {
   bool decode = false;
@@ -1144,6 +1413,8 @@ dli_status run_attention(AttnArgs& args, dli_dtype dtype, int64_t max_kv, void* 
     return args.head_dim == 64 ? launch_tc_attention<__half, 64>(args, plan, stream)
                                : launch_tc_attention<__half, 128>(args, plan, stream);
   }
+  if (dtype == DLI_DTYPE_F32 && f32_attention_ok(args))
+    return args.head_dim == 64 ? launch_attn_f32<64>(args, stream) : launch_attn_f32<128>(args, stream);
   if (args.head_dim > 256) return fail(DLI_ERR_UNSUPPORTED, "attention: head_dim > 256");
   const int64_t rows = static_cast<int64_t>(args.batch) * args.hq * args.seq_q;
   const int warps = 4;

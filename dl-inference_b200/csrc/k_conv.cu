@@ -6,7 +6,9 @@
 // so TMA row strides stay 16-byte aligned) into the workspace; the weight
 // [OC, C, KH, KW] is already a K-major [OC, K] operand (repacked to Kp columns
 // when K % 8 != 0). The GEMM epilogue scatters D[m, oc] straight to NCHW.
-// f32: direct convolution, one output per thread, fp32 FMA (exact arithmetic).
+// f32: 3x3 kernels run the tiled kernel below (shared-memory input patches and
+// weights, 16 output channels per thread); other sizes a direct convolution,
+// one output per thread. Both exact fp32 FMA.
 #include <algorithm>
 
 #include "gemm.cuh"
@@ -80,6 +82,78 @@ __global__ void conv_direct_kernel(const T* __restrict__ x, const T* __restrict_
     }
     out[i] = from_f32<T>(acc);
   }
+}
+
+// fp32 3x3 convolution on CUDA cores, tiled: CTA = a 16x16 block of output
+// pixels of one image x 16 output channels, 256 threads of one pixel and 16
+// channel accumulators each. Input channels go through shared memory 8 at a
+// time: the (15*stride + 3)^2 input patch (zero-padded at the borders) and the
+// matching 8 x 9 x 16 weights, stored channel-fastest so one 16-byte shared
+// load serves four accumulators. Exact fp32 FMA in (c, ky, kx) order.
+constexpr int kConvTile = 16, kConvOcb = 16, kConvCb = 8;
+
+__host__ __device__ inline int conv_patch(int64_t stride) { return static_cast<int>((kConvTile - 1) * stride + 3); }
+
+__global__ void __launch_bounds__(256)
+    conv3x3_f32_kernel(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ bias,
+                       float* __restrict__ out, ConvShape s, int tiles_x) {
+  DLI_PDL_ENTRY();
+  extern __shared__ __align__(16) float conv_smem[];
+  const int ih = conv_patch(s.sh), iw = conv_patch(s.sw);
+  float* wsm = conv_smem;                             // [kConvCb * 9][kConvOcb]
+  float* patch = conv_smem + kConvCb * 9 * kConvOcb;  // [kConvCb][ih][iw]
+  const int tid = threadIdx.x;
+  const int py = tid / kConvTile, px = tid % kConvTile;
+  const int ty = blockIdx.x / tiles_x, tx = blockIdx.x % tiles_x;
+  const int oc0 = blockIdx.y * kConvOcb;
+  const int64_t img = blockIdx.z;
+  const int64_t oy = static_cast<int64_t>(ty) * kConvTile + py, ox = static_cast<int64_t>(tx) * kConvTile + px;
+  const int64_t iy0 = static_cast<int64_t>(ty) * kConvTile * s.sh - s.ph;
+  const int64_t ix0 = static_cast<int64_t>(tx) * kConvTile * s.sw - s.pw;
+  float acc[kConvOcb];
+#pragma unroll
+  for (int o = 0; o < kConvOcb; ++o) acc[o] = (bias && oc0 + o < s.oc) ? bias[oc0 + o] : 0.f;
+  const int plane = ih * iw;
+  for (int64_t c0 = 0; c0 < s.c; c0 += kConvCb) {
+    const int cb = static_cast<int>(s.c - c0 < kConvCb ? s.c - c0 : kConvCb);
+    for (int i = tid; i < kConvCb * plane; i += 256) {
+      const int cc = i / plane, rem = i - cc * plane;
+      const int r = rem / iw, q = rem - r * iw;
+      const int64_t iy = iy0 + r, ix = ix0 + q;
+      float v = 0.f;
+      if (cc < cb && iy >= 0 && iy < s.h && ix >= 0 && ix < s.w) v = x[((img * s.c + c0 + cc) * s.h + iy) * s.w + ix];
+      patch[i] = v;
+    }
+    for (int i = tid; i < kConvCb * 9 * kConvOcb; i += 256) {
+      const int o = i % kConvOcb, t = i / kConvOcb;
+      const int cc = t / 9, kk = t - cc * 9;
+      wsm[i] = (cc < cb && oc0 + o < s.oc) ? w[((static_cast<int64_t>(oc0) + o) * s.c + c0 + cc) * 9 + kk] : 0.f;
+    }
+    __syncthreads();
+    for (int cc = 0; cc < cb; ++cc) {
+#pragma unroll
+      for (int ky = 0; ky < 3; ++ky) {
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+          const float xv = patch[cc * plane + (py * static_cast<int>(s.sh) + ky) * iw + px * static_cast<int>(s.sw) + kx];
+          const float4* wr = reinterpret_cast<const float4*>(wsm + (cc * 9 + ky * 3 + kx) * kConvOcb);
+#pragma unroll
+          for (int q = 0; q < kConvOcb / 4; ++q) {
+            const float4 wv = wr[q];
+            acc[4 * q] = fmaf(xv, wv.x, acc[4 * q]);
+            acc[4 * q + 1] = fmaf(xv, wv.y, acc[4 * q + 1]);
+            acc[4 * q + 2] = fmaf(xv, wv.z, acc[4 * q + 2]);
+            acc[4 * q + 3] = fmaf(xv, wv.w, acc[4 * q + 3]);
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (oy >= s.oh || ox >= s.ow) return;
+#pragma unroll
+  for (int o = 0; o < kConvOcb; ++o)
+    if (oc0 + o < s.oc) out[((img * s.oc + oc0 + o) * s.oh + oy) * s.ow + ox] = acc[o];
 }
 
 inline unsigned grid_for(int64_t n) {
@@ -169,6 +243,21 @@ extern "C" dli_status dli_sm100_conv2d(const void* x, const void* weight, const 
     return run_tn_gemm_tcgen05(cols, wk, bias, out, s.m(), s.oc, s.kp(), s.kp(), s.kp(), 0,
                                kEpiNchw, s.oh * s.ow, dtype, ws.plan, base + ws.cols + ws.weight,
                                ws.gemm, cs, false, ws.weight == 0);
+  }
+  static const bool tiled = tuning_knob("CONV_F32_TILED", 1) != 0;
+  if (tiled && dtype == DLI_DTYPE_F32 && s.kh == 3 && s.kw == 3 && s.sh <= 2 && s.sw <= 2 && s.n <= 65535 &&
+      ceil_div(s.oc, kConvOcb) <= 65535) {
+    const int64_t tiles_x = ceil_div(s.ow, kConvTile), tiles_y = ceil_div(s.oh, kConvTile);
+    if (tiles_x * tiles_y <= 0x7fffffff) {
+      const int smem = (kConvCb * 9 * kConvOcb + kConvCb * conv_patch(s.sh) * conv_patch(s.sw)) * 4;
+      st = ensure_smem(reinterpret_cast<const void*>(conv3x3_f32_kernel), smem, "conv2d fp32");
+      if (st != DLI_OK) return st;
+      launch_pdl(conv3x3_f32_kernel, dim3(static_cast<unsigned>(tiles_x * tiles_y),
+                                          static_cast<unsigned>(ceil_div(s.oc, kConvOcb)), static_cast<unsigned>(s.n)),
+                 dim3(256), smem, cs, static_cast<const float*>(x), static_cast<const float*>(weight),
+                 static_cast<const float*>(bias), static_cast<float*>(out), s, static_cast<int>(tiles_x));
+      return check_launch("conv2d fp32 3x3");
+    }
   }
   st = dispatch_float(dtype, "conv2d", [&](auto tag) {
     using T = decltype(tag);

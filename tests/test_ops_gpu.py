@@ -237,6 +237,22 @@ ALEXNET_CONVS = [  # (C, H, OC) at k3 s1 p1
     (3, 32, 64), (64, 16, 192), (192, 8, 384), (384, 8, 256), (256, 8, 256)]
 
 
+@pytest.mark.parametrize("n,c,h,w,oc,stride,pad", [(2, 3, 32, 32, 64, 1, 1), (1, 5, 17, 23, 20, 2, 1),
+                                                    (3, 9, 15, 15, 17, 1, 0), (1, 64, 16, 16, 192, 2, 2)])
+def test_conv2d_fp32_3x3_tiled(n, c, h, w, oc, stride, pad):
+    """The tiled fp32 3x3 kernel at ragged sizes, both strides, channel counts
+    not multiples of its 8/16 blocks: rel-err <= 1e-4 against float64."""
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(n + c + h + oc)
+    x = torch.randn(n, c, h, w, device="cuda", generator=g)
+    wt = torch.randn(oc, c, 3, 3, device="cuda", generator=g) * 0.05
+    b = torch.randn(oc, device="cuda", generator=g) * 0.05
+    y = C.conv2d(x, wt, b, (stride, stride), (pad, pad))
+    ref = torch.nn.functional.conv2d(x.double(), wt.double(), b.double(), stride=stride, padding=pad)
+    assert_close(y, ref, torch.float32, f"conv fp32 {c}->{oc} s{stride} p{pad}")
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32], ids=["f16", "bf16", "f32"])
 @pytest.mark.parametrize("c,h,oc", ALEXNET_CONVS)
 def test_conv2d_alexnet_shapes(c, h, oc, dtype):
@@ -269,6 +285,41 @@ def test_attention_dense(b, hq, hkv, sq, sk, d, causal, dtype):
     ref = torch.from_numpy(O.attention(q.double().cpu().numpy(), k.double().cpu().numpy(),
                                        v.double().cpu().numpy(), causal))
     assert_close(out.float(), ref, dtype, "attention")
+
+
+@pytest.mark.parametrize("b,hq,hkv,sq,sk,d,causal", [
+    (1, 1, 1, 1, 2048, 128, True), (1, 1, 1, 1, 517, 64, True), (2, 4, 4, 128, 128, 128, True),
+    (1, 6, 2, 77, 300, 64, False), (3, 8, 1, 33, 33, 128, True), (2, 2, 2, 5, 1000, 128, True)])
+def test_attention_fp32_tiles(b, hq, hkv, sq, sk, d, causal):
+    """The fp32 attention kernel (16-row tiles, split-KV merged in a cluster for
+    decode-sized rows) at the reference's dtype: rel-err <= 1e-4 against the oracle."""
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(sq * 5 + sk + d)
+    q = torch.randn(b, hq, sq, d, device="cuda", generator=g)
+    k = torch.randn(b, hkv, sk, d, device="cuda", generator=g)
+    v = torch.randn(b, hkv, sk, d, device="cuda", generator=g)
+    out = C.attention(q, k, v, causal=causal)
+    ref = torch.from_numpy(O.attention(q.double().cpu().numpy(), k.double().cpu().numpy(),
+                                       v.double().cpu().numpy(), causal))
+    assert_close(out, ref, torch.float32, "attention fp32")
+
+
+def test_attention_kvcache_fp32_positions():
+    import dli_sm100 as C
+
+    b, s, hq, hkv, d, cap = 3, 3, 4, 2, 128, 700
+    positions = [0, 250, 696]
+    g = torch.Generator(device="cuda").manual_seed(8)
+    q = torch.randn(b, s, hq, d, device="cuda", generator=g)
+    ck = torch.randn(b, hkv, cap, d, device="cuda", generator=g)
+    cv = torch.randn(b, hkv, cap, d, device="cuda", generator=g)
+    for i, p in enumerate(positions):  # stale rows past each sequence must not reach the output
+        ck[i, :, p + s:] = float("nan")
+        cv[i, :, p + s:] = float("nan")
+    out = C.attention_kvcache(q, ck, cv, torch.tensor(positions, device="cuda"))
+    assert torch.isfinite(out).all()
+    assert_close(out, _cache_reference(q, ck, cv, positions), torch.float32, "attention_kvcache fp32")
 
 
 def _cache_reference(q_bshd, ck, cv, positions):
