@@ -947,6 +947,28 @@ struct F32AttnSmem {
   static constexpr int kBytes = kFloats * 4;
 };
 
+// A lane's DL consecutive fp32 columns (DL = D/32: 2 at D=64, 4 at D=128) as
+// one 8- or 16-byte access: the address is aligned to the access width.
+template <int DL>
+__device__ __forceinline__ void load_cols(const float* p, float (&v)[DL]) {
+  static_assert(DL == 2 || DL == 4, "2 or 4 columns per lane");
+  if constexpr (DL == 4) {
+    const float4 x = *reinterpret_cast<const float4*>(p);
+    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+  } else {
+    const float2 x = *reinterpret_cast<const float2*>(p);
+    v[0] = x.x; v[1] = x.y;
+  }
+}
+template <int DL>
+__device__ __forceinline__ void store_cols(float* p, const float* v, float scale) {
+  if constexpr (DL == 4) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0] * scale, v[1] * scale, v[2] * scale, v[3] * scale);
+  } else {
+    *reinterpret_cast<float2*>(p) = make_float2(v[0] * scale, v[1] * scale);
+  }
+}
+
 template <int D>
 __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
   DLI_PDL_ENTRY();
@@ -1055,14 +1077,7 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
 #pragma unroll 4
       for (int j = 0; j < kF32Keys; ++j) {
         float vv[DL];
-#pragma unroll
-        for (int c = 0; c < DL; c += 4) {
-          const float4 x = *reinterpret_cast<const float4*>(vt + j * L::kRow + lane * DL + c);
-          vv[c] = x.x;
-          vv[c + 1] = x.y;
-          vv[c + 2] = x.z;
-          vv[c + 3] = x.w;
-        }
+        load_cols<DL>(vt + j * L::kRow + lane * DL, vv);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float pj = __shfl_sync(0xffffffffu, pr[i], j);
@@ -1078,9 +1093,7 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
     const int qs = m0 + r;
     if (qs >= a.seq_q) return;
     float* dst = static_cast<float*>(a.out) + b * a.o_sb + h * a.o_sh + static_cast<int64_t>(qs) * a.o_ss;
-    for (int c = 0; c < DL; c += 4)
-      *reinterpret_cast<float4*>(dst + lane * DL + c) =
-          make_float4(vals[c] * inv, vals[c + 1] * inv, vals[c + 2] * inv, vals[c + 3] * inv);
+    store_cols<DL>(dst + lane * DL, vals, inv);
   };
   if (splits == 1) {
 #pragma unroll
@@ -1093,10 +1106,7 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
   float* sl = sm + kF32Rows;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-#pragma unroll
-    for (int c = 0; c < DL; c += 4)
-      *reinterpret_cast<float4*>(so + (r_base + i) * D + lane * DL + c) =
-          make_float4(o[i][c], o[i][c + 1], o[i][c + 2], o[i][c + 3]);
+    store_cols<DL>(so + (r_base + i) * D + lane * DL, o[i], 1.f);
     if (lane == 0) {
       sm[r_base + i] = m_row[i];
       sl[r_base + i] = l_row[i];
@@ -1131,12 +1141,13 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
       const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - mm);
       ll += ls * w;
 #pragma unroll
-      for (int c = 0; c < DL; c += 4) {
-        const float4 x = ld_dsmem_f4(mapa_shared(base + static_cast<uint32_t>((r * D + lane * DL + c) * 4), s));
-        acc[c] += w * x.x;
-        acc[c + 1] += w * x.y;
-        acc[c + 2] += w * x.z;
-        acc[c + 3] += w * x.w;
+      for (int c = 0; c < DL; ++c) {  // scalar DSMEM loads: 4-byte aligned for any DL
+        float x;
+        asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                     : "=f"(x)
+                     : "r"(mapa_shared(base + static_cast<uint32_t>((r * D + lane * DL + c) * 4), s))
+                     : "memory");
+        acc[c] += w * x;
       }
     }
     store_row(r, acc, ll > 0.f ? 1.f / ll : 0.f);
