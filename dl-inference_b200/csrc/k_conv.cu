@@ -250,7 +250,9 @@ extern "C" dli_status dli_sm100_conv2d(const void* x, const void* weight, const 
     const int64_t tiles_x = ceil_div(s.ow, kConvTile), tiles_y = ceil_div(s.oh, kConvTile);
     if (tiles_x * tiles_y <= 0x7fffffff) {
       const int smem = (kConvCb * 9 * kConvOcb + kConvCb * conv_patch(s.sh) * conv_patch(s.sw)) * 4;
-      st = ensure_smem(reinterpret_cast<const void*>(conv3x3_f32_kernel), smem, "conv2d fp32");
+      // the limit is set once per device: at the largest patch (stride 2) so every launch fits
+      constexpr int kMaxSmem = (kConvCb * 9 * kConvOcb + kConvCb * (15 * 2 + 3) * (15 * 2 + 3)) * 4;
+      st = ensure_smem(reinterpret_cast<const void*>(conv3x3_f32_kernel), kMaxSmem, "conv2d fp32");
       if (st != DLI_OK) return st;
       launch_pdl(conv3x3_f32_kernel, dim3(static_cast<unsigned>(tiles_x * tiles_y),
                                           static_cast<unsigned>(ceil_div(s.oc, kConvOcb)), static_cast<unsigned>(s.n)),
