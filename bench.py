@@ -54,6 +54,26 @@ SMALL = {
 }
 
 
+
+# ncu summaries (profiles/) of the dominant decode kernel per (model, tp, batch per rank)
+NCU_SUMMARIES = {("7b", 1, 32): "glu_decode_gate_up_qwen2_7b.md"}
+_UNITS = {"byte": 1, "kbyte": 1e3, "mbyte": 1e6, "gbyte": 1e9}
+
+
+def ncu_traffic(name):
+    """dram__bytes_read.sum + dram__bytes_write.sum of the launch an ncu summary
+    records (its metric table rows `| metric | value unit |`), or None."""
+    path = ROOT / "profiles" / name if name else None
+    if path is None or not path.exists():
+        return None
+    found = {}
+    for line in path.read_text().splitlines():
+        cells = [c.strip().strip("`") for c in line.strip().strip("|").split("|")]
+        if len(cells) >= 2 and cells[0] in ("dram__bytes_read.sum", "dram__bytes_write.sum"):
+            value, unit = cells[1].split()
+            found[cells[0]] = float(value) * _UNITS[unit.lower()]
+    return found["dram__bytes_read.sum"] + found["dram__bytes_write.sum"] if len(found) == 2 else None
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -583,12 +603,9 @@ def main() -> int:
     gemm_ms = ea.elapsed_time(eb) / reps
     gemm_bytes = (rows_w * k_gu + b_local * (k_gu + inter_local)) * 2  # weights + x + act
     achieved = gemm_bytes / (gemm_ms / 1e3) / 1e9
-    traffic = None
-    # DRAM bytes (read + write) of one launch of this kernel from an ncu capture,
-    # recorded by hand in profiles/traffic.txt (JSON text) from the committed summary
-    prof = ROOT / "profiles" / "traffic.txt"
-    if prof.exists():
-        traffic = json.loads(prof.read_text()).get(f"decode_glu_gate_up_{args.model}_tp{tp}_b{b_local}")
+    # DRAM bytes (read + write) of one launch of this kernel, parsed from the
+    # committed ncu summary of the same launch shape; null for shapes without one
+    traffic = ncu_traffic(NCU_SUMMARIES.get((args.model, tp, b_local)))
     # prefill: the same kernel at M = b_local * prompt (capped for memory)
     m_pre = min(b_local * prompt, 16384)
     x_pre = torch.randn(m_pre, k_gu, device=dev).to(torch.bfloat16)

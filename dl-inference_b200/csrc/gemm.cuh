@@ -42,6 +42,8 @@ int gemm_occupancy(int bn, int stages, int cluster);
 GemmPlan plan_tn_gemm(int64_t rows_a, int64_t rows_b, int64_t k, dli_dtype dtype, bool allow_split);
 
 // Runs D = A * B^T on tcgen05 (bf16/f16 only; K % 8 == 0; A/B 16-byte aligned).
+// `b_mn`: B is given MN-major as [K, rows_b] with row stride ldb (matmul's right
+// operand); needs a row-major epilogue and a plan of tile width >= 64.
 // `ldo` is the output row stride (elements); `ohw` is used by kEpiNchw.
 // `const_a` / `const_b` mark an operand that no kernel writes (weights): its
 // first tiles are fetched before the kernel waits on the previous kernel.
@@ -52,7 +54,8 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
                                int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,
                                dli_dtype dtype, const GemmPlan& plan, void* workspace,
                                size_t workspace_bytes, cudaStream_t stream, bool const_a,
-                               bool const_b, int64_t glu_cols = 0, bool out_f32 = false);
+                               bool const_b, int64_t glu_cols = 0, bool out_f32 = false,
+                               bool b_mn = false);
 
 // SIMT fallback (any float dtype, any alignment): out[M,N] = A[M,K] . B + bias,
 // with B given as [N,K] (b_kmajor) or [K,N].

@@ -51,12 +51,17 @@ namespace {
 constexpr int kFmhaThreads = 192;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 2^8 before O is rescaled
 
-template <int D>
+// Shared-memory and tensor-memory plan per head dim and key-block width. Keys
+// per block 128: one CTA per SM (230 KB, all 512 TMEM columns). Keys per block
+// 64: two CTAs per SM (<= 113 KB and 256 TMEM columns each), so one CTA's
+// prologue, epilogue and softmax latency overlap the other's MMAs.
+template <int D, int BN_>
 struct FmhaLayout {
   static constexpr int BM = 128;  // query rows per CTA (tcgen05 M)
-  static constexpr int BN = 128;  // keys per block
-  static constexpr int KST = 3;
-  static constexpr int VST = D == 128 ? 2 : 3;
+  static constexpr int BN = BN_;  // keys per block
+  static constexpr int kCtasPerSm = BN_ == 64 ? 2 : 1;
+  static constexpr int KST = BN_ == 128 ? 3 : (D == 128 ? 2 : 3);
+  static constexpr int VST = BN_ == 128 ? (D == 128 ? 2 : 3) : (D == 128 ? 1 : 2);
   static constexpr int kBox = 128 * 128;                   // one 128-row x 64-element box
   static constexpr int kQBytes = (D / 64) * kBox;
   static constexpr int kKVBytes = (D / 64) * BN * 128;     // one K or V block
@@ -70,10 +75,11 @@ struct FmhaLayout {
   // s_empty[2], p_full, o_done, mma_done
   static constexpr int kBars = 1 + 2 * KST + 2 * VST + 4 + 3;
   static constexpr int kBytes = kBarOff + kBars * 8 + 16 + 1024;
-  static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kOCol = 256;
-  static_assert(kBytes <= 232448, "shared memory per CTA");
-  static_assert(2 * BN + D <= 512, "TMEM columns");
+  static constexpr uint32_t kTmemCols = BN_ == 128 ? 512 : 256;
+  static constexpr uint32_t kOCol = 2 * BN;  // S double buffer in columns [0, 2 BN), then O
+  static_assert(BN_ == 64 || BN_ == 128, "key block of 64 or 128");
+  static_assert(kBytes <= (kCtasPerSm == 2 ? 115712 : 232448), "shared memory per CTA");
+  static_assert(2 * BN + D <= static_cast<int>(kTmemCols), "TMEM columns");
 };
 
 struct FmhaParams {
@@ -115,11 +121,11 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, done && *abort_flag == 0);
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kFmhaThreads, 1)
+template <typename T, int D, int BNK>
+__global__ void __launch_bounds__(kFmhaThreads, FmhaLayout<D, BNK>::kCtasPerSm)
     fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv, const FmhaParams p) {
-  using L = FmhaLayout<D>;
+  using L = FmhaLayout<D, BNK>;
   constexpr int BM = L::BM, BN = L::BN, KST = L::KST, VST = L::VST;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
@@ -501,9 +507,9 @@ dli_status make_map_4d(CUtensorMap* map, const void* base, bool bf16, const uint
   return DLI_OK;
 }
 
-template <typename T, int D>
+template <typename T, int D, int BNK>
 dli_status launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
-  using L = FmhaLayout<D>;
+  using L = FmhaLayout<D, BNK>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap tq, tk, tv;
   const bool s_inner = a.q_ss <= a.q_sh;
@@ -538,7 +544,7 @@ dli_status launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
   p.positions = a.positions;
   p.scale_log2 = a.scale_log2;
   p.err = device_error_word();
-  auto kern = fmha_prefill_kernel<T, D>;
+  auto kern = fmha_prefill_kernel<T, D, BNK>;
   st = ensure_smem(reinterpret_cast<const void*>(kern), L::kBytes, "attention prefill (tcgen05)");
   if (st != DLI_OK) return st;
   dim3 grid(static_cast<unsigned>(ceil_div(a.seq_q, L::BM)), static_cast<unsigned>(a.hq),
@@ -578,10 +584,24 @@ bool fmha_supported(const FmhaArgs& a, dli_dtype dtype) {
   return true;
 }
 
-dli_status run_fmha_prefill(const FmhaArgs& a, dli_dtype dtype, cudaStream_t stream) {
+// DLI_SM100_ATTN_FMHA_BN: keys per block, 64 (default: two CTAs per SM) or 128
+// (one). Measured at the Qwen2-7B prefill launch (32 x 2048, 28/4 heads): 1.39
+// against 1.70 ms.
+static int fmha_block_keys() {
+  static const int bn = tuning_knob("ATTN_FMHA_BN", 64) == 128 ? 128 : 64;
+  return bn;
+}
+
+template <int BNK>
+dli_status run_fmha_bn(const FmhaArgs& a, dli_dtype dtype, cudaStream_t stream) {
   if (dtype == DLI_DTYPE_BF16)
-    return a.head_dim == 64 ? launch_fmha<__nv_bfloat16, 64>(a, stream) : launch_fmha<__nv_bfloat16, 128>(a, stream);
-  return a.head_dim == 64 ? launch_fmha<__half, 64>(a, stream) : launch_fmha<__half, 128>(a, stream);
+    return a.head_dim == 64 ? launch_fmha<__nv_bfloat16, 64, BNK>(a, stream)
+                            : launch_fmha<__nv_bfloat16, 128, BNK>(a, stream);
+  return a.head_dim == 64 ? launch_fmha<__half, 64, BNK>(a, stream) : launch_fmha<__half, 128, BNK>(a, stream);
+}
+
+dli_status run_fmha_prefill(const FmhaArgs& a, dli_dtype dtype, cudaStream_t stream) {
+  return fmha_block_keys() == 64 ? run_fmha_bn<64>(a, dtype, stream) : run_fmha_bn<128>(a, dtype, stream);
 }
 
 }  // namespace dli_sm100

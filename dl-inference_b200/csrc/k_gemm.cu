@@ -61,6 +61,8 @@ struct TcParams {
   int const_b;  // same for operand B
   int glu_cols; // SwiGLU epilogues: valid output columns (the intermediate size)
   int out_f32;  // RowMajor / Transposed: the output is float32 (operands stay T)
+  int b_mn;     // operand B is MN-major: [K, rows_b] with rows_b contiguous (matmul)
+  int bias_f32; // out_f32 epilogues: the bias is float32 (fp32 GEMM), else T
   // stream-K (tcgen05_gemm_streamk_kernel): partial tiles [ctas][2][128][BN] fp32
   // and one arrival counter per tile, zero between calls
   float* sk_part;
@@ -80,6 +82,28 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_i, int tiles_j, 
   tj = r / gsize;
 }
 
+// Operand B of one K block (BN rows x kBK). K-major B ([rows_b, K]) is one box;
+// MN-major B ([K, rows_b]) is BN/64 boxes, each a 128B-swizzled panel of kBK K
+// rows x 64 consecutive j (the host never pairs MN-major B with BN < 64).
+template <int BN>
+__device__ __forceinline__ void load_b_block(uint8_t* dst, const CUtensorMap* map, int kb, int tj, int b_mn,
+                                             uint64_t* bar) {
+  if (b_mn) {
+#pragma unroll
+    for (int c = 0; c < BN / 64; ++c) tma_load_2d(dst + c * 64 * kBK * 2, map, tj * BN + c * 64, kb * kBK, bar);
+  } else {
+    tma_load_2d(dst, map, kb * kBK, tj * BN, bar);
+  }
+}
+
+// Shared-memory descriptor of operand B at K step kk (16 elements) of a block:
+// K-major advances 32 bytes inside the swizzle atom; MN-major advances 16 K rows
+// (2 KiB), with the 64-column panels kBK * 128 bytes apart (leading offset) and
+// 8-row groups 1 KiB apart (stride offset).
+__device__ __forceinline__ uint64_t b_block_desc(uint32_t b_addr, int kk, int b_mn) {
+  return b_mn ? umma_desc_mn_sw128(b_addr + kk * 16 * 128, 64 * kBK * 2, 1024) : umma_desc_sw128(b_addr) + 2 * kk;
+}
+
 // Writes n (<= 32) accumulator values of D row `gi`, columns jc.. through the
 // epilogue mapping, adding the bias.
 template <typename T>
@@ -90,10 +114,12 @@ __device__ __forceinline__ void store_vals(const TcParams& p, int64_t gi, int jc
   if (gi >= p.rows_a) return;
   if (p.out_f32) {  // fp32 output (logits): the accumulator is stored unrounded
     float* outf = static_cast<float*>(p.out);
+    const float* biasf = static_cast<const float*>(p.bias);
     const bool tr = p.epilogue == kEpiTransposed;
-    const float bt = (tr && bias) ? to_f32(bias[gi]) : 0.f;
+    auto bias_at = [&](int64_t i) { return !bias ? 0.f : p.bias_f32 ? biasf[i] : to_f32(bias[i]); };
+    const float bt = tr ? bias_at(gi) : 0.f;
     for (int k = 0; k < n && jc + k < p.rows_b; ++k) {
-      const float bv = tr ? bt : (bias ? to_f32(bias[jc + k]) : 0.f);
+      const float bv = tr ? bt : bias_at(jc + k);
       outf[tr ? static_cast<int64_t>(jc + k) * p.ldo + gi : gi * p.ldo + jc + k] = v[k] + bv;
     }
     return;
@@ -200,6 +226,139 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, uint32_t tbase,
   }
 }
 
+// Epilogue warps (2-5) of a one-tile CTA: wait for the accumulator, then store
+// the tile (un-split) or stage its fp32 partial in shared memory for the cluster
+// reduction (split-K). `smem` is the CTA's idle operand ring.
+template <typename T, int BN>
+__device__ __forceinline__ void tile_epilogue_warps(const TcParams& p, uint8_t* smem, uint32_t tmem_base,
+                                                    uint64_t* acc_full, volatile int* flags, int ti, int tj,
+                                                    int warp, int lane) {
+  // Epilogue: warp w may only touch TMEM lanes 32*(w%4) .. 32*(w%4)+31.
+  const int quarter = warp & 3;
+  const int row = quarter * 32 + lane;
+  const int64_t gi = static_cast<int64_t>(ti) * kBM + row;
+  const int j0 = tj * BN;
+  const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+  if (!mbar_wait(acc_full, 0)) {
+    set_device_error(p.err, kDevErrGemmTimeout);
+    flags[0] = 1;
+  }
+  tc_fence_after();
+  epilogue_bar();  // every epilogue warp sees the same abort flag
+  const bool aborted = flags[0] != 0;
+  if (!aborted && p.splits == 1 && p.epilogue == kEpiGluT) {
+    // gate rows live in TMEM lanes 0-63 (quarters 0, 1), up rows in lanes 64-127:
+    // the up quarters pass their values through shared memory (the idle ring)
+    float* xch = reinterpret_cast<float*>(smem);  // [64][33]
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tbase + c, r);
+      tmem_ld_wait();
+      if (quarter >= 2) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) xch[(row - 64) * 33 + k] = __uint_as_float(r[k]);
+      }
+      epilogue_bar();
+      const int64_t col = static_cast<int64_t>(ti) * 64 + row;
+      if (quarter < 2 && col < p.glu_cols) {
+        T* out = static_cast<T*>(p.out) + col;
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+          if (j0 + c + k < p.rows_b)
+            out[static_cast<int64_t>(j0 + c + k) * p.ldo] = glu_val<T>(__uint_as_float(r[k]), xch[row * 33 + k]);
+      }
+      epilogue_bar();
+    }
+  } else if (!aborted && p.splits == 1) {
+    epilogue_tile<T, BN>(p, tbase, gi, j0);
+  } else if (p.splits > 1) {
+    // Split-K: stage this CTA's fp32 partial tile in its own shared memory
+    // (the operand ring is idle: every load was consumed before acc_full).
+    float* red = reinterpret_cast<float*>(smem);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tbase + c, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int k = 0; k < 32; k += 4)
+        *reinterpret_cast<float4*>(red + row * (BN + 4) + c + k) =
+            make_float4(aborted ? 0.f : __uint_as_float(r[k]), aborted ? 0.f : __uint_as_float(r[k + 1]),
+                        aborted ? 0.f : __uint_as_float(r[k + 2]), aborted ? 0.f : __uint_as_float(r[k + 3]));
+    }
+  }
+}
+
+// Split-K tail, run by every thread of every CTA of the tile's cluster after
+// the partials were staged (tile_epilogue_warps) and the CTA synchronised.
+template <typename T, int BN, int kThreads = kGemmThreads>
+__device__ __forceinline__ void tile_cluster_reduce(const TcParams& p, uint8_t* smem, int ti, int tj, int split) {
+  // The K-splits of this tile form one thread-block cluster (ranks 0..S-1 along
+  // y). After the cluster barrier every partial is visible through distributed
+  // shared memory; CTA `split` sums rows [split*R, (split+1)*R) of all S
+  // partials in rank order (deterministic) and writes them. The second barrier
+  // keeps every CTA's shared memory alive until all ranks finished reading.
+  cluster_sync();
+  const int S = p.splits;
+  const uint32_t red_local = smem_u32(smem);
+  if (p.epilogue == kEpiGluT) {
+    // each rank reduces gate rows [split*R, ...) of 0..63 and their up rows (+64)
+    const int R = (64 + S - 1) / S;
+    const int quads = R * (BN / 4);
+    for (int q = threadIdx.x; q < quads; q += kThreads) {
+      const int rr = split * R + q % R;
+      const int cq = (q / R) * 4;
+      if (rr >= 64) continue;
+      const uint32_t og = static_cast<uint32_t>((rr * (BN + 4) + cq) * 4);
+      const uint32_t ou = static_cast<uint32_t>(((rr + 64) * (BN + 4) + cq) * 4);
+      float4 pg[8], pu[8];
+#pragma unroll
+      for (int s2 = 0; s2 < 8; ++s2) {
+        if (s2 < S) {
+          pg[s2] = ld_dsmem_f4(mapa_shared(red_local + og, s2));
+          pu[s2] = ld_dsmem_f4(mapa_shared(red_local + ou, s2));
+        }
+      }
+      float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s2 = 0; s2 < 8; ++s2) {
+        if (s2 < S) {
+          g[0] += pg[s2].x; g[1] += pg[s2].y; g[2] += pg[s2].z; g[3] += pg[s2].w;
+          u[0] += pu[s2].x; u[1] += pu[s2].y; u[2] += pu[s2].z; u[3] += pu[s2].w;
+        }
+      }
+      if (tj * BN + cq < p.rows_b) store_glu_t<T>(p, ti, rr, tj * BN + cq, g, u, 4);
+    }
+  }
+  const int R = (kBM + S - 1) / S;  // rows reduced by each rank (the last may get fewer)
+  const int quads = p.epilogue == kEpiGluT ? 0 : R * (BN / 4);
+  for (int q = threadIdx.x; q < quads; q += kThreads) {
+    const int rr = split * R + q % R;  // consecutive threads: consecutive rows
+    const int cq = (q / R) * 4;
+    if (rr >= kBM) continue;
+    const uint32_t off = static_cast<uint32_t>((rr * (BN + 4) + cq) * 4);
+    // issue every rank's load before the first add: one DSMEM round trip, not S
+    float4 part[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+      if (s < S) part[s] = ld_dsmem_f4(mapa_shared(red_local + off, s));
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      if (s < S) {
+        v[0] += part[s].x;
+        v[1] += part[s].y;
+        v[2] += part[s].z;
+        v[3] += part[s].w;
+      }
+    }
+    const int64_t gi = static_cast<int64_t>(ti) * kBM + rr;
+    if (tj * BN + cq < p.rows_b) store_vals<T>(p, gi, tj * BN + cq, v, 4);
+  }
+  cluster_sync();
+}
+
 template <typename T, int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tcgen05_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -253,7 +412,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint8_t* sa = smem + it * L::kStageBytes;
         mbar_arrive_expect_tx(&full[it], L::kStageBytes);
         if (p.const_a) tma_load_2d(sa, &tmap_a, (kb0 + it) * kBK, ti * kBM, &full[it]);
-        else tma_load_2d(sa + L::kABytes, &tmap_b, (kb0 + it) * kBK, tj * BN, &full[it]);
+        else load_b_block<BN>(sa + L::kABytes, &tmap_b, kb0 + it, tj, p.b_mn, &full[it]);
       }
       pdl_wait();
       pdl_trigger();
@@ -263,7 +422,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t ph = (it / STAGES) & 1;
         uint8_t* sa = smem + s * L::kStageBytes;
         if (it < pre) {  // stage armed above: add the dependent operand
-          if (p.const_a) tma_load_2d(sa + L::kABytes, &tmap_b, (kb0 + it) * kBK, tj * BN, &full[s]);
+          if (p.const_a) load_b_block<BN>(sa + L::kABytes, &tmap_b, kb0 + it, tj, p.b_mn, &full[s]);
           else tma_load_2d(sa, &tmap_a, (kb0 + it) * kBK, ti * kBM, &full[s]);
           continue;
         }
@@ -275,7 +434,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (flags[0]) break;
         mbar_arrive_expect_tx(&full[s], L::kStageBytes);
         tma_load_2d(sa, &tmap_a, (kb0 + it) * kBK, ti * kBM, &full[s]);
-        tma_load_2d(sa + L::kABytes, &tmap_b, (kb0 + it) * kBK, tj * BN, &full[s]);
+        load_b_block<BN>(sa + L::kABytes, &tmap_b, kb0 + it, tj, p.b_mn, &full[s]);
         issued = it + 1;
       }
       // No bulk copy may still be writing shared memory when the CTA exits.
@@ -284,7 +443,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, BN);
+      const uint32_t idesc =
+          umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, BN) | (p.b_mn ? (1u << 16) : 0u);
       for (int it = 0; it < nkb; ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
@@ -296,138 +456,332 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
         const uint64_t adesc = umma_desc_sw128(a_addr);
-        const uint64_t bdesc = umma_desc_sw128(a_addr + L::kABytes);
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
-          umma_f16(tmem_base, adesc + 2 * kk, bdesc + 2 * kk, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tmem_base, adesc + 2 * kk, b_block_desc(a_addr + L::kABytes, kk, p.b_mn), idesc,
+                   (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&empty[s]);
       }
       umma_commit(acc_full);
     }
   } else {
-    // Epilogue: warp w may only touch TMEM lanes 32*(w%4) .. 32*(w%4)+31.
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const int64_t gi = static_cast<int64_t>(ti) * kBM + row;
-    const int j0 = tj * BN;
-    const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-    if (!mbar_wait(acc_full, 0)) {
-      set_device_error(p.err, kDevErrGemmTimeout);
-      flags[0] = 1;
-    }
+    tile_epilogue_warps<T, BN>(p, smem, tmem_base, acc_full, flags, ti, tj, warp, lane);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (p.splits > 1) tile_cluster_reduce<T, BN>(p, smem, ti, tj, split);
+  if (warp == 1) {
+    __syncwarp();
     tc_fence_after();
-    epilogue_bar();  // every epilogue warp sees the same abort flag
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// ---- fp32 GEMM on tcgen05 through a three-term bf16 split -----------------------
+// fp32 operands stream in by TMA unchanged (128B-swizzled boxes of 32 floats).
+// Converter warps split every element into three bf16 terms, x = h + m + l with
+// h = bf16(x), m = bf16(x - h), l = bf16(x - h - m) (both differences exact in
+// fp32), and write them as the operand tiles of f16-kind MMAs. Each 64-wide K
+// block accumulates the six products whose order is at most 2^-16 below x*y
+// (h*l, l*h, m*m, h*m, m*h, h*h) into a fresh tensor-memory buffer; the same
+// warps then add that block partial into fp32 registers with round-to-nearest
+// adds. The tensor core's own accumulation loses a little on every MMA it adds
+// into a running sum (the error grows with the number of MMAs per sum), so
+// bounding each hardware sum to one K block and promoting block sums to
+// registers keeps the result at the accuracy of an fp32 FFMA GEMM. Dropped split
+// terms are near 2^-26 of each product. Non-finite inputs keep h, with m = l = 0.
+//
+// 320 threads: warp 0 TMA producer, warp 1 TMEM owner and MMA issuer, warps 2-9
+// converters, promoters and epilogue (warp w reads TMEM lanes 32*(w%4).. and
+// column half (w-2)/4 of each block). Rings: raw (TMA -> converters), converted
+// (converters -> MMA) and the two block-partial buffers in tensor memory
+// (MMA -> promoters), every wait bounded. Split-K partials are reduced over the
+// cluster like the bf16 kernel's, storing float32.
+constexpr int kSplitTerms = 3;
+constexpr int kF32SplitThreads = 320;
+constexpr int kF32SplitWorkers = 256;  // warps 2-9
+
+template <int BN, int RS, int CS>
+struct F32x3Layout {
+  static constexpr int kRawStageBytes = (kBM + BN) * 256;                 // fp32 [A | B] of one K block
+  static constexpr int kCvStageBytes = (kBM + BN) * 128 * kSplitTerms;   // bf16 [A h|m|l | B h|m|l]
+  static constexpr int kCvOff = RS * kRawStageBytes;
+  static constexpr int kBarOffset = kCvOff + CS * kCvStageBytes;
+  // raw_full[RS], raw_empty[RS], cv_full[CS], cv_empty[CS], acc_full[2], acc_empty[2], mma_done
+  static constexpr int kBytes = kBarOffset + (2 * RS + 2 * CS + 5) * 8 + 16 + 1024;
+  static constexpr uint32_t kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;  // two block-partial buffers
+  static_assert(kBM * (BN + 4) * 4 <= kBarOffset, "split-K staging must fit the rings");
+  static_assert(kBytes <= 232448, "shared memory per CTA");
+};
+
+// Splits 4 floats into three bf16 terms, stored as 8 bytes in each plane
+// (planes `plane` bytes apart).
+__device__ __forceinline__ void split_bf16x4(const float4 v, uint8_t* dst, int plane) {
+  const float x[4] = {v.x, v.y, v.z, v.w};
+  uint32_t w[3][2];
+#pragma unroll
+  for (int e = 0; e < 4; e += 2) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x[e], x[e + 1]);
+    const float2 hf = __bfloat1622float2(h);
+    const bool fin0 = fabsf(hf.x) < __int_as_float(0x7f800000), fin1 = fabsf(hf.y) < __int_as_float(0x7f800000);
+    const float r0 = fin0 ? x[e] - hf.x : 0.f, r1 = fin1 ? x[e + 1] - hf.y : 0.f;
+    const __nv_bfloat162 m = __floats2bfloat162_rn(r0, r1);
+    const float2 mf = __bfloat1622float2(m);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(r0 - mf.x, r1 - mf.y);
+    w[0][e / 2] = *reinterpret_cast<const uint32_t*>(&h);
+    w[1][e / 2] = *reinterpret_cast<const uint32_t*>(&m);
+    w[2][e / 2] = *reinterpret_cast<const uint32_t*>(&l);
+  }
+#pragma unroll
+  for (int t = 0; t < 3; ++t) *reinterpret_cast<uint2*>(dst + t * plane) = make_uint2(w[t][0], w[t][1]);
+}
+
+// Converts one operand block of `rows` rows x 64 K (or, MN-major, 64 K rows per
+// 64-column panel) from its raw fp32 boxes to 128B-swizzled bf16 planes
+// (`plane` bytes apart). Raw boxes come in groups of G rows: group g, K half h
+// at (2g + h) * G * 128 bytes, row r % G at 128 bytes per row, 16-byte chunks
+// XOR-swizzled by r % 8. Converted row r sits at r * 128 with chunks swizzled
+// the same way. One task is one raw chunk (4 floats): 8 consecutive threads read
+// one 128-byte box row and 16 consecutive threads write one 128-byte bf16 row,
+// both conflict-free.
+__device__ __forceinline__ void split_block(const uint8_t* raw, int G, int rows, uint8_t* cv, int plane, int tid) {
+#pragma unroll 2
+  for (int t = tid; t < rows * 16; t += kF32SplitWorkers) {
+    const int r = t >> 4, h = (t >> 3) & 1, qc = t & 7, sw = r & 7;
+    const int g = r / G, rg = r - g * G;
+    const float4 v = *reinterpret_cast<const float4*>(raw + (2 * g + h) * G * 128 + rg * 128 + ((qc ^ sw) << 4));
+    const int off = r * 128 + (((h * 4 + (qc >> 1)) ^ sw) << 4) + (qc & 1) * 8;
+    split_bf16x4(v, cv + off, plane);
+  }
+}
+
+// Adds n (16 or 32) tensor-memory columns of this thread's lane into acc.
+template <int N>
+__device__ __forceinline__ void tmem_add_cols(uint32_t taddr, float* acc) {
+  if constexpr (N == 16) {
+    uint32_t r[16];
+    tmem_ld_32x32b_x16(taddr, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] += __uint_as_float(r[i]);
+  } else {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] += __uint_as_float(r[i]);
+  }
+}
+
+template <int BN, int RS, int CS>
+__global__ void __launch_bounds__(kF32SplitThreads, 1)
+    tcgen05_gemm_f32x3_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                              const __grid_constant__ CUtensorMap tmap_b, const TcParams p) {
+  using L = F32x3Layout<BN, RS, CS>;
+  constexpr int HALF = BN / 2;                 // columns per promoter thread
+  constexpr int CH = HALF < 32 ? HALF : 32;    // columns per TMEM load
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* raw_empty = raw_full + RS;
+  uint64_t* cv_full = raw_empty + RS;
+  uint64_t* cv_empty = cv_full + CS;
+  uint64_t* acc_full = cv_empty + CS;   // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint64_t* mma_done = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  int ti, tj;
+  tile_coords(tile, p.tiles_i, p.tiles_j, ti, tj);
+  const int kb0 = static_cast<int>(static_cast<int64_t>(split) * p.kblocks / p.splits);
+  const int nkb = static_cast<int>(static_cast<int64_t>(split + 1) * p.kblocks / p.splits) - kb0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(mma_done, 1);
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&raw_full[s], 1);
+      mbar_init(&raw_empty[s], 8);  // one arrive per converter warp
+    }
+    for (int s = 0; s < CS; ++s) {
+      mbar_init(&cv_full[s], 8);
+      mbar_init(&cv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);  // one arrive per promoter warp
+    }
+    flags[0] = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      pdl_wait();
+      pdl_trigger();
+      int issued = 0;
+      for (int it = 0; it < nkb; ++it) {
+        const int s = it % RS;
+        if (!mbar_wait(&raw_empty[s], ((it / RS) & 1) ^ 1)) {
+          set_device_error(p.err, kDevErrGemmTimeout);
+          flags[0] = 1;
+          break;
+        }
+        if (flags[0]) break;
+        uint8_t* ra = smem + s * L::kRawStageBytes;
+        uint8_t* rb = ra + kBM * 256;
+        const int k0 = (kb0 + it) * kBK;
+        mbar_arrive_expect_tx(&raw_full[s], L::kRawStageBytes);
+        tma_load_2d(ra, &tmap_a, k0, ti * kBM, &raw_full[s]);
+        tma_load_2d(ra + kBM * 128, &tmap_a, k0 + 32, ti * kBM, &raw_full[s]);
+        if (p.b_mn) {
+#pragma unroll
+          for (int q = 0; q < 2 * (BN / 64); ++q)
+            tma_load_2d(rb + q * 64 * 128, &tmap_b, tj * BN + q * 32, k0, &raw_full[s]);
+        } else {
+          tma_load_2d(rb, &tmap_b, k0, tj * BN, &raw_full[s]);
+          tma_load_2d(rb + BN * 128, &tmap_b, k0 + 32, tj * BN, &raw_full[s]);
+        }
+        issued = it + 1;
+      }
+      // No bulk copy may still be writing shared memory when the CTA exits.
+      for (int it = max(0, issued - RS); it < issued; ++it) mbar_wait(&raw_full[it % RS], (it / RS) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(true, kBM, BN) | (p.b_mn ? (1u << 16) : 0u);
+      int done = 0;
+      for (int it = 0; it < nkb; ++it) {
+        const int s = it % CS, b = it & 1;
+        if (!mbar_wait(&cv_full[s], (it / CS) & 1) || !mbar_wait(&acc_empty[b], ((it >> 1) & 1) ^ 1) || flags[0]) {
+          set_device_error(p.err, kDevErrGemmTimeout);
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_h = smem_u32(smem + L::kCvOff + s * L::kCvStageBytes);
+        const uint32_t a_m = a_h + kBM * 128, a_l = a_m + kBM * 128;
+        const uint32_t b_h = a_h + kSplitTerms * kBM * 128, b_m = b_h + BN * 128, b_l = b_m + BN * 128;
+        const uint32_t acc = tmem_base + static_cast<uint32_t>(b * BN);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          const uint64_t ah = umma_desc_sw128(a_h) + 2 * kk, am = umma_desc_sw128(a_m) + 2 * kk,
+                         al = umma_desc_sw128(a_l) + 2 * kk;
+          const uint64_t bh = b_block_desc(b_h, kk, p.b_mn), bm = b_block_desc(b_m, kk, p.b_mn),
+                         bl = b_block_desc(b_l, kk, p.b_mn);
+          umma_f16(acc, ah, bl, idesc, kk > 0 ? 1u : 0u);  // a fresh sum per K block
+          umma_f16(acc, al, bh, idesc, 1u);
+          umma_f16(acc, am, bm, idesc, 1u);
+          umma_f16(acc, ah, bm, idesc, 1u);
+          umma_f16(acc, am, bh, idesc, 1u);
+          umma_f16(acc, ah, bh, idesc, 1u);
+        }
+        umma_commit(&cv_empty[s]);
+        umma_commit(&acc_full[b]);
+        done = it + 1;
+      }
+      if (done < nkb) {  // aborted: release promoters waiting on a block that never comes
+        umma_commit(&acc_full[0]);
+        umma_commit(&acc_full[1]);
+      }
+      // every issued MMA has finished before the CTA releases tensor memory
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0);
+    }
+  } else {
+    // warps 2-9: convert block it, then promote block it-1 (its MMAs overlap the
+    // conversion of block it); the last block is promoted after the loop
+    const int tid = threadIdx.x - 64;
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(half * HALF);
+    float accum[HALF];
+#pragma unroll
+    for (int i = 0; i < HALF; ++i) accum[i] = 0.f;
+    bool ok = true;
+    auto promote = [&](int j) -> bool {
+      const int b = j & 1;
+      const bool w = mbar_wait(&acc_full[b], (j >> 1) & 1);
+      if (!__all_sync(0xffffffffu, w)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < HALF; c += CH) tmem_add_cols<CH>(lane_base + static_cast<uint32_t>(b * BN + c), accum + c);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      return true;
+    };
+    for (int it = 0; it < nkb && ok; ++it) {
+      const int rs = it % RS, cs = it % CS;
+      bool w = mbar_wait(&raw_full[rs], (it / RS) & 1);
+      w = w && mbar_wait(&cv_empty[cs], ((it / CS) & 1) ^ 1);
+      const int abort_seen = __shfl_sync(0xffffffffu, flags[0], 0);
+      if (!__all_sync(0xffffffffu, w) || abort_seen) {
+        ok = false;
+        break;
+      }
+      const uint8_t* ra = smem + rs * L::kRawStageBytes;
+      uint8_t* cv = smem + L::kCvOff + cs * L::kCvStageBytes;
+      split_block(ra, kBM, kBM, cv, kBM * 128, tid);
+      split_block(ra + kBM * 256, p.b_mn ? 64 : BN, BN, cv + kSplitTerms * kBM * 128, BN * 128, tid);
+      fence_proxy_async_smem();  // the bf16 tiles are read by the tensor core (async proxy)
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&raw_empty[rs]);
+        mbar_arrive(&cv_full[cs]);
+      }
+      if (it > 0) ok = promote(it - 1);
+    }
+    if (ok && nkb > 0) ok = promote(nkb - 1);
+    if (!ok) {
+      if (lane == 0) {
+        set_device_error(p.err, kDevErrGemmTimeout);
+        flags[0] = 1;
+      }
+    }
+    // named barrier over the 8 epilogue warps: every one sees the same abort flag
+    asm volatile("bar.sync 1, %0;" ::"n"(kF32SplitWorkers) : "memory");
     const bool aborted = flags[0] != 0;
-    if (!aborted && p.splits == 1 && p.epilogue == kEpiGluT) {
-      // gate rows live in TMEM lanes 0-63 (quarters 0, 1), up rows in lanes 64-127:
-      // the up quarters pass their values through shared memory (the idle ring)
-      float* xch = reinterpret_cast<float*>(smem);  // [64][33]
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + c, r);
-        tmem_ld_wait();
-        if (quarter >= 2) {
+    const int64_t gi = static_cast<int64_t>(ti) * kBM + row;
+    const int jc = tj * BN + half * HALF;
+    if (p.splits == 1) {
+      if (!aborted) {
 #pragma unroll
-          for (int k = 0; k < 32; ++k) xch[(row - 64) * 33 + k] = __uint_as_float(r[k]);
+        for (int c = 0; c < HALF; c += CH) {
+          float v[CH];  // a copy: accum stays in registers (constant indices only)
+#pragma unroll
+          for (int i = 0; i < CH; ++i) v[i] = accum[c + i];
+          if (jc + c < p.rows_b) store_vals<__nv_bfloat16>(p, gi, jc + c, v, CH);
         }
-        epilogue_bar();
-        const int64_t col = static_cast<int64_t>(ti) * 64 + row;
-        if (quarter < 2 && col < p.glu_cols) {
-          T* out = static_cast<T*>(p.out) + col;
-#pragma unroll
-          for (int k = 0; k < 32; ++k)
-            if (j0 + c + k < p.rows_b)
-              out[static_cast<int64_t>(j0 + c + k) * p.ldo] = glu_val<T>(__uint_as_float(r[k]), xch[row * 33 + k]);
-        }
-        epilogue_bar();
       }
-    } else if (!aborted && p.splits == 1) {
-      epilogue_tile<T, BN>(p, tbase, gi, j0);
-    } else if (p.splits > 1) {
-      // Split-K: stage this CTA's fp32 partial tile in its own shared memory
-      // (the operand ring is idle: every load was consumed before acc_full).
-      float* red = reinterpret_cast<float*>(smem);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tbase + c, r);
-        tmem_ld_wait();
+    } else {
+      float* red = reinterpret_cast<float*>(smem);  // the idle raw ring: [128][BN + 4]
 #pragma unroll
-        for (int k = 0; k < 32; k += 4)
-          *reinterpret_cast<float4*>(red + row * (BN + 4) + c + k) =
-              make_float4(aborted ? 0.f : __uint_as_float(r[k]), aborted ? 0.f : __uint_as_float(r[k + 1]),
-                          aborted ? 0.f : __uint_as_float(r[k + 2]), aborted ? 0.f : __uint_as_float(r[k + 3]));
-      }
+      for (int c = 0; c < HALF; c += 4)
+        *reinterpret_cast<float4*>(red + row * (BN + 4) + half * HALF + c) =
+            aborted ? make_float4(0.f, 0.f, 0.f, 0.f)
+                    : make_float4(accum[c], accum[c + 1], accum[c + 2], accum[c + 3]);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (p.splits > 1) {
-    // The K-splits of this tile form one thread-block cluster (ranks 0..S-1 along
-    // y). After the cluster barrier every partial is visible through distributed
-    // shared memory; CTA `split` sums rows [split*R, (split+1)*R) of all S
-    // partials in rank order (deterministic) and writes them. The second barrier
-    // keeps every CTA's shared memory alive until all ranks finished reading.
-    cluster_sync();
-    const int S = p.splits;
-    const uint32_t red_local = smem_u32(smem);
-    if (p.epilogue == kEpiGluT) {
-      // each rank reduces gate rows [split*R, ...) of 0..63 and their up rows (+64)
-      const int R = (64 + S - 1) / S;
-      const int quads = R * (BN / 4);
-      for (int q = threadIdx.x; q < quads; q += kGemmThreads) {
-        const int rr = split * R + q % R;
-        const int cq = (q / R) * 4;
-        if (rr >= 64) continue;
-        const uint32_t og = static_cast<uint32_t>((rr * (BN + 4) + cq) * 4);
-        const uint32_t ou = static_cast<uint32_t>(((rr + 64) * (BN + 4) + cq) * 4);
-        float4 pg[8], pu[8];
-#pragma unroll
-        for (int s2 = 0; s2 < 8; ++s2) {
-          if (s2 < S) {
-            pg[s2] = ld_dsmem_f4(mapa_shared(red_local + og, s2));
-            pu[s2] = ld_dsmem_f4(mapa_shared(red_local + ou, s2));
-          }
-        }
-        float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int s2 = 0; s2 < 8; ++s2) {
-          if (s2 < S) {
-            g[0] += pg[s2].x; g[1] += pg[s2].y; g[2] += pg[s2].z; g[3] += pg[s2].w;
-            u[0] += pu[s2].x; u[1] += pu[s2].y; u[2] += pu[s2].z; u[3] += pu[s2].w;
-          }
-        }
-        if (tj * BN + cq < p.rows_b) store_glu_t<T>(p, ti, rr, tj * BN + cq, g, u, 4);
-      }
-    }
-    const int R = (kBM + S - 1) / S;  // rows reduced by each rank (the last may get fewer)
-    const int quads = p.epilogue == kEpiGluT ? 0 : R * (BN / 4);
-    for (int q = threadIdx.x; q < quads; q += kGemmThreads) {
-      const int rr = split * R + q % R;  // consecutive threads: consecutive rows
-      const int cq = (q / R) * 4;
-      if (rr >= kBM) continue;
-      const uint32_t off = static_cast<uint32_t>((rr * (BN + 4) + cq) * 4);
-      // issue every rank's load before the first add: one DSMEM round trip, not S
-      float4 part[8];
-#pragma unroll
-      for (int s = 0; s < 8; ++s)
-        if (s < S) part[s] = ld_dsmem_f4(mapa_shared(red_local + off, s));
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        if (s < S) {
-          v[0] += part[s].x;
-          v[1] += part[s].y;
-          v[2] += part[s].z;
-          v[3] += part[s].w;
-        }
-      }
-      const int64_t gi = static_cast<int64_t>(ti) * kBM + rr;
-      if (tj * BN + cq < p.rows_b) store_vals<T>(p, gi, tj * BN + cq, v, 4);
-    }
-    cluster_sync();
-  }
+  if (p.splits > 1) tile_cluster_reduce<__nv_bfloat16, BN, kF32SplitThreads>(p, smem, ti, tj, split);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -519,7 +873,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint8_t* sa = smem + s * L::kStageBytes;
           mbar_arrive_expect_tx(&full[s], L::kStageBytes);
           tma_load_2d(sa, &tmap_a, kb * kBK, ti * kBM, &full[s]);
-          tma_load_2d(sa + L::kABytes, &tmap_b, kb * kBK, tj * BN, &full[s]);
+          load_b_block<BN>(sa + L::kABytes, &tmap_b, kb, tj, p.b_mn, &full[s]);
           ++it;
         }
       }
@@ -528,7 +882,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, BN);
+      const uint32_t idesc =
+          umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, BN) | (p.b_mn ? (1u << 16) : 0u);
       int it = 0, lt = 0;
       bool stop = false;
       for (int tile = blockIdx.x; tile < tiles && !stop; tile += gridDim.x, ++lt) {
@@ -552,10 +907,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
           const uint64_t adesc = umma_desc_sw128(a_addr);
-          const uint64_t bdesc = umma_desc_sw128(a_addr + L::kABytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_f16(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(acc, adesc + 2 * kk, b_block_desc(a_addr + L::kABytes, kk, p.b_mn), idesc,
+                     (kb > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&empty[s]);
           ++it;
         }
@@ -1119,6 +1474,24 @@ dli_status make_kmajor_map(CUtensorMap* map, const void* base, int64_t rows, int
   return DLI_OK;
 }
 
+// MN-major 2-D map over [k, cols] (cols contiguous, row stride `ld` elements),
+// box {64 columns, kBK rows}: the right operand of matmul.
+dli_status make_mnmajor_map(CUtensorMap* map, const void* base, int64_t k, int64_t cols, int64_t ld, bool bf16) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(DLI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(k)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+  const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(kBK)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DLI_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
+  return DLI_OK;
+}
+
 // Pipeline depth per tile width. Narrow (decode, swap-AB) tiles use ~100 KB of
 // shared memory so two CTAs share an SM: one CTA's prologue and split-K
 // epilogue overlap the other's weight streaming. Wide tiles fill ~200 KB.
@@ -1253,6 +1626,10 @@ int layout_bytes(int bn, int stages) {
     case 6408: return TcLayout<64, 8>::kBytes;
     case 12806: return TcLayout<128, 6>::kBytes;
     case 25604: return TcLayout<256, 4>::kBytes;
+    // stages 0: the fp32 split-bf16 kernel's rings at that tile width
+    case 3200: return F32x3Layout<32, 3, 1>::kBytes;
+    case 6400: return F32x3Layout<64, 3, 1>::kBytes;
+    case 12800: return F32x3Layout<128, 2, 1>::kBytes;
     default: return 0;
   }
 }
@@ -1357,8 +1734,10 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
                                int64_t ldb, int64_t ldo, int epilogue, int64_t ohw,
                                dli_dtype dtype, const GemmPlan& plan, void* workspace,
                                size_t workspace_bytes, cudaStream_t stream, bool const_a,
-                               bool const_b, int64_t glu_cols, bool out_f32) {
+                               bool const_b, int64_t glu_cols, bool out_f32, bool b_mn) {
   if (!plan.tcgen05) return fail(DLI_ERR_UNSUPPORTED, "gemm: shape not served by tcgen05");
+  if (b_mn && (plan.bn < 64 || plan.streamk_ctas > 0 || epilogue != kEpiRowMajor))
+    return fail(DLI_ERR_UNSUPPORTED, "gemm: MN-major B needs a row-major plan with tile width >= 64");
   if (out_f32 && epilogue != kEpiRowMajor && epilogue != kEpiTransposed)
     return fail(DLI_ERR_UNSUPPORTED, "gemm: float32 output only for plain row-major/transposed epilogues");
   if (!aligned(a, 16) || !aligned(b, 16) || lda % 8 != 0 || ldb % 8 != 0)
@@ -1371,7 +1750,7 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
   CUtensorMap ma, mb;
   dli_status st = make_kmajor_map(&ma, a, rows_a, k, lda, kBM, bf16);
   if (st != DLI_OK) return st;
-  st = make_kmajor_map(&mb, b, rows_b, k, ldb, plan.bn, bf16);
+  st = b_mn ? make_mnmajor_map(&mb, b, k, rows_b, ldb, bf16) : make_kmajor_map(&mb, b, rows_b, k, ldb, plan.bn, bf16);
   if (st != DLI_OK) return st;
   TcParams p{};
   p.rows_a = static_cast<int>(rows_a);
@@ -1391,6 +1770,7 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
   p.const_b = const_b ? 1 : 0;
   p.glu_cols = static_cast<int>(glu_cols);
   p.out_f32 = out_f32 ? 1 : 0;
+  p.b_mn = b_mn ? 1 : 0;
   if (plan.streamk_ctas > 0) {
     p.sk_part = static_cast<float*>(workspace);
     p.sk_count = reinterpret_cast<int*>(static_cast<char*>(workspace) +
@@ -1405,6 +1785,99 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
     return bf16 ? launch_tc_persistent<__nv_bfloat16>(ma, mb, p, stream) : launch_tc_persistent<__half>(ma, mb, p, stream);
   if (bf16) return launch_tc_bn<__nv_bfloat16>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
   return launch_tc_bn<__half>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
+}
+
+// fp32 2-D map over [outer, inner] (row stride `ld` floats), 128B-swizzled
+// boxes of 32 x box_outer: K-major operands (inner = K) and MN-major B (inner = N).
+dli_status make_f32_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t ld,
+                        int box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(DLI_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+  const cuuint32_t box[2] = {32u, static_cast<cuuint32_t>(box_outer)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DLI_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
+  return DLI_OK;
+}
+
+template <int BN, int RS, int CS>
+dli_status launch_f32x3(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p, int splits,
+                        cudaStream_t stream) {
+  using L = F32x3Layout<BN, RS, CS>;
+  auto kernel = tcgen05_gemm_f32x3_kernel<BN, RS, CS>;
+  const dli_status st = ensure_smem(reinterpret_cast<const void*>(kernel), L::kBytes, "fp32 tcgen05 gemm");
+  if (st != DLI_OK) return st;
+  dim3 grid(static_cast<unsigned>(p.tiles_i * p.tiles_j), static_cast<unsigned>(splits));
+  launch_pdl_cluster(kernel, grid, dim3(kF32SplitThreads), L::kBytes, stream, static_cast<unsigned>(splits), ma, mb,
+                     p);
+  return check_launch("fp32 tcgen05 gemm");
+}
+
+// fp32 D = A * B^T (+ bias) on tcgen05 through the three-term bf16 split: A [rows_a,
+// K] K-major; B [rows_b, K] K-major, or [K, rows_b] MN-major (b_mn). True when
+// it served the call (16-byte aligned operands, K and the leading dimensions
+// multiples of 4 floats, DLI_SM100_GEMM_F32X3 not 0); *status then holds the
+// launch result.
+bool try_gemm_f32x3(const void* a, const void* b, const void* bias, void* out, int64_t rows_a, int64_t rows_b,
+                    int64_t k, int64_t ldb, int64_t ldo, int epilogue, bool b_mn, cudaStream_t stream,
+                    dli_status* status) {
+  static const bool on = tuning_knob("GEMM_F32X3", 1) != 0;
+  if (!on || k % 4 != 0 || ldb % 4 != 0 || !aligned(a, 16) || !aligned(b, 16) || rows_a <= 0 || rows_b <= 0 ||
+      rows_a > (1ll << 30) || rows_b > (1ll << 30) || k > (1ll << 30))
+    return false;
+  const int bn = (rows_b <= 32 && !b_mn) ? 32 : rows_b <= 64 ? 64 : 128;
+  const int stages_code = 0;
+  GemmPlan plan;
+  plan.bn = bn;
+  plan.tiles_i = static_cast<int>(ceil_div(rows_a, kBM));
+  plan.tiles_j = static_cast<int>(ceil_div(rows_b, bn));
+  plan.kblocks = static_cast<int>(ceil_div(k, kBK));
+  if (static_cast<int64_t>(plan.tiles_i) * plan.tiles_j > 0x7fffffff) return false;
+  const int64_t tiles = static_cast<int64_t>(plan.tiles_i) * plan.tiles_j;
+  const int slots = sm_count() * std::max(1, gemm_occupancy(bn, stages_code, 1));
+  plan.splits = 1;
+  if (tiles < slots) {  // the bf16 plan's rule: largest cluster split that fits, >= 3 K blocks each
+    for (int s = 8; s >= 2; --s) {
+      if (plan.kblocks < 3 * s || tiles * s > slots) continue;
+      if (tiles <= gemm_occupancy(bn, stages_code, s)) {
+        plan.splits = s;
+        break;
+      }
+    }
+  }
+  CUtensorMap ma, mb;
+  *status = make_f32_map(&ma, a, k, rows_a, k, kBM);
+  if (*status == DLI_OK)
+    *status = b_mn ? make_f32_map(&mb, b, rows_b, k, ldb, kBK) : make_f32_map(&mb, b, k, rows_b, ldb, bn);
+  if (*status != DLI_OK) return true;
+  TcParams p{};
+  p.rows_a = static_cast<int>(rows_a);
+  p.rows_b = static_cast<int>(rows_b);
+  p.tiles_i = plan.tiles_i;
+  p.tiles_j = plan.tiles_j;
+  p.kblocks = plan.kblocks;
+  p.splits = plan.splits;
+  p.epilogue = epilogue;
+  p.ldo = ldo;
+  p.ohw = 1;
+  p.out_vec = 0;
+  p.bias = bias;
+  p.out = out;
+  p.err = device_error_word();
+  p.out_f32 = 1;
+  p.bias_f32 = 1;
+  p.b_mn = b_mn ? 1 : 0;
+  switch (bn) {
+    case 32: *status = launch_f32x3<32, 3, 1>(ma, mb, p, plan.splits, stream); break;
+    case 64: *status = launch_f32x3<64, 3, 1>(ma, mb, p, plan.splits, stream); break;
+    default: *status = launch_f32x3<128, 2, 1>(ma, mb, p, plan.splits, stream); break;
+  }
+  return true;
 }
 
 // Cluster split-K fp32 GEMM: true when it served the call (fp32, 16-byte aligned
@@ -1489,6 +1962,12 @@ extern "C" dli_status dli_sm100_linear(const void* x, const void* w, const void*
   if (m == 0) return ok();
   if (!x || !w || !y) return fail(DLI_ERR_INVALID_ARGUMENT, "linear: null pointer");
   const bool swap = m <= kSwapRows;
+  if (dtype == DLI_DTYPE_F32) {
+    dli_status st = DLI_OK;
+    const bool served = swap ? try_gemm_f32x3(w, x, bias, y, n, m, k, k, n, kEpiTransposed, false, as_stream(stream), &st)
+                             : try_gemm_f32x3(x, w, bias, y, m, n, k, k, n, kEpiRowMajor, false, as_stream(stream), &st);
+    if (served) return st;
+  }
   const GemmPlan plan = linear_plan(m, n, k, dtype, workspace ? workspace_bytes : 0, false);
   const bool tma_ok = aligned(x, 16) && aligned(w, 16);
   if (plan.tcgen05 && tma_ok) {
@@ -1552,5 +2031,21 @@ extern "C" dli_status dli_sm100_matmul(const void* a, const void* b, void* out, 
   if (m < 0 || n <= 0 || k <= 0) return fail(DLI_ERR_INVALID_ARGUMENT, "matmul: bad sizes");
   if (!is_float_dtype(dtype)) return fail(DLI_ERR_INVALID_ARGUMENT, "matmul expects a float dtype");
   if (m == 0) return ok();
+  if (!a || !b || !out) return fail(DLI_ERR_INVALID_ARGUMENT, "matmul: null pointer");
+  if (dtype == DLI_DTYPE_F32) {
+    dli_status st = DLI_OK;
+    if (try_gemm_f32x3(a, b, nullptr, out, m, n, k, n, n, kEpiRowMajor, true, as_stream(stream), &st)) return st;
+  }
+  // bf16/f16 on tcgen05: A [M,K] K-major, B [K,N] MN-major through 64-column
+  // TMA panels (tile width >= 64). Other shapes/alignments take the SIMT kernel.
+  GemmPlan plan = plan_tn_gemm(m, n, k, dtype, true);
+  if (plan.tcgen05 && n % 8 == 0 && aligned(a, 16) && aligned(b, 16)) {
+    if (plan.bn < 64) {
+      plan = plan_tn_gemm(m, 64, k, dtype, true);  // the 64-wide plan, N columns masked by TMA/epilogue
+      plan.tiles_j = 1;
+    }
+    return run_tn_gemm_tcgen05(a, b, nullptr, out, m, n, k, k, n, n, kEpiRowMajor, 0, dtype, plan, nullptr, 0,
+                               as_stream(stream), false, false, 0, false, true);
+  }
   return run_gemm_simt(a, b, nullptr, out, m, n, k, false, dtype, as_stream(stream));
 }

@@ -123,16 +123,22 @@ for (b, s, hq, hkv, d, cap, pos) in [(2, 2048, 28, 4, 128, 2560, [0, 0]), (8, 51
     q, ck, cv, p = _cache_case(b, s, hq, hkv, d, cap, pos, torch.bfloat16, seed=1)
     out = C.attention_kvcache(q, ck, cv, p)
     assert_close(out.float(), torch_cache_attention(q, ck, cv, pos), torch.bfloat16, "strict")
+g = torch.Generator(device="cuda").manual_seed(5)
+q, k, v = (torch.randn(2, 6, n, 128, device="cuda", generator=g).bfloat16() for n in (200, 700, 700))
+ref = torch_cache_attention(q.permute(0, 2, 1, 3), k, v, [500, 500], causal=False)
+assert_close(C.attention(q, k, v, causal=False).float(), ref.permute(0, 2, 1, 3), torch.bfloat16, "strict dense")
 C.check_device_error()
 print("fmha strict ok")
 """
 
 
-def test_prefill_runs_on_tcgen05_kernel():
+@pytest.mark.parametrize("block_keys", ["128", "64"])
+def test_prefill_runs_on_tcgen05_kernel(block_keys):
     """DLI_SM100_ATTN_FMHA=2 turns a fallback to the mma.sync kernel into an
-    error, so these shapes provably ran on the tcgen05 kernel (knobs are read
-    once per process: run in a child)."""
-    env = dict(os.environ, DLI_SM100_ATTN_FMHA="2")
+    error, so these shapes provably ran on the tcgen05 kernel, with 128-key
+    blocks (one CTA per SM) and with 64-key blocks (two CTAs per SM); knobs are
+    read once per process, so each runs in a child."""
+    env = dict(os.environ, DLI_SM100_ATTN_FMHA="2", DLI_SM100_ATTN_FMHA_BN=block_keys)
     here = Path(__file__).resolve().parent
     env["PYTHONPATH"] = os.pathsep.join([str(here), str(here.parent), str(Path(C.__file__).resolve().parents[1]),
                                          env.get("PYTHONPATH", "")])

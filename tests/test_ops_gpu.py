@@ -213,6 +213,26 @@ def test_linear_fp32_split_k_shapes(m, n, k):
     assert torch.equal(y, y2)  # deterministic split-K reduction
 
 
+@pytest.mark.parametrize("m,n,k", [(64, 4096, 1024), (1, 4096, 4096), (128, 512, 2048), (600, 384, 1000)])
+def test_linear_fp32_tcgen05_split_accuracy(m, n, k):
+    """fp32 on tcgen05 through the three-term bf16 split (six bf16 products per
+    K step): the dropped terms sit near 2^-26 of each product, so the error is
+    that of an fp32 FFMA GEMM (3-9e-7 at these shapes), bound 2e-6 here, far
+    inside the 1e-4 fp32 tolerance; NaN inputs propagate."""
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(11 * m + n + k)
+    x = torch.randn(m, k, device="cuda", generator=g)
+    w = torch.randn(n, k, device="cuda", generator=g) * 0.02
+    b = torch.randn(n, device="cuda", generator=g) * 0.02
+    ref = torch.nn.functional.linear(x.double(), w.double(), b.double())
+    err = rel_err(C.linear(x, w, b).double().cpu(), ref.cpu())
+    assert err <= 2e-6, f"fp32 split GEMM {m}x{n}x{k}: relative error {err:.2e}"
+    x[0, k // 2] = float("nan")
+    y = C.linear(x, w, b)
+    assert torch.isnan(y[0]).all() and torch.isfinite(y[1:]).all()
+
+
 @pytest.mark.parametrize("m,n,k", [(70, 132, 52), (64, 4096, 1024), (33, 257, 4000), (5, 12, 3), (16, 512, 8192)])
 def test_matmul_fp32_shapes(m, n, k):
     import dli_sm100 as C
@@ -231,6 +251,29 @@ def test_matmul_bf16_and_f32():
         a = torch.randn(70, 130, device="cuda", generator=g).to(dtype)
         b = torch.randn(130, 50, device="cuda", generator=g).to(dtype)
         assert_close(C.matmul(a, b).float(), a.float() @ b.float(), dtype, f"matmul {dtype}")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k", [
+    (1, 4096, 1024),      # one row: tile width 64 + cluster split-K
+    (16, 24, 64),         # N < 64: one 64-wide tile, columns masked
+    (64, 4096, 1024),     # the single-linear workload as a matmul
+    (300, 1000, 520),     # ragged M, N not a multiple of 64, K not a multiple of 64
+    (512, 3584, 3584),    # 7B-width square-ish: tile width 256
+    (4096, 2048, 1024),   # many tiles: persistent double-buffered kernel
+])
+def test_matmul_tcgen05_shapes(m, n, k, dtype):
+    """bf16/f16 matmul with B [K, N] row-major (MN-major on the tensor core)
+    against an fp64 product of the same rounded inputs."""
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(m + 5 * n + 7 * k)
+    a = torch.randn(m, k, device="cuda", generator=g).to(dtype)
+    b = (torch.randn(k, n, device="cuda", generator=g) * 0.05).to(dtype)
+    y = C.matmul(a, b)
+    assert y.dtype == dtype
+    assert_close(y.float(), a.double() @ b.double(), dtype, f"matmul {dtype} {m}x{n}x{k}")
+    assert torch.equal(y, C.matmul(a, b))  # deterministic (cluster split-K reduces in rank order)
 
 
 ALEXNET_CONVS = [  # (C, H, OC) at k3 s1 p1
