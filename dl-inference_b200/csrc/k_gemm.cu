@@ -37,18 +37,56 @@ constexpr int kBK = 64;
 constexpr int kGemmThreads = 192;
 constexpr int kGroupI = 8;
 
+// kPush (tile widths <= 64, the decode tiles): split-K partials are pushed into a
+// dedicated receive buffer of the owning cluster rank (kRecvRows rows of BN + 4
+// floats: S ranks x R rows never exceed 128 + 2 * 7); wider tiles stage their
+// partial in the idle operand ring and pull.
 template <int BN, int STAGES>
 struct TcLayout {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = STAGES * kStageBytes;
-  static constexpr int kBytes = kBarOffset + (2 * STAGES + 1) * 8 + 16 + 1024;
+  static constexpr bool kPush = BN <= 64;
+  static constexpr int kRecvRows = kBM + 16;
+  static constexpr int kRecvOff = STAGES * kStageBytes;
+  static constexpr int kRecvBytes = kPush ? kRecvRows * (BN + 4) * 4 : 0;
+  static constexpr int kBarOffset = kRecvOff + kRecvBytes;
+  // full[STAGES], empty[STAGES], acc_full, red_full
+  static constexpr int kBytes = kBarOffset + (2 * STAGES + 2) * 8 + 16 + 1024;
   static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
   static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KiB alignment");
-  // the split-K partial tile [128][BN + 4] fp32 is staged in the idle operand ring
-  static_assert(kBM * (BN + 4) * 4 <= kBarOffset, "split-K staging must fit the operand ring");
+  // the pull reduction stages the partial tile [128][BN + 4] fp32 in the idle operand ring
+  static_assert(kBM * (BN + 4) * 4 <= STAGES * kStageBytes, "split-K staging must fit the operand ring");
 };
+
+// Owner of accumulator row `row` under a push reduction over S cluster ranks, and
+// its row index in the owner's receive slot. Row-per-rank layouts: rank r owns
+// rows [r*R, (r+1)*R), R = ceil(128/S). kEpiGluT: rank r owns gate rows
+// [r*Rg, (r+1)*Rg) of 0..63, Rg = ceil(64/S), and the matching up rows (+64),
+// stored after its Rg gate rows.
+__device__ __forceinline__ void push_owner(int epilogue, int S, int row, int& owner, int& lidx) {
+  if (epilogue == kEpiGluT) {
+    const int rg = (64 + S - 1) / S, g = row & 63;
+    owner = g / rg;
+    lidx = (g - owner * rg) + (row >> 6) * rg;
+  } else {
+    const int r = (kBM + S - 1) / S;
+    owner = row / r;
+    lidx = row - owner * r;
+  }
+}
+// Receive-slot height (rows per sender) and the rows this rank owns.
+__device__ __host__ __forceinline__ int push_slot_rows(int epilogue, int S) {
+  return epilogue == kEpiGluT ? 2 * ((64 + S - 1) / S) : (kBM + S - 1) / S;
+}
+__device__ __host__ __forceinline__ int push_my_rows(int epilogue, int S, int rank) {
+  if (epilogue == kEpiGluT) {
+    const int rg = (64 + S - 1) / S;
+    return 2 * max(0, min(rg, 64 - rank * rg));
+  }
+  const int r = (kBM + S - 1) / S;
+  return max(0, min(r, kBM - rank * r));
+}
 
 struct TcParams {
   int rows_a, rows_b;
@@ -359,6 +397,98 @@ __device__ __forceinline__ void tile_cluster_reduce(const TcParams& p, uint8_t* 
   cluster_sync();
 }
 
+// Split-K by push (epilogue warps 2-5): wait for the accumulator, then send each
+// accumulator row to the cluster rank that owns it, into slot `split` of that
+// rank's receive buffer, with st.async completing bytes on the owner's
+// red_full mbarrier (the own rank's rows are plain shared stores). Every rank
+// sends all of its rows, zeros after an abort, so no receiver waits for bytes
+// that never come. The owners' barriers were initialised before the
+// cluster-barrier arrival at kernel start; cluster_wait() makes that visible.
+template <typename T, int BN, int STAGES>
+__device__ __forceinline__ void tile_push_partial(const TcParams& p, uint8_t* smem, uint32_t tmem_base,
+                                                  uint64_t* acc_full, uint64_t* red_full, volatile int* flags,
+                                                  int split, int warp, int lane) {
+  using L = TcLayout<BN, STAGES>;
+  const int quarter = warp & 3;
+  const int row = quarter * 32 + lane;
+  const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+  if (!mbar_wait(acc_full, 0)) {
+    set_device_error(p.err, kDevErrGemmTimeout);
+    flags[0] = 1;
+  }
+  tc_fence_after();
+  epilogue_bar();  // every epilogue warp sees the same abort flag
+  const bool aborted = flags[0] != 0;
+  int owner, lidx;
+  push_owner(p.epilogue, p.splits, row, owner, lidx);
+  const int slot_rows = push_slot_rows(p.epilogue, p.splits);
+  const uint32_t dst_local = smem_u32(smem + L::kRecvOff) +
+                             static_cast<uint32_t>(((split * slot_rows + lidx) * (BN + 4)) * 4);
+  const uint32_t dst = mapa_shared(dst_local, static_cast<uint32_t>(owner));
+  const uint32_t bar = mapa_shared(smem_u32(red_full), static_cast<uint32_t>(owner));
+  cluster_wait();
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tbase + c, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int k = 0; k < 32 && c + k < BN; k += 4) {
+      const float4 v = aborted ? make_float4(0.f, 0.f, 0.f, 0.f)
+                               : make_float4(__uint_as_float(r[k]), __uint_as_float(r[k + 1]),
+                                             __uint_as_float(r[k + 2]), __uint_as_float(r[k + 3]));
+      if (owner == split)
+        *reinterpret_cast<float4*>(smem + L::kRecvOff + ((split * slot_rows + lidx) * (BN + 4) + c + k) * 4) = v;
+      else
+        st_async_f4(dst + static_cast<uint32_t>((c + k) * 4), v, bar);
+    }
+  }
+}
+
+// Split-K by push, all threads after a CTA barrier: wait until every peer's rows
+// arrived (bounded; longer than any sender's own bounded waits), then sum this
+// rank's rows over the S slots in rank order (deterministic) and store them.
+template <typename T, int BN, int STAGES>
+__device__ __forceinline__ void tile_push_reduce(const TcParams& p, uint8_t* smem, uint64_t* red_full, int ti, int tj,
+                                                 int split) {
+  using L = TcLayout<BN, STAGES>;
+  const int S = p.splits;
+  const int slot_rows = push_slot_rows(p.epilogue, S);
+  const int mine = push_my_rows(p.epilogue, S, split);
+  if (!mbar_wait(red_full, 0, 8000000000ull)) {
+    if (threadIdx.x == 0) set_device_error(p.err, kDevErrGemmTimeout);
+    return;
+  }
+  const float* recv = reinterpret_cast<const float*>(smem + L::kRecvOff);
+  if (p.epilogue == kEpiGluT) {
+    const int rg = mine / 2, rgs = slot_rows / 2;
+    const int quads = rg * (BN / 4);
+    for (int q = threadIdx.x; q < quads; q += kGemmThreads) {
+      const int lg = q % rg, cq = (q / rg) * 4;
+      float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int s2 = 0; s2 < S; ++s2) {
+        const float4 a = *reinterpret_cast<const float4*>(recv + (s2 * slot_rows + lg) * (BN + 4) + cq);
+        const float4 b = *reinterpret_cast<const float4*>(recv + (s2 * slot_rows + lg + rgs) * (BN + 4) + cq);
+        g[0] += a.x; g[1] += a.y; g[2] += a.z; g[3] += a.w;
+        u[0] += b.x; u[1] += b.y; u[2] += b.z; u[3] += b.w;
+      }
+      if (tj * BN + cq < p.rows_b) store_glu_t<T>(p, ti, split * rgs + lg, tj * BN + cq, g, u, 4);
+    }
+    return;
+  }
+  const int quads = mine * (BN / 4);
+  for (int q = threadIdx.x; q < quads; q += kGemmThreads) {
+    const int lr = q % mine, cq = (q / mine) * 4;  // consecutive threads: consecutive rows
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s2 = 0; s2 < S; ++s2) {
+      const float4 a = *reinterpret_cast<const float4*>(recv + (s2 * slot_rows + lr) * (BN + 4) + cq);
+      v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+    }
+    const int64_t gi = static_cast<int64_t>(ti) * kBM + split * slot_rows + lr;
+    if (tj * BN + cq < p.rows_b) store_vals<T>(p, gi, tj * BN + cq, v, 4);
+  }
+}
+
 template <typename T, int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tcgen05_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -370,11 +500,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* red_full = acc_full + 1;  // push split-K: the peers' rows have arrived
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_full + 1);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);  // [0] abort, [1] last split
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
+  const bool push = L::kPush && p.splits > 1;
   int ti, tj;
   tile_coords(tile, p.tiles_i, p.tiles_j, ti, tj);
   // K blocks are spread evenly over the splits (the plan keeps >= 1 per split).
@@ -387,6 +519,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
+    mbar_init(red_full, 1);
+    if (push)  // the peers' rows of this rank: (S - 1) senders x its rows x BN floats
+      mbar_arrive_expect_tx(red_full, static_cast<uint32_t>((p.splits - 1) *
+                                                            push_my_rows(p.epilogue, p.splits, split) * BN * 4));
     flags[0] = 0;
     mbar_fence_init();
   }
@@ -401,6 +537,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (push) cluster_arrive();  // this rank's receive barrier is ready for its peers
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
@@ -465,11 +602,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       umma_commit(acc_full);
     }
   } else {
-    tile_epilogue_warps<T, BN>(p, smem, tmem_base, acc_full, flags, ti, tj, warp, lane);
+    if (push) tile_push_partial<T, BN, STAGES>(p, smem, tmem_base, acc_full, red_full, flags, split, warp, lane);
+    else tile_epilogue_warps<T, BN>(p, smem, tmem_base, acc_full, flags, ti, tj, warp, lane);
   }
+  if (push && warp < 2) cluster_wait();  // pairs this thread's arrival at kernel start
   tc_fence_before();
   __syncthreads();
-  if (p.splits > 1) tile_cluster_reduce<T, BN>(p, smem, ti, tj, split);
+  if (push) tile_push_reduce<T, BN, STAGES>(p, smem, red_full, ti, tj, split);
+  else if (p.splits > 1) tile_cluster_reduce<T, BN>(p, smem, ti, tj, split);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -1503,8 +1643,8 @@ bool gemm_deep() {
 int stages_for(int bn) {
   if (bn >= 256) return 4;
   if (bn >= 128) return 6;
-  if (bn >= 64) return gemm_deep() ? 8 : 4;
-  return gemm_deep() ? 10 : 5;
+  if (bn >= 64) return gemm_deep() ? 7 : 3;
+  return gemm_deep() ? 10 : 4;
 }
 
 template <typename T, int BN, int STAGES>
@@ -1561,9 +1701,9 @@ dli_status launch_tc_bn(int bn, int stages, const CUtensorMap& ma, const CUtenso
                         const TcParams& p, int splits, cudaStream_t stream) {
   switch (bn) {
     case 32: return stages == 10 ? launch_tc<T, 32, 10>(ma, mb, p, splits, stream)
-                                 : launch_tc<T, 32, 5>(ma, mb, p, splits, stream);
-    case 64: return stages == 8 ? launch_tc<T, 64, 8>(ma, mb, p, splits, stream)
-                                : launch_tc<T, 64, 4>(ma, mb, p, splits, stream);
+                                 : launch_tc<T, 32, 4>(ma, mb, p, splits, stream);
+    case 64: return stages == 7 ? launch_tc<T, 64, 7>(ma, mb, p, splits, stream)
+                                : launch_tc<T, 64, 3>(ma, mb, p, splits, stream);
     case 128: return launch_tc<T, 128, 6>(ma, mb, p, splits, stream);
     case 256: return launch_tc<T, 256, 4>(ma, mb, p, splits, stream);
   }
@@ -1620,10 +1760,10 @@ int query_occupancy(int smem_bytes, int cluster) {
 
 int layout_bytes(int bn, int stages) {
   switch (bn * 100 + stages) {
-    case 3205: return TcLayout<32, 5>::kBytes;
+    case 3204: return TcLayout<32, 4>::kBytes;
     case 3210: return TcLayout<32, 10>::kBytes;
-    case 6404: return TcLayout<64, 4>::kBytes;
-    case 6408: return TcLayout<64, 8>::kBytes;
+    case 6403: return TcLayout<64, 3>::kBytes;
+    case 6407: return TcLayout<64, 7>::kBytes;
     case 12806: return TcLayout<128, 6>::kBytes;
     case 25604: return TcLayout<256, 4>::kBytes;
     // stages 0: the fp32 split-bf16 kernel's rings at that tile width

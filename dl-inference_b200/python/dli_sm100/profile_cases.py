@@ -27,6 +27,13 @@ def _gemm(m, n, k):
     return (lambda: C.linear(x, w)), 2 * (n * k + m * (n + k)), 2.0 * m * n * k
 
 
+def _gemm_f32(m, n, k):
+    x = torch.randn(m, k, device="cuda")
+    w = torch.randn(n, k, device="cuda") * 0.02
+    b = torch.randn(n, device="cuda") * 0.02
+    return (lambda: C.linear(x, w, b)), 4 * (n * k + m * (n + k) + n), 2.0 * m * n * k
+
+
 def _glu(m, inter, k):
     from dli_export.qwen2 import glu_blocked
 
@@ -57,12 +64,14 @@ def _attn_prefill(b=2, hq=28, hkv=4, d=128, s=2048):
 
 CASES = {
     "gemm_decode_gate_up": lambda: _gemm(32, 37888, 3584),
-    "gemm_decode_qkv": lambda: _gemm(32, 4608, 3584),
-    "gemm_decode_o": lambda: _gemm(32, 3584, 3584),
+    "gemm_decode_qkv": lambda: _gemm(32, 4608, 3584),   # 33 MB of weights: fits L2
+    "gemm_decode_o": lambda: _gemm(32, 3584, 3584),     # 26 MB: fits L2
     "gemm_decode_down": lambda: _gemm(32, 3584, 18944),
     "gemm_decode_lm_head": lambda: _gemm(32, 152064, 3584),
     "gemm_prefill_gate_up": lambda: _gemm(8192, 37888, 3584),
     "gemm_prefill_o": lambda: _gemm(8192, 3584, 3584),
+    "gemm_f32_linear": lambda: _gemm_f32(64, 4096, 1024),       # config 1 (16 MB weights: fits L2)
+    "gemm_f32_decode_qkv": lambda: _gemm_f32(32, 4608, 3584),   # fp32 7B qkv shape (66 MB: fits L2)
     "glu_decode_gate_up": lambda: _glu(32, 18944, 3584),
     "glu_prefill_gate_up": lambda: _glu(8192, 18944, 3584),
     "attn_decode": _attn_decode,

@@ -11,7 +11,8 @@ dynamic shared-memory limit raised above 48 KB where the kernel asks for more).
 Each case checks parity in both directions against the float64 oracle: this
 repository's kernel within its own tolerance, the reference kernel within a
 TF32 tolerance (its fp32 tl.dot runs as TF32), and times both with CUDA events
-(3 warm-up launches, 20 timed). The timings go to $DLI_REF_TIMING when set.
+over 20 launches captured in a CUDA graph (after 3 warm-up launches), so host
+launch costs are excluded on both sides. The timings go to $DLI_REF_TIMING.
 Skipped when the cubins were not built (no reference checkout at build time).
 """
 from __future__ import annotations
@@ -86,13 +87,21 @@ class RefKernel:
 
 
 def _time(fn, reps=20) -> float:
+    """Device time per launch: `reps` launches captured in one CUDA graph and
+    replayed, so neither side's host launch cost (ctypes, tensor-map encoding)
+    shows up in the figure."""
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(reps):
+            fn()
+    graph.replay()
+    torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for _ in range(reps):
-        fn()
+    graph.replay()
     b.record()
     torch.cuda.synchronize()
     return a.elapsed_time(b) / reps
@@ -168,7 +177,7 @@ def test_conv1_against_reference_kernel():
     xh, wh, bh = x.half(), w.half(), b.half()
     t_f16 = _time(lambda: C.conv2d(xh, wh, bh, (1, 1), (1, 1)))
     _report("conv1 64x3x32x32 -> 64 k3 fp32", reference_ms=t_ref, ours_ms=t_ours, ours_f16_ms=t_f16,
-            speedup=t_ref / t_ours)
+            reference_rel_err=_rel(y_ref, oracle), ours_rel_err=_rel(ours, oracle), speedup=t_ref / t_ours)
 
 
 @pytest.mark.parametrize("spec,bh,sq,sk", [
@@ -198,4 +207,4 @@ def test_attention_against_reference_kernel(spec, bh, sq, sk):
     qb, kb, vb = q.bfloat16(), k.bfloat16(), v.bfloat16()
     t_bf16 = _time(lambda: C.attention(qb, kb, vb, causal=True))
     _report(f"attention bh{bh} q{sq} k{sk} d128 fp32", reference_ms=t_ref, ours_ms=t_ours, ours_bf16_ms=t_bf16,
-            speedup=t_ref / t_ours)
+            reference_rel_err=_rel(o_ref, oracle), ours_rel_err=_rel(ours, oracle), speedup=t_ref / t_ours)
