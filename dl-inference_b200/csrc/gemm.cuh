@@ -57,6 +57,17 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
                                bool const_b, int64_t glu_cols = 0, bool out_f32 = false,
                                bool b_mn = false);
 
+// NCHW convolution geometry (every extent, and N*C*H*W and N*OC*OH*OW, below 2^31).
+struct ConvGeom {
+  int n, c, h, w, oc, kh, kw, sh, sw, ph, pw, oh, ow;
+};
+
+// Implicit-GEMM convolution on tcgen05 (bf16/f16): patch tiles gathered in shared
+// memory from the NCHW input, the weight as a K-major [OC, kp] operand (kp =
+// C*KH*KW rounded up to 8, zero columns past K), bias, NCHW output.
+dli_status run_conv_implicit_tcgen05(const void* x, const void* w_kmajor, int64_t kp, const void* bias, void* out,
+                                     const ConvGeom& g, dli_dtype dtype, cudaStream_t stream, bool const_w);
+
 // SIMT fallback (any float dtype, any alignment): out[M,N] = A[M,K] . B + bias,
 // with B given as [N,K] (b_kmajor) or [K,N].
 dli_status run_gemm_simt(const void* a, const void* b, const void* bias, void* out, int64_t m,

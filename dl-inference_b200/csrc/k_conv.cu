@@ -1,11 +1,13 @@
 // conv2d (NCHW, python/dli_ops/aot/conv2d/kernel.py:5-49 semantics: zero padding,
 // stride, optional bias).
 //
-// bf16/f16: implicit GEMM on the tcgen05 path. An im2col kernel writes the
-// patch matrix cols[M = N*OH*OW, Kp] (K = C*KH*KW rounded up to a multiple of 8
-// so TMA row strides stay 16-byte aligned) into the workspace; the weight
-// [OC, C, KH, KW] is already a K-major [OC, K] operand (repacked to Kp columns
-// when K % 8 != 0). The GEMM epilogue scatters D[m, oc] straight to NCHW.
+// bf16/f16: implicit GEMM on tcgen05 (run_conv_implicit_tcgen05): the patch
+// tiles are gathered into shared memory inside the GEMM, no patch matrix is
+// written. The weight [OC, C, KH, KW] is already a K-major [OC, K] operand,
+// repacked into the workspace with K rounded up to Kp, a multiple of 8 (TMA row
+// strides are 16-byte aligned), when K % 8 != 0. The epilogue scatters
+// D[m, oc] straight to NCHW. DLI_SM100_CONV_IMPLICIT=0 selects the older form:
+// an im2col kernel writes cols[M = N*OH*OW, Kp] and the plain GEMM reads it.
 // f32: 3x3 kernels run the tiled kernel below (shared-memory input patches and
 // weights, 16 output channels per thread); other sizes a direct convolution,
 // one output per thread. Both exact fp32 FMA.
@@ -165,16 +167,25 @@ inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 struct ConvWorkspace {
   size_t cols = 0, weight = 0, gemm = 0, total = 0;
   GemmPlan plan;
-  bool implicit = false;
+  bool tensor = false;  // a tcgen05 path serves the shape
+  bool gather = false;  // the implicit (gathering) kernel; else im2col + GEMM
 };
+
+bool conv_implicit_enabled() {
+  static const bool on = tuning_knob("CONV_IMPLICIT", 1) != 0;
+  return on;
+}
 
 ConvWorkspace conv_workspace(const ConvShape& s, dli_dtype dtype) {
   ConvWorkspace ws;
   if (dtype != DLI_DTYPE_BF16 && dtype != DLI_DTYPE_F16) return ws;
   ws.plan = plan_tn_gemm(s.m(), s.oc, s.kp(), dtype, true);
   if (!ws.plan.tcgen05) return ws;
-  ws.implicit = true;
-  ws.cols = align256(static_cast<size_t>(s.m() * s.kp()) * 2);
+  ws.tensor = true;
+  constexpr int64_t kIntMax = 0x7fffffff;
+  ws.gather = conv_implicit_enabled() && s.n * s.c * s.h * s.w <= kIntMax && s.m() * s.oc <= kIntMax &&
+              s.c * s.kh * s.kw <= kIntMax;
+  ws.cols = ws.gather ? 0 : align256(static_cast<size_t>(s.m() * s.kp()) * 2);
   ws.weight = s.kp() != s.k() ? align256(static_cast<size_t>(s.oc * s.kp()) * 2) : 0;
   ws.gemm = align256(ws.plan.workspace);
   ws.total = ws.cols + ws.weight + ws.gemm;
@@ -222,7 +233,28 @@ extern "C" dli_status dli_sm100_conv2d(const void* x, const void* weight, const 
   if (!x || !weight || !out) return fail(DLI_ERR_INVALID_ARGUMENT, "conv2d: null pointer");
   cudaStream_t cs = as_stream(stream);
   const ConvWorkspace ws = conv_workspace(s, dtype);
-  if (ws.implicit && s.m() * s.oc < (1ll << 31)) {
+  if (ws.tensor && ws.gather) {
+    if (ws.total > 0 && (workspace == nullptr || workspace_bytes < ws.total))
+      return fail(DLI_ERR_WORKSPACE, "conv2d: workspace too small (need " + std::to_string(ws.total) + " bytes)");
+    const void* wk = weight;
+    if (ws.weight) {
+      st = dispatch_float(dtype, "conv2d", [&](auto tag) {
+        using T = decltype(tag);
+        launch_pdl(pad_weight_kernel<T>, grid_for(s.oc * s.kp()), 256, 0, cs, (const T*)weight, (T*)workspace,
+                   s.oc, s.k(), s.kp());
+      });
+      if (st != DLI_OK) return st;
+      st = check_launch("conv2d weight repack");
+      if (st != DLI_OK) return st;
+      wk = workspace;
+    }
+    const ConvGeom g{static_cast<int>(s.n), static_cast<int>(s.c), static_cast<int>(s.h), static_cast<int>(s.w),
+                     static_cast<int>(s.oc), static_cast<int>(s.kh), static_cast<int>(s.kw), static_cast<int>(s.sh),
+                     static_cast<int>(s.sw), static_cast<int>(s.ph), static_cast<int>(s.pw), static_cast<int>(s.oh),
+                     static_cast<int>(s.ow)};
+    return run_conv_implicit_tcgen05(x, wk, s.kp(), bias, out, g, dtype, cs, ws.weight == 0);
+  }
+  if (ws.tensor && s.m() * s.oc < (1ll << 31)) {
     if (workspace == nullptr || workspace_bytes < ws.total)
       return fail(DLI_ERR_WORKSPACE, "conv2d: workspace too small (need " + std::to_string(ws.total) + " bytes)");
     uint8_t* base = static_cast<uint8_t*>(workspace);

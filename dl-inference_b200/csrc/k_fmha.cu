@@ -61,7 +61,7 @@ struct FmhaLayout {
   static constexpr int BN = BN_;  // keys per block
   static constexpr int kCtasPerSm = BN_ == 64 ? 2 : 1;
   static constexpr int KST = BN_ == 128 ? 3 : (D == 128 ? 2 : 3);
-  static constexpr int VST = BN_ == 128 ? (D == 128 ? 2 : 3) : (D == 128 ? 1 : 2);
+  static constexpr int VST = BN_ == 128 ? (D == 128 ? 2 : 3) : 2;
   static constexpr int kBox = 128 * 128;                   // one 128-row x 64-element box
   static constexpr int kQBytes = (D / 64) * kBox;
   static constexpr int kKVBytes = (D / 64) * BN * 128;     // one K or V block
@@ -74,7 +74,12 @@ struct FmhaLayout {
   // q_full, k_full[KST], k_empty[KST], v_full[VST], v_empty[VST], s_full[2],
   // s_empty[2], p_full, o_done, mma_done
   static constexpr int kBars = 1 + 2 * KST + 2 * VST + 4 + 3;
-  static constexpr int kBytes = kBarOff + kBars * 8 + 16 + 1024;
+  // One CTA per SM rounds its base up to 1 KiB inside the allocation; two CTAs
+  // per SM have no room for that slack and rely on the dynamic shared memory
+  // base being 1 KiB aligned, which the kernel checks (an error, never a
+  // misaligned swizzle atom).
+  static constexpr int kSlack = kCtasPerSm == 2 ? 0 : 1024;
+  static constexpr int kBytes = kBarOff + kBars * 8 + 16 + kSlack;
   static constexpr uint32_t kTmemCols = BN_ == 128 ? 512 : 256;
   static constexpr uint32_t kOCol = 2 * BN;  // S double buffer in columns [0, 2 BN), then O
   static_assert(BN_ == 64 || BN_ == 128, "key block of 64 or 128");
@@ -129,6 +134,10 @@ __global__ void __launch_bounds__(kFmhaThreads, FmhaLayout<D, BNK>::kCtasPerSm)
   constexpr int BM = L::BM, BN = L::BN, KST = L::KST, VST = L::VST;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
+  if (L::kSlack == 0 && (smem_u32(smem_raw) & 1023u) != 0) {
+    if (threadIdx.x == 0) set_device_error(p.err, kDevErrAttentionTimeout);
+    return;  // uniform for the whole CTA: nothing was started
+  }
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);

@@ -448,7 +448,7 @@ __device__ __forceinline__ void tile_push_partial(const TcParams& p, uint8_t* sm
 // Split-K by push, all threads after a CTA barrier: wait until every peer's rows
 // arrived (bounded; longer than any sender's own bounded waits), then sum this
 // rank's rows over the S slots in rank order (deterministic) and store them.
-template <typename T, int BN, int STAGES>
+template <typename T, int BN, int STAGES, int kThreads = kGemmThreads>
 __device__ __forceinline__ void tile_push_reduce(const TcParams& p, uint8_t* smem, uint64_t* red_full, int ti, int tj,
                                                  int split) {
   using L = TcLayout<BN, STAGES>;
@@ -463,7 +463,7 @@ __device__ __forceinline__ void tile_push_reduce(const TcParams& p, uint8_t* sme
   if (p.epilogue == kEpiGluT) {
     const int rg = mine / 2, rgs = slot_rows / 2;
     const int quads = rg * (BN / 4);
-    for (int q = threadIdx.x; q < quads; q += kGemmThreads) {
+    for (int q = threadIdx.x; q < quads; q += kThreads) {
       const int lg = q % rg, cq = (q / rg) * 4;
       float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
       for (int s2 = 0; s2 < S; ++s2) {
@@ -477,7 +477,7 @@ __device__ __forceinline__ void tile_push_reduce(const TcParams& p, uint8_t* sme
     return;
   }
   const int quads = mine * (BN / 4);
-  for (int q = threadIdx.x; q < quads; q += kGemmThreads) {
+  for (int q = threadIdx.x; q < quads; q += kThreads) {
     const int lr = q % mine, cq = (q / mine) * 4;  // consecutive threads: consecutive rows
     float v[4] = {0.f, 0.f, 0.f, 0.f};
     for (int s2 = 0; s2 < S; ++s2) {
@@ -610,6 +610,204 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (push) tile_push_reduce<T, BN, STAGES>(p, smem, red_full, ti, tj, split);
   else if (p.splits > 1) tile_cluster_reduce<T, BN>(p, smem, ti, tj, split);
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// ---- implicit-GEMM convolution on tcgen05 ---------------------------------------
+// D[m, oc] = sum_k patch[m, k] * W[oc, k] with m = (image, output pixel) and
+// k = (channel, ky, kx), the weight's own [OC, C, KH, KW] order. No patch
+// matrix is written: eight gather warps build each 128-pixel x 64-k A tile in
+// shared memory straight from the NCHW input (thread = one pixel row and one
+// half of the block's k values; the (channel, ky, kx) of each k comes from a
+// per-block table, so the 32 loads carry no branches and are all in flight at
+// once; zero outside the image and past K), 128B-swizzled like a TMA box,
+// while warp 0 streams the K-major weight tiles by TMA. MMA, split-K and the
+// NCHW epilogue (warps 2-5) are the GEMM kernel's.
+constexpr int kConvThreads = 320;
+constexpr int kConvGatherThreads = 256;
+
+template <typename T, int BN, int STAGES>
+__global__ void __launch_bounds__(kConvThreads, 1)
+    tcgen05_conv_kernel(const __grid_constant__ CUtensorMap tmap_b, const TcParams p, const T* __restrict__ x,
+                        const ConvGeom g) {
+  using L = TcLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);  // weight tile landed (TMA)
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* red_full = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_full + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // [STAGES] patch tile written: after the GEMM layout's barriers, slot and flags
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset + (2 * STAGES + 2) * 8 + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const bool push = L::kPush && p.splits > 1;
+  int ti, tj;
+  tile_coords(tile, p.tiles_i, p.tiles_j, ti, tj);
+  const int kb0 = static_cast<int>(static_cast<int64_t>(split) * p.kblocks / p.splits);
+  const int nkb = static_cast<int>(static_cast<int64_t>(split + 1) * p.kblocks / p.splits) - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&a_full[s], 8);  // one arrive per gather warp
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(red_full, 1);
+    if (push)
+      mbar_arrive_expect_tx(red_full, static_cast<uint32_t>((p.splits - 1) *
+                                                            push_my_rows(p.epilogue, p.splits, split) * BN * 4));
+    flags[0] = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tmap_b);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (push) cluster_arrive();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // the weights do not depend on the previous kernel: their first tiles load before the wait
+      const int pre = min(STAGES, nkb);
+      for (int it = 0; it < pre; ++it) {
+        mbar_arrive_expect_tx(&full[it], L::kBBytes);
+        tma_load_2d(smem + it * L::kStageBytes + L::kABytes, &tmap_b, (kb0 + it) * kBK, tj * BN, &full[it]);
+      }
+      pdl_wait();
+      pdl_trigger();
+      int issued = pre;
+      for (int it = pre; it < nkb; ++it) {
+        const int s = it % STAGES;
+        if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1) || flags[0]) {
+          set_device_error(p.err, kDevErrGemmTimeout);
+          flags[0] = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], L::kBBytes);
+        tma_load_2d(smem + s * L::kStageBytes + L::kABytes, &tmap_b, (kb0 + it) * kBK, tj * BN, &full[s]);
+        issued = it + 1;
+      }
+      for (int it = max(0, issued - STAGES); it < issued; ++it) mbar_wait(&full[it % STAGES], (it / STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, BN);
+      for (int it = 0; it < nkb; ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph) || !mbar_wait(&a_full[s], ph)) {
+          set_device_error(p.err, kDevErrGemmTimeout);
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + s * L::kStageBytes);
+        const uint64_t adesc = umma_desc_sw128(a_addr);
+        const uint64_t bdesc = umma_desc_sw128(a_addr + L::kABytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          umma_f16(tmem_base, adesc + 2 * kk, bdesc + 2 * kk, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(acc_full);
+    }
+  } else {
+    // gather warps 2-9: thread = one output pixel (A row) and one half of the k block
+    const int gtid = threadIdx.x - 64;
+    const int row = gtid & (kBM - 1), khalf = gtid >> 7;
+    const int64_t m = static_cast<int64_t>(ti) * kBM + row;
+    const int ohw = g.oh * g.ow, khw = g.kh * g.kw, hw = g.h * g.w;
+    const bool live = m < p.rows_a;
+    const int img = live ? static_cast<int>(m / ohw) : 0;
+    const int pix = live ? static_cast<int>(m - static_cast<int64_t>(img) * ohw) : 0;
+    const int iy0 = (pix / g.ow) * g.sh - g.ph, ix0 = (pix % g.ow) * g.sw - g.pw;
+    const unsigned short* xb = reinterpret_cast<const unsigned short*>(x) + static_cast<int64_t>(img) * g.c * hw;
+    const int pbase = iy0 * g.w + ix0;  // + (c*H + ky)*W + kx = the element's offset in the image
+    const int kdim = g.c * khw;
+    int2* ktable = reinterpret_cast<int2*>(a_full + STAGES);                  // [2][kBK]
+    volatile int* votes = reinterpret_cast<volatile int*>(ktable + 2 * kBK);  // [2][8]
+    pdl_wait();  // the input is the previous kernel's output
+    for (int it = 0; it < nkb; ++it) {
+      const int s = it % STAGES;
+      const bool w = mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1);
+      const int abort_seen = __shfl_sync(0xffffffffu, flags[0], 0);
+      const bool warp_ok = __all_sync(0xffffffffu, w) && !abort_seen;
+      // the (channel, ky, kx) of the block's 64 k values, shared by every pixel
+      // row. Table and votes are double-buffered, so one barrier per block
+      // suffices; every gather warp reaches it on every block (the waits above
+      // are bounded) and the votes make the abort decision the same in all.
+      int2* tbl = ktable + (it & 1) * kBK;
+      if (gtid < kBK) {
+        const int k = (kb0 + it) * kBK + gtid;
+        const int c = k / khw, r = k - c * khw, ky = r / g.kw, kx = r - ky * g.kw;
+        tbl[gtid] = k < kdim ? make_int2((c * g.h + ky) * g.w + kx, (ky << 16) | kx) : make_int2(-1, 0);
+      }
+      if (lane == 0) votes[(it & 1) * 8 + (warp - 2)] = warp_ok ? 1 : 0;
+      asm volatile("bar.sync 2, %0;" ::"n"(kConvGatherThreads) : "memory");
+      volatile const int* vt = votes + (it & 1) * 8;
+      bool all_ok = true;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) all_ok = all_ok && vt[i] != 0;
+      if (!all_ok) {
+        if (lane == 0) {
+          set_device_error(p.err, kDevErrGemmTimeout);
+          flags[0] = 1;
+        }
+        break;
+      }
+      uint32_t v[kBK / 4];
+#pragma unroll
+      for (int e = 0; e < kBK / 2; e += 2) {
+        uint32_t pair = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int2 t = tbl[khalf * (kBK / 2) + e + h];
+          const int iy = iy0 + (t.y >> 16), ix = ix0 + (t.y & 0xffff);
+          const bool ok = live && t.x >= 0 && static_cast<unsigned>(iy) < static_cast<unsigned>(g.h) &&
+                          static_cast<unsigned>(ix) < static_cast<unsigned>(g.w);
+          // unconditional load (element 0 of the image when outside it), then a
+          // select: no branch between the loads, so all are in flight at once
+          const uint32_t raw = __ldg(xb + (ok ? pbase + t.x : 0));
+          pair |= (ok ? raw : 0u) << (16 * h);
+        }
+        v[e >> 1] = pair;
+      }
+      uint8_t* a_tile = smem + s * L::kStageBytes + row * 128;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int chunk = khalf * 4 + q;
+        *reinterpret_cast<uint4*>(a_tile + ((chunk ^ (row & 7)) << 4)) =
+            make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      }
+      fence_proxy_async_smem();  // read by the tensor core (async proxy)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[s]);
+    }
+    if (warp < 6) {  // the epilogue runs on warps 2-5 (one TMEM lane quarter each)
+      if (push) tile_push_partial<T, BN, STAGES>(p, smem, tmem_base, acc_full, red_full, flags, split, warp, lane);
+      else tile_epilogue_warps<T, BN>(p, smem, tmem_base, acc_full, flags, ti, tj, warp, lane);
+    }
+  }
+  if (push && (warp < 2 || warp >= 6)) cluster_wait();  // the threads that push nothing
+  tc_fence_before();
+  __syncthreads();
+  if (push) tile_push_reduce<T, BN, STAGES, kConvThreads>(p, smem, red_full, ti, tj, split);
+  else if (p.splits > 1) tile_cluster_reduce<T, BN, kConvThreads>(p, smem, ti, tj, split);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -1927,6 +2125,34 @@ dli_status run_tn_gemm_tcgen05(const void* a, const void* b, const void* bias, v
   return launch_tc_bn<__half>(plan.bn, plan.stages, ma, mb, p, plan.splits, stream);
 }
 
+template <typename T, int BN, int STAGES>
+dli_status launch_conv(const CUtensorMap& mb, const TcParams& p, const void* x, const ConvGeom& g, int splits,
+                       cudaStream_t stream) {
+  using L = TcLayout<BN, STAGES>;
+  constexpr int kBytes = L::kBytes + STAGES * 8 + 2 * kBK * 8 + 64;  // + patch barriers, k tables, votes
+  auto kernel = tcgen05_conv_kernel<T, BN, STAGES>;
+  const dli_status st = ensure_smem(reinterpret_cast<const void*>(kernel), kBytes, "tcgen05 conv");
+  if (st != DLI_OK) return st;
+  dim3 grid(static_cast<unsigned>(p.tiles_i * p.tiles_j), static_cast<unsigned>(splits));
+  launch_pdl_cluster(kernel, grid, dim3(kConvThreads), kBytes, stream, static_cast<unsigned>(splits), mb, p,
+                     static_cast<const T*>(x), g);
+  return check_launch("tcgen05 conv");
+}
+
+template <typename T>
+dli_status launch_conv_bn(int bn, int stages, const CUtensorMap& mb, const TcParams& p, const void* x,
+                          const ConvGeom& g, int splits, cudaStream_t stream) {
+  switch (bn) {
+    case 32: return stages == 10 ? launch_conv<T, 32, 10>(mb, p, x, g, splits, stream)
+                                 : launch_conv<T, 32, 4>(mb, p, x, g, splits, stream);
+    case 64: return stages == 7 ? launch_conv<T, 64, 7>(mb, p, x, g, splits, stream)
+                                : launch_conv<T, 64, 3>(mb, p, x, g, splits, stream);
+    case 128: return launch_conv<T, 128, 6>(mb, p, x, g, splits, stream);
+    case 256: return launch_conv<T, 256, 4>(mb, p, x, g, splits, stream);
+  }
+  return fail(DLI_ERR_UNSUPPORTED, "conv: unsupported tile width");
+}
+
 // fp32 2-D map over [outer, inner] (row stride `ld` floats), 128B-swizzled
 // boxes of 32 x box_outer: K-major operands (inner = K) and MN-major B (inner = N).
 dli_status make_f32_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t ld,
@@ -1956,6 +2182,36 @@ dli_status launch_f32x3(const CUtensorMap& ma, const CUtensorMap& mb, const TcPa
   launch_pdl_cluster(kernel, grid, dim3(kF32SplitThreads), L::kBytes, stream, static_cast<unsigned>(splits), ma, mb,
                      p);
   return check_launch("fp32 tcgen05 gemm");
+}
+
+dli_status run_conv_implicit_tcgen05(const void* x, const void* w_kmajor, int64_t kp, const void* bias, void* out,
+                                     const ConvGeom& g, dli_dtype dtype, cudaStream_t stream, bool const_w) {
+  const bool bf16 = dtype == DLI_DTYPE_BF16;
+  if (!bf16 && dtype != DLI_DTYPE_F16) return fail(DLI_ERR_UNSUPPORTED, "conv: bfloat16/float16 only");
+  const int64_t m = static_cast<int64_t>(g.n) * g.oh * g.ow;
+  const GemmPlan plan = plan_tn_gemm(m, g.oc, kp, dtype, true);
+  if (!plan.tcgen05 || kp % 8 != 0 || !aligned(w_kmajor, 16))
+    return fail(DLI_ERR_UNSUPPORTED, "conv: shape not served by the implicit tcgen05 path");
+  CUtensorMap mb;
+  dli_status st = make_kmajor_map(&mb, w_kmajor, g.oc, kp, kp, plan.bn, bf16);
+  if (st != DLI_OK) return st;
+  TcParams p{};
+  p.rows_a = static_cast<int>(m);
+  p.rows_b = g.oc;
+  p.tiles_i = plan.tiles_i;
+  p.tiles_j = plan.tiles_j;
+  p.kblocks = plan.kblocks;
+  p.splits = plan.splits;
+  p.epilogue = kEpiNchw;
+  p.ldo = 0;
+  p.ohw = static_cast<int64_t>(g.oh) * g.ow;
+  p.out_vec = 0;
+  p.bias = bias;
+  p.out = out;
+  p.err = device_error_word();
+  p.const_b = const_w ? 1 : 0;
+  return bf16 ? launch_conv_bn<__nv_bfloat16>(plan.bn, plan.stages, mb, p, x, g, plan.splits, stream)
+              : launch_conv_bn<__half>(plan.bn, plan.stages, mb, p, x, g, plan.splits, stream);
 }
 
 // fp32 D = A * B^T (+ bias) on tcgen05 through the three-term bf16 split: A [rows_a,

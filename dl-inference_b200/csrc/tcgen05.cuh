@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the Blackwell (sm_100a) primitives the kernels
-// use: mbarriers with bounded waits, TMA tiled loads (no multicast), tcgen05
+// use: mbarriers with bounded waits, TMA tiled loads (each CTA its own tiles), tcgen05
 // MMA/commit/TMEM alloc/ld, and the UMMA shared-memory/instruction descriptors.
 // Descriptor bit layouts follow the PTX ISA "tcgen05 matrix descriptors" and
 // "instruction descriptor" tables (kind::f16).
