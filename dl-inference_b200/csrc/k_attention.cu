@@ -1193,6 +1193,251 @@ dli_status launch_attn_f32(const AttnArgs& args, cudaStream_t stream) {
   return check_launch("attention fp32");
 }
 
+// ---- fp32 decode: few query rows per KV head ---------------------------------------
+// CTA = (key split, KV head, sequence), 4 warps, each walking its own contiguous
+// range of 32-key chunks for all R = seq_q * group (<= 8) query rows of the KV
+// head at once: lane j scores key j from its own K row (D/4 independent 16-byte
+// loads in flight) against the rows in shared memory, the online softmax runs
+// per row across the warp, and for O += P V each lane owns D/32 columns of the
+// key's V row (one coalesced 16-byte load per key). The four warps merge their
+// (m, l, O) through shared memory, and the key splits of one (sequence, KV
+// head) merge through distributed shared memory in rank order: exact fp32,
+// deterministic, no workspace.
+constexpr int kF32DecWarps = 4;
+
+template <int D, int R>
+__global__ void __launch_bounds__(128) attn_f32_decode_kernel(const AttnArgs a, int rows) {
+  DLI_PDL_ENTRY();
+  constexpr int DL = D / 32;
+  __shared__ __align__(16) float sq[R][D];                  // query rows, pre-scaled by scale*log2(e)
+  __shared__ __align__(16) float so[kF32DecWarps][R][D];    // per-warp O
+  __shared__ float sm[kF32DecWarps][R], sl[kF32DecWarps][R];
+  __shared__ __align__(16) float co[R][D];                  // this CTA's merged O (split merge source)
+  __shared__ float cml[2][R];                               // its m and l
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, splits = gridDim.x;
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int kv_len = kv_len_of(a, b);
+  const int off = kv_len - a.seq_q;
+  // row r = query position r / group, query head kvh * group + r % group
+  for (int i = threadIdx.x; i < R * D; i += 128) {
+    const int r = i / D, d = i - (i / D) * D;
+    float v = 0.f;
+    if (r < rows) {
+      const int sqp = r / a.group, h = kvh * a.group + r % a.group;
+      v = static_cast<const float*>(a.q)[b * a.q_sb + h * a.q_sh + static_cast<int64_t>(sqp) * a.q_ss + d] *
+          a.scale_log2;
+    }
+    sq[r][d] = v;
+  }
+  __syncthreads();
+  const float* kbase = static_cast<const float*>(a.k) + b * a.k_sb + kvh * a.k_sh;
+  const float* vbase = static_cast<const float*>(a.v) + b * a.k_sb + kvh * a.k_sh;
+  const int n_end = max(min(kv_len, a.seq_k), 0);  // never past the cache rows
+  const int nchunks = (n_end + 31) / 32;
+  const int c0 = static_cast<int>(static_cast<int64_t>(split) * nchunks / splits);
+  const int c1 = static_cast<int>(static_cast<int64_t>(split + 1) * nchunks / splits);
+  const int w0 = c0 + (c1 - c0) * warp / kF32DecWarps, w1 = c0 + (c1 - c0) * (warp + 1) / kF32DecWarps;
+  int lim[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int sqp = r / a.group;
+    lim[r] = r < rows ? min(a.causal ? min(kv_len, sqp + off + 1) : kv_len, n_end) : 0;
+  }
+  float m[R], l[R], o[R][DL];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+#pragma unroll
+    for (int c = 0; c < DL; ++c) o[r][c] = 0.f;
+  }
+  for (int ch = w0; ch < w1; ++ch) {
+    const int key = ch * 32 + lane;
+    const float* kr = kbase + static_cast<int64_t>(key < n_end ? key : 0) * D;
+    float sc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) sc[r] = 0.f;
+#pragma unroll 8
+    for (int d = 0; d < D; d += 4) {
+      const float4 kv = __ldg(reinterpret_cast<const float4*>(kr + d));
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float4 qv = *reinterpret_cast<const float4*>(&sq[r][d]);
+        sc[r] = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, fmaf(qv.w, kv.w, sc[r]))));
+      }
+    }
+    float pr[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float v = key < lim[r] ? sc[r] : -INFINITY;
+      const float mnew = fmaxf(m[r], warp_max(v));
+      const float alpha = mnew == -INFINITY ? 1.f : exp2f(m[r] - mnew);
+      pr[r] = mnew == -INFINITY ? 0.f : exp2f(v - mnew);
+      l[r] = l[r] * alpha + warp_sum(pr[r]);
+      m[r] = mnew;
+#pragma unroll
+      for (int c = 0; c < DL; ++c) o[r][c] *= alpha;
+    }
+    const int nk = min(32, n_end - ch * 32);
+    for (int j = 0; j < nk; ++j) {
+      const float* vr = vbase + static_cast<int64_t>(ch * 32 + j) * D + lane * DL;
+      float vv[DL];
+      if constexpr (DL == 4) {
+        const float4 x = __ldg(reinterpret_cast<const float4*>(vr));
+        vv[0] = x.x; vv[1] = x.y; vv[2] = x.z; vv[3] = x.w;
+      } else {
+        const float2 x = __ldg(reinterpret_cast<const float2*>(vr));
+        vv[0] = x.x; vv[1] = x.y;
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float pj = __shfl_sync(0xffffffffu, pr[r], j);
+#pragma unroll
+        for (int c = 0; c < DL; ++c) o[r][c] = fmaf(pj, vv[c], o[r][c]);
+      }
+    }
+  }
+  // merge the four warps (in warp order) into this CTA's (m, l, O)
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+#pragma unroll
+    for (int c = 0; c < DL; ++c) so[warp][r][lane * DL + c] = o[r][c];
+    if (lane == 0) {
+      sm[warp][r] = m[r];
+      sl[warp][r] = l[r];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < R * D; i += 128) {
+    const int r = i / D, d = i - (i / D) * D;
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kF32DecWarps; ++w) mm = fmaxf(mm, sm[w][r]);
+    float acc = 0.f, ll = 0.f;
+#pragma unroll
+    for (int w = 0; w < kF32DecWarps; ++w) {
+      const float wt = sm[w][r] == -INFINITY ? 0.f : exp2f(sm[w][r] - mm);
+      acc += so[w][r][d] * wt;
+      ll += sl[w][r] * wt;
+    }
+    co[r][d] = acc;
+    if (d == 0) {
+      cml[0][r] = mm;
+      cml[1][r] = ll;
+    }
+  }
+  auto store = [&](int r, int d, float val) {
+    if (r >= rows) return;
+    const int sqp = r / a.group, h = kvh * a.group + r % a.group;
+    static_cast<float*>(a.out)[b * a.o_sb + h * a.o_sh + static_cast<int64_t>(sqp) * a.o_ss + d] = val;
+  };
+  if (splits == 1) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < R * D; i += 128) {
+      const int r = i / D, d = i - (i / D) * D;
+      store(r, d, cml[1][r] > 0.f ? co[r][d] / cml[1][r] : 0.f);
+    }
+    return;
+  }
+  // split-KV: merge the cluster's ranks in rank order; rank s writes elements s, s + S, ...
+  cluster_sync();
+  const uint32_t co_l = static_cast<uint32_t>(__cvta_generic_to_shared(&co[0][0]));
+  const uint32_t ml_l = static_cast<uint32_t>(__cvta_generic_to_shared(&cml[0][0]));
+  for (int i = split * 128 + threadIdx.x; i < R * D; i += splits * 128) {
+    const int r = i / D, d = i - (i / D) * D;
+    float ms[8], ls[8], os[8];
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2) {
+      if (s2 < splits) {
+        asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                     : "=f"(ms[s2]) : "r"(mapa_shared(ml_l + r * 4, s2)) : "memory");
+        asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                     : "=f"(ls[s2]) : "r"(mapa_shared(ml_l + (R + r) * 4, s2)) : "memory");
+        asm volatile("ld.shared::cluster.f32 %0, [%1];"
+                     : "=f"(os[s2]) : "r"(mapa_shared(co_l + (r * D + d) * 4, s2)) : "memory");
+      }
+    }
+    float mm = -INFINITY;
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2)
+      if (s2 < splits) mm = fmaxf(mm, ms[s2]);
+    float acc = 0.f, ll = 0.f;
+#pragma unroll
+    for (int s2 = 0; s2 < 8; ++s2) {
+      if (s2 < splits) {
+        const float wt = ms[s2] == -INFINITY ? 0.f : exp2f(ms[s2] - mm);
+        acc += os[s2] * wt;
+        ll += ls[s2] * wt;
+      }
+    }
+    store(r, d, ll > 0.f ? acc / ll : 0.f);
+  }
+  cluster_sync();  // every rank's shared memory stays alive until all reads are done
+}
+
+template <int D, int R>
+dli_status launch_attn_f32_decode(const AttnArgs& args, int rows, cudaStream_t stream) {
+  const int64_t heads = static_cast<int64_t>(args.batch) * args.hkv;
+  const int64_t keys = args.seq_k;  // the cache rows (or the dense key count) bound every sequence
+  const int64_t nchunks = ceil_div(std::max<int64_t>(keys, 1), 32);
+  // enough CTAs for four per SM, each warp keeping >= 2 chunks of 32 keys
+  int splits = static_cast<int>(std::min<int64_t>(8, std::max<int64_t>(1, ceil_div(4 * sm_count(), heads))));
+  splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(splits, nchunks / (2 * kF32DecWarps))));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(splits), static_cast<unsigned>(args.hkv), static_cast<unsigned>(args.batch));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (splits > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  cudaLaunchKernelEx(&cfg, attn_f32_decode_kernel<D, R>, args, rows);
+  return check_launch("attention fp32 decode");
+}
+
+// The fp32 decode kernel serves <= 8 query rows per KV head, head_dim 64/128,
+// 16-byte aligned K/V rows (DLI_SM100_ATTN_F32_DECODE=0 sends them to the tile kernel).
+bool f32_decode_ok(const AttnArgs& a) {
+  static const bool on = tuning_knob("ATTN_F32_DECODE", 1) != 0;
+  const int64_t rows = static_cast<int64_t>(a.seq_q) * a.group;
+  if (!on || rows < 1 || rows > 8 || (a.head_dim != 64 && a.head_dim != 128)) return false;
+  if (a.batch > 65535 || a.hkv > 65535 || !aligned(a.k, 16) || !aligned(a.v, 16)) return false;
+  return a.k_sb % 4 == 0 && a.k_sh % 4 == 0;
+}
+
+dli_status run_attn_f32_decode(const AttnArgs& a, cudaStream_t stream) {
+  const int rows = a.seq_q * a.group;
+  const int r = rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : 8;
+  if (a.head_dim == 64) {
+    switch (r) {
+      case 1: return launch_attn_f32_decode<64, 1>(a, rows, stream);
+      case 2: return launch_attn_f32_decode<64, 2>(a, rows, stream);
+      case 4: return launch_attn_f32_decode<64, 4>(a, rows, stream);
+      default: return launch_attn_f32_decode<64, 8>(a, rows, stream);
+    }
+  }
+  switch (r) {
+    case 1: return launch_attn_f32_decode<128, 1>(a, rows, stream);
+    case 2: return launch_attn_f32_decode<128, 2>(a, rows, stream);
+    case 4: return launch_attn_f32_decode<128, 4>(a, rows, stream);
+    default: return launch_attn_f32_decode<128, 8>(a, rows, stream);
+  }
+}
+
 bool f32_attention_ok(const AttnArgs& a) {
   static const bool on = tuning_knob("ATTN_F32", 1) != 0;
   if (!on || (a.head_dim != 64 && a.head_dim != 128)) return false;
@@ -1424,6 +1669,7 @@ dli_status run_attention(AttnArgs& args, dli_dtype dtype, int64_t max_kv, void* 
     return args.head_dim == 64 ? launch_tc_attention<__half, 64>(args, plan, stream)
                                : launch_tc_attention<__half, 128>(args, plan, stream);
   }
+  if (dtype == DLI_DTYPE_F32 && f32_decode_ok(args)) return run_attn_f32_decode(args, stream);
   if (dtype == DLI_DTYPE_F32 && f32_attention_ok(args))
     return args.head_dim == 64 ? launch_attn_f32<64>(args, stream) : launch_attn_f32<128>(args, stream);
   if (args.head_dim > 256) return fail(DLI_ERR_UNSUPPORTED, "attention: head_dim > 256");

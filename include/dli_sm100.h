@@ -113,7 +113,10 @@ dli_status dli_sm100_matmul(const void* a, const void* b, void* out, int64_t m, 
 /* conv2d (NCHW): out[N,OC,OH,OW] = conv(x[N,C,H,W], w[OC,C,KH,KW]) + bias[OC].
  * OH = (H + 2*pad_h - KH)/stride_h + 1 (python/dli_ops/aot/conv2d/template.cc:13-14).
  * Replaces python/dli_ops/aot/conv2d/kernel.py:5-49. BF16/F16 run as an implicit
- * GEMM (im2col into the workspace + tcgen05 GEMM writing NCHW); F32 runs direct. */
+ * GEMM on tcgen05: patch tiles are gathered into shared memory inside the GEMM,
+ * no patch matrix is written; the workspace holds only a copy of the weight
+ * padded to a multiple of 8 columns when C*KH*KW is not one (else 0 bytes).
+ * F32 3x3 runs a tiled CUDA-core kernel, other F32 shapes a direct one. */
 size_t dli_sm100_conv2d_workspace_size(int64_t n, int64_t c, int64_t h, int64_t w, int64_t oc,
                                        int64_t kh, int64_t kw, int64_t stride_h, int64_t stride_w,
                                        int64_t pad_h, int64_t pad_w, dli_dtype dtype);

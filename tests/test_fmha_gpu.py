@@ -144,3 +144,24 @@ def test_prefill_runs_on_tcgen05_kernel(block_keys):
                                          env.get("PYTHONPATH", "")])
     res = subprocess.run([sys.executable, "-c", _STRICT], env=env, capture_output=True, text=True, timeout=600)
     assert res.returncode == 0 and "fmha strict ok" in res.stdout, (res.stdout[-2000:], res.stderr[-3000:])
+
+
+@pytest.mark.parametrize("b,s,hq,hkv,d,cap,positions", [
+    (4, 1, 8, 8, 128, 2048, [2047, 100, 0, 1500]),   # MHA decode, ragged contexts (one of 1 key)
+    (3, 1, 28, 4, 128, 700, [699, 64, 333]),         # 7B heads: 7 query rows per KV head
+    (2, 1, 64, 8, 128, 300, [299, 31]),              # 72B group: 8 rows
+    (2, 2, 14, 2, 64, 600, [500, 5]),                # two tokens at group 7: 14 rows -> the tile kernel
+    (1, 4, 2, 1, 64, 4096, [4000]),                  # 8 rows from 4 positions x group 2, long context
+    (96, 1, 1, 1, 128, 256, list(range(0, 192, 2))),  # many heads, a few keys each
+])
+def test_f32_decode_attention_against_fp32_reference(b, s, hq, hkv, d, cap, positions):
+    """fp32 attention over the KV cache with few query rows per KV head (the
+    decode kernel: one warp per key range, merged across warps and a cluster),
+    against a PyTorch fp32 reference at the fp32 tolerance. Cache rows past each
+    sequence hold NaN and must not reach the output."""
+    q, ck, cv, pos = _cache_case(b, s, hq, hkv, d, cap, positions, torch.float32, seed=b + s + hq, nan_tail=True)
+    out = C.attention_kvcache(q, ck, cv, pos)
+    C.check_device_error()
+    assert torch.isfinite(out).all()
+    assert_close(out, torch_cache_attention(q, ck, cv, positions), torch.float32, "fp32 decode attention")
+    assert torch.equal(out, C.attention_kvcache(q, ck, cv, pos))  # deterministic merge
