@@ -14,6 +14,10 @@ enum GemmEpilogue : int {
   // 64b.., rows 128b+64.. = the matching up rows): out = silu(gate) * up, I cols
   kEpiGluT = 3,       // swap-AB: D row i = weight row -> out[j * ldo + (i/128)*64 + i%64]
   kEpiGlu = 4,        // D column j = weight row -> out[i * ldo + (j/128)*64 + j%64]
+  // swap-AB, split-K push plans only: D row i = output feature, column j = token;
+  // the rows, rounded to T, go as epoch-tagged words into every tensor-parallel
+  // rank's exchange buffer (row j, feature pairs i, i+1 per word), not to `out`
+  kEpiExchange = 5,
 };
 
 struct GemmPlan {

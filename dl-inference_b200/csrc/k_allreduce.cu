@@ -32,13 +32,12 @@
 #include <algorithm>
 #include <type_traits>
 
-#include "common.cuh"
+#include "exchange.cuh"
 
 namespace dli_sm100 {
 namespace {
 
-constexpr int kMaxRanks = 8;
-constexpr int64_t kHeaderAlign = 4096;
+constexpr int kMaxRanks = kExchangeMaxRanks;
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;
 
 struct ExchangeParams {
@@ -53,9 +52,7 @@ struct ExchangeParams {
   unsigned* err;
 };
 
-__host__ __device__ inline int64_t header_bytes(int64_t max_rows) {
-  return (2 * max_rows * 4 + kHeaderAlign - 1) / kHeaderAlign * kHeaderAlign;
-}
+__host__ __device__ inline int64_t header_bytes(int64_t max_rows) { return exchange_header_bytes(max_rows); }
 
 __device__ __forceinline__ uint64_t timer_ns() {
   uint64_t t;
@@ -73,8 +70,7 @@ __device__ __forceinline__ void ld_ll2(const uint64_t* p, uint64_t& a, uint64_t&
 }
 
 __device__ __forceinline__ uint64_t* row_words(char* base, const ExchangeParams& p, int slot, int src, int64_t row) {
-  uint64_t* w = reinterpret_cast<uint64_t*>(base + header_bytes(p.max_rows));
-  return w + ((static_cast<int64_t>(slot) * p.tp + src) * p.max_rows + row) * p.row_words;
+  return exchange_row_words(base, p.max_rows, p.row_words, p.tp, slot, src, row);
 }
 
 // (value, id) candidate words of the argmax exchange, after the row words.
@@ -150,7 +146,11 @@ __device__ __forceinline__ void store_res(R* ptr, const float (&f)[Vec16<T>::N])
   }
 }
 
-template <typename T, typename R, int kVpt>
+// kPushed: the row-split GEMM already stored every rank's partial rows (its own
+// included) into the group's buffers at this call's epoch (dli_sm100_linear_
+// exchange_push); `delta` is unused and every source is read from this rank's
+// buffer.
+template <typename T, typename R, int kVpt, bool kPushed = false>
 __global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
     ExchangeParams p, const T* __restrict__ delta, const R* residual /* may alias residual_out */,
     const T* __restrict__ w, T* __restrict__ normed, R* residual_out) {
@@ -175,9 +175,9 @@ __global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
 #pragma unroll
   for (int i = 0; i < kVpt; ++i) {
     const int64_t c = threadIdx.x + static_cast<int64_t>(i) * blockDim.x;
-    if (c < lanes) own[i] = load16(delta + off + c * V);
+    if (!kPushed && c < lanes) own[i] = load16(delta + off + c * V);
   }
-  for (int q = 0; q < p.tp; ++q) {
+  for (int q = 0; q < (kPushed ? 0 : p.tp); ++q) {
     if (q == rank) continue;
     uint64_t* dst = row_words(p.buf[q], p, slot, rank, r);
 #pragma unroll
@@ -198,7 +198,7 @@ __global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
     for (int j = 0; j < V; ++j) acc[i][j] = 0.f;
   bool failed = false;
   for (int src = 0; src < p.tp; ++src) {
-    if (src == rank) {
+    if (src == rank && !kPushed) {
 #pragma unroll
       for (int i = 0; i < kVpt; ++i)
 #pragma unroll
@@ -368,12 +368,16 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm(
                                              timeout_ns, dtype, dtype, stream);
 }
 
-extern "C" dli_status dli_sm100_allreduce_add_rms_norm_ex(
-    void* const* buffers, int tp, int rank, int ranks_in_launch, int64_t max_rows, int64_t row_elems,
-    const void* delta, const void* residual, const void* w, void* normed, void* residual_out,
-    int64_t rank_stride, int64_t rows, int64_t hidden, float eps, int64_t timeout_ns, dli_dtype dtype,
-    dli_dtype residual_dtype, void* stream) {
-  const char* name = "allreduce_add_rms_norm";
+namespace {
+// The all-reduce + residual add + RMSNorm launch; `pushed`: the partial rows are
+// already in the buffers (delta unused).
+dli_status run_allreduce_norm(void* const* buffers, int tp, int rank, int ranks_in_launch, int64_t max_rows,
+                              int64_t row_elems, const void* delta, const void* residual, const void* w, void* normed,
+                              void* residual_out, int64_t rank_stride, int64_t rows, int64_t hidden, float eps,
+                              int64_t timeout_ns, dli_dtype dtype, dli_dtype residual_dtype, bool pushed,
+                              void* stream) {
+  const char* name = pushed ? "exchange_add_rms_norm" : "allreduce_add_rms_norm";
+  if (pushed) delta = residual;  // unused: keeps the null-pointer check below meaningful
   const bool res32 = residual_dtype != dtype;
   if (res32 && (residual_dtype != DLI_DTYPE_F32 || (dtype != DLI_DTYPE_BF16 && dtype != DLI_DTYPE_F16)))
     return fail(DLI_ERR_INVALID_ARGUMENT, std::string(name) + ": a float32 residual needs bfloat16/float16 tensors");
@@ -447,8 +451,12 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm_ex(
   auto go = [&](auto ttag, auto rtag) {
     using T = decltype(ttag);
     using R = decltype(rtag);
-    auto kern = vpt == 1 ? allreduce_add_rms_norm_kernel<T, R, 1>
-                         : (vpt == 2 ? allreduce_add_rms_norm_kernel<T, R, 2> : allreduce_add_rms_norm_kernel<T, R, 4>);
+    auto kern = pushed ? (vpt == 1 ? allreduce_add_rms_norm_kernel<T, R, 1, true>
+                                   : (vpt == 2 ? allreduce_add_rms_norm_kernel<T, R, 2, true>
+                                               : allreduce_add_rms_norm_kernel<T, R, 4, true>))
+                       : (vpt == 1 ? allreduce_add_rms_norm_kernel<T, R, 1>
+                                   : (vpt == 2 ? allreduce_add_rms_norm_kernel<T, R, 2>
+                                               : allreduce_add_rms_norm_kernel<T, R, 4>));
     const T* d = static_cast<const T*>(delta);
     const R* res = static_cast<const R*>(residual);
     const T* wt = static_cast<const T*>(w);
@@ -470,6 +478,26 @@ extern "C" dli_status dli_sm100_allreduce_add_rms_norm_ex(
   });
   if (st != DLI_OK) return st;
   return check_launch(name);
+}
+}  // namespace
+
+extern "C" dli_status dli_sm100_allreduce_add_rms_norm_ex(
+    void* const* buffers, int tp, int rank, int ranks_in_launch, int64_t max_rows, int64_t row_elems,
+    const void* delta, const void* residual, const void* w, void* normed, void* residual_out,
+    int64_t rank_stride, int64_t rows, int64_t hidden, float eps, int64_t timeout_ns, dli_dtype dtype,
+    dli_dtype residual_dtype, void* stream) {
+  return run_allreduce_norm(buffers, tp, rank, ranks_in_launch, max_rows, row_elems, delta, residual, w, normed,
+                            residual_out, rank_stride, rows, hidden, eps, timeout_ns, dtype, residual_dtype, false,
+                            stream);
+}
+
+extern "C" dli_status dli_sm100_exchange_add_rms_norm_ex(
+    void* const* buffers, int tp, int rank, int ranks_in_launch, int64_t max_rows, int64_t row_elems,
+    const void* residual, const void* w, void* normed, void* residual_out, int64_t rank_stride, int64_t rows,
+    int64_t hidden, float eps, int64_t timeout_ns, dli_dtype dtype, dli_dtype residual_dtype, void* stream) {
+  return run_allreduce_norm(buffers, tp, rank, ranks_in_launch, max_rows, row_elems, nullptr, residual, w, normed,
+                            residual_out, rank_stride, rows, hidden, eps, timeout_ns, dtype, residual_dtype, true,
+                            stream);
 }
 
 extern "C" dli_status dli_sm100_allgather_argmax(void* const* buffers, int tp, int rank, int ranks_in_launch,

@@ -27,6 +27,7 @@
 #include <type_traits>
 
 #include "gemm.cuh"
+#include "exchange.cuh"
 #include "tcgen05.cuh"
 
 namespace dli_sm100 {
@@ -64,27 +65,31 @@ struct TcLayout {
 // rows [r*R, (r+1)*R), R = ceil(128/S). kEpiGluT: rank r owns gate rows
 // [r*Rg, (r+1)*Rg) of 0..63, Rg = ceil(64/S), and the matching up rows (+64),
 // stored after its Rg gate rows.
+// kEpiExchange: R = 2*ceil(64/S), even, so each rank owns whole feature pairs.
+__device__ __host__ __forceinline__ int push_rows_per_rank(int epilogue, int S) {
+  return epilogue == kEpiExchange ? 2 * ((64 + S - 1) / S) : (kBM + S - 1) / S;
+}
 __device__ __forceinline__ void push_owner(int epilogue, int S, int row, int& owner, int& lidx) {
   if (epilogue == kEpiGluT) {
     const int rg = (64 + S - 1) / S, g = row & 63;
     owner = g / rg;
     lidx = (g - owner * rg) + (row >> 6) * rg;
   } else {
-    const int r = (kBM + S - 1) / S;
+    const int r = push_rows_per_rank(epilogue, S);
     owner = row / r;
     lidx = row - owner * r;
   }
 }
 // Receive-slot height (rows per sender) and the rows this rank owns.
 __device__ __host__ __forceinline__ int push_slot_rows(int epilogue, int S) {
-  return epilogue == kEpiGluT ? 2 * ((64 + S - 1) / S) : (kBM + S - 1) / S;
+  return epilogue == kEpiGluT ? 2 * ((64 + S - 1) / S) : push_rows_per_rank(epilogue, S);
 }
 __device__ __host__ __forceinline__ int push_my_rows(int epilogue, int S, int rank) {
   if (epilogue == kEpiGluT) {
     const int rg = (64 + S - 1) / S;
     return 2 * max(0, min(rg, 64 - rank * rg));
   }
-  const int r = (kBM + S - 1) / S;
+  const int r = push_rows_per_rank(epilogue, S);
   return max(0, min(r, kBM - rank * r));
 }
 
@@ -101,6 +106,10 @@ struct TcParams {
   int out_f32;  // RowMajor / Transposed: the output is float32 (operands stay T)
   int b_mn;     // operand B is MN-major: [K, rows_b] with rows_b contiguous (matmul)
   int bias_f32; // out_f32 epilogues: the bias is float32 (fp32 GEMM), else T
+  // kEpiExchange: the group's exchange buffers as mapped here, this rank, and their geometry
+  char* xbuf[kExchangeMaxRanks];
+  int xtp, xrank;
+  int64_t xmax_rows, xrow_words;
   // stream-K (tcgen05_gemm_streamk_kernel): partial tiles [ctas][2][128][BN] fp32
   // and one arrival counter per tile, zero between calls
   float* sk_part;
@@ -477,6 +486,49 @@ __device__ __forceinline__ void tile_push_reduce(const TcParams& p, uint8_t* sme
     return;
   }
   const int quads = mine * (BN / 4);
+  if (p.epilogue == kEpiExchange) {
+    // rows = output features, columns = tokens; a word holds features (f, f+1)
+    // of one token: the even row's thread packs its value with its neighbour's
+    // (mine and the rank's first row are even, so the pair is lanes q, q ^ 1)
+    // and stores the word, at the token row's next epoch, into every rank's buffer
+    const uint32_t* epochs = reinterpret_cast<const uint32_t*>(p.xbuf[p.xrank]);
+    const T* bias = static_cast<const T*>(p.bias);
+    for (int base = 0; base < quads; base += kThreads) {  // the same trip count in every lane
+      const int q = base + static_cast<int>(threadIdx.x);
+      const bool act = q < quads;
+      const int lr = act ? q % mine : 0, cq = act ? (q / mine) * 4 : 0;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (act) {
+        for (int s2 = 0; s2 < S; ++s2) {
+          const float4 a = *reinterpret_cast<const float4*>(recv + (s2 * slot_rows + lr) * (BN + 4) + cq);
+          v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+        }
+      }
+      const int64_t f = static_cast<int64_t>(ti) * kBM + split * slot_rows + lr;  // output feature
+      const bool live = act && f < p.rows_a;
+      const float bv = (live && bias) ? to_f32(bias[f]) : 0.f;
+      uint32_t h[4], other[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const T x = from_f32<T>(v[k] + bv);
+        h[k] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&x));
+        other[k] = __shfl_xor_sync(0xffffffffu, h[k], 1);
+      }
+      if (live && (lr & 1) == 0) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int t = tj * BN + cq + k;  // token = exchange row
+          if (t >= p.rows_b) break;
+          const uint32_t e = epochs[t] + 1u;
+          for (int dst = 0; dst < p.xtp; ++dst)
+            exchange_store_word(exchange_row_words(p.xbuf[dst], p.xmax_rows, p.xrow_words, p.xtp,
+                                                   static_cast<int>(e & 1u), p.xrank, t) + f / 2,
+                                h[k] | (other[k] << 16), e);
+        }
+      }
+    }
+    return;
+  }
   for (int q = threadIdx.x; q < quads; q += kThreads) {
     const int lr = q % mine, cq = (q / mine) * 4;  // consecutive threads: consecutive rows
     float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -2396,6 +2448,61 @@ extern "C" dli_status dli_sm100_linear_ex(const void* x, const void* w, const vo
                                workspace_bytes, as_stream(stream), true, false, 0, true);
   return run_tn_gemm_tcgen05(x, w, bias, y, m, n, k, k, k, n, kEpiRowMajor, 0, dtype, plan, workspace,
                              workspace_bytes, as_stream(stream), false, true, 0, true);
+}
+
+extern "C" dli_status dli_sm100_linear_exchange_push(const void* x, const void* w, const void* bias, int64_t m,
+                                                     int64_t n, int64_t k, dli_dtype dtype, void* const* buffers,
+                                                     int tp, int rank, int64_t max_rows, int64_t row_elems,
+                                                     void* stream) {
+  const std::string name = "linear_exchange_push";
+  if (m < 0 || n <= 0 || k <= 0 || max_rows <= 0 || row_elems <= 0)
+    return fail(DLI_ERR_INVALID_ARGUMENT, name + ": bad sizes");
+  if (buffers == nullptr || tp < 1 || tp > kExchangeMaxRanks || rank < 0 || rank >= tp)
+    return fail(DLI_ERR_INVALID_ARGUMENT, name + ": bad rank arguments");
+  if (dtype != DLI_DTYPE_BF16 && dtype != DLI_DTYPE_F16)
+    return fail(DLI_ERR_UNSUPPORTED, name + ": bfloat16/float16 only");
+  if (m == 0) return ok();
+  if (!x || !w) return fail(DLI_ERR_INVALID_ARGUMENT, name + ": null pointer");
+  // Shape checks only (the same answer on every rank, so a caller that falls
+  // back to the two-kernel path on DLI_ERR_UNSUPPORTED keeps the group in step):
+  // a swap-AB decode tile whose K is split over a cluster (push reduction).
+  if (m > kSwapRows || m > max_rows || n > row_elems || n % 8 != 0 || row_elems % 8 != 0 || k % 8 != 0)
+    return fail(DLI_ERR_UNSUPPORTED, name + ": shape outside the fused exchange path");
+  const GemmPlan plan = plan_tn_gemm(n, m, k, dtype, true);
+  if (!plan.tcgen05 || plan.bn > 64 || plan.splits < 2)
+    return fail(DLI_ERR_UNSUPPORTED, name + ": plan without a split-K push reduction");
+  if (!aligned(x, 16) || !aligned(w, 16) || (bias && !aligned(bias, 2)))
+    return fail(DLI_ERR_INVALID_ARGUMENT, name + ": 16-byte aligned operands expected");
+  TcParams p{};
+  for (int i = 0; i < tp; ++i) {
+    if (buffers[i] == nullptr || !aligned(buffers[i], 256))
+      return fail(DLI_ERR_INVALID_ARGUMENT, name + ": exchange buffers must be 256-byte aligned");
+    p.xbuf[i] = static_cast<char*>(buffers[i]);
+  }
+  const bool bf16 = dtype == DLI_DTYPE_BF16;
+  CUtensorMap ma, mb;
+  dli_status st = make_kmajor_map(&ma, w, n, k, k, kBM, bf16);
+  if (st != DLI_OK) return st;
+  st = make_kmajor_map(&mb, x, m, k, k, plan.bn, bf16);
+  if (st != DLI_OK) return st;
+  p.rows_a = static_cast<int>(n);
+  p.rows_b = static_cast<int>(m);
+  p.tiles_i = plan.tiles_i;
+  p.tiles_j = plan.tiles_j;
+  p.kblocks = plan.kblocks;
+  p.splits = plan.splits;
+  p.epilogue = kEpiExchange;
+  p.ohw = 1;
+  p.bias = bias;
+  p.out = nullptr;
+  p.err = device_error_word();
+  p.const_a = 1;
+  p.xtp = tp;
+  p.xrank = rank;
+  p.xmax_rows = max_rows;
+  p.xrow_words = row_elems * 2 / 4;
+  return bf16 ? launch_tc_bn<__nv_bfloat16>(plan.bn, plan.stages, ma, mb, p, plan.splits, as_stream(stream))
+              : launch_tc_bn<__half>(plan.bn, plan.stages, ma, mb, p, plan.splits, as_stream(stream));
 }
 
 extern "C" dli_status dli_sm100_linear_silu_mul(const void* x, const void* w_glu, void* y, int64_t m,

@@ -764,6 +764,70 @@ class AllReduceAddRmsNormOp final : public dli::Operator {
   }
 };
 
+// linear_all_reduce_add_rms_norm: (residual, x, w, weight) -> (normed, residual +
+// all_reduce(x . w^T)). A row-split projection and the all-reduce + residual add +
+// RMSNorm after it as one node. With an exchange buffer for the run's
+// communicator and a decode-sized call, the projection's GEMM pushes its
+// partial rows into every rank's exchange buffer from its own split-K epilogue
+// (dli_sm100_linear_exchange_push) and one kernel sums, adds and normalises
+// (dli_sm100_exchange_add_rms_norm_ex), bit-identical to the two-node form.
+// Other calls (prefill rows, tp == 1, no buffer) run linear, then the
+// all_reduce_add_rms_norm operator. The fused path is declined
+// (DLI_ERR_UNSUPPORTED) for shape reasons only, the same on every rank.
+class LinearAllReduceAddRmsNormOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "linear_all_reduce_add_rms_norm"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 4, 4, 2, type());
+    dli::requireCudaInputs(in, type());
+    for (const Tensor* t : in) dli::requireFloat(*t, type());
+    const Tensor& r = *in[0];
+    const Tensor& x = *in[1];
+    const Tensor& w = *in[2];
+    const Tensor& g = *in[3];
+    dli::requireSameDtype(x, w, type());
+    dli::requireSameDtype(x, g, type());
+    if (r.dtype() != x.dtype() &&
+        !(r.dtype() == DType::Float32 && (x.dtype() == DType::BFloat16 || x.dtype() == DType::Float16)))
+      throw std::invalid_argument(type() + ": residual must match x or be float32 around a 16-bit x");
+    if (w.rank() != 2) throw std::invalid_argument(type() + ": weight must be 2-D");
+    const std::int64_t k = x.shape().back(), n = w.dim(0);
+    if (w.dim(1) != k) throw std::invalid_argument(type() + ": weight K mismatch");
+    const std::int64_t m = dli::product(x.shape(), 0, x.rank() - 1);
+    if (r.shape().back() != n || static_cast<std::int64_t>(r.numel()) != m * n)
+      throw std::invalid_argument(type() + ": residual must be [.., " + std::to_string(n) + "] with x's rows");
+    if (static_cast<std::int64_t>(g.numel()) != n) throw std::invalid_argument(type() + ": norm weight size");
+    const float eps = static_cast<float>(dli::attrDouble(attrs, "eps", 1e-6));
+    if (ctx.tp_size > 1 && ctx.communicator != nullptr) {
+      const Exchange* ex = findExchange(ctx.communicator);
+      if (ex != nullptr && ex->tp == ctx.tp_size && ex->rank == ctx.tp_rank && ex->dtype == cdt(x.dtype()) &&
+          m <= ex->max_rows && n <= ex->row_elems) {
+        const dli_status st = dli_sm100_linear_exchange_push(dli::ptr(x), dli::ptr(w), nullptr, m, n, k,
+                                                             cdt(x.dtype()), ex->ptrs.data(), ex->tp, ex->rank,
+                                                             ex->max_rows, ex->row_elems, ctx.cuda_stream);
+        if (st == DLI_OK) {
+          *out[0] = Tensor::cuda(x.dtype(), r.shape(), r.deviceId());
+          *out[1] = Tensor::cuda(r.dtype(), r.shape(), r.deviceId());
+          check(dli_sm100_exchange_add_rms_norm_ex(ex->ptrs.data(), ex->tp, ex->rank, 1, ex->max_rows,
+                                                   ex->row_elems, dli::ptr(r), dli::ptr(g), out[0]->deviceData(),
+                                                   out[1]->deviceData(), 0, m, n, eps, 0, cdt(x.dtype()),
+                                                   cdt(r.dtype()), ctx.cuda_stream),
+                type());
+          return;
+        }
+        if (st != DLI_ERR_UNSUPPORTED) check(st, type());
+      }
+    }
+    // two-node form: the partial projection, then the all-reduce + add + norm
+    Tensor part;
+    const Tensor* lin_in[2] = {&x, &w};
+    Tensor* lin_out[1] = {&part};
+    LinearOp().compute(Inputs(lin_in, lin_in + 2), Outputs(lin_out, lin_out + 1), Attributes{}, ctx);
+    const Tensor* ar_in[3] = {&r, &part, &g};
+    AllReduceAddRmsNormOp().compute(Inputs(ar_in, ar_in + 3), out, attrs, ctx);
+  }
+};
+
 // tp_argmax: logits [.., width] holding ids [tp_rank*width, (tp_rank+1)*width) of a
 // vocabulary split over the tensor-parallel group -> int64 ids of the row maxima
 // over the whole vocabulary (lowest id on ties). One kernel: local argmax and an
@@ -828,6 +892,7 @@ extern "C" bool dli_register_operators(dli::OperatorRegistry* registry) {
   reg<CastOp>(registry, "cast");
   reg<AllReduceOp>(registry, "all_reduce");
   reg<AllReduceAddRmsNormOp>(registry, "all_reduce_add_rms_norm");
+  reg<LinearAllReduceAddRmsNormOp>(registry, "linear_all_reduce_add_rms_norm");
   reg<TpArgmaxOp>(registry, "tp_argmax");
   return true;
 }

@@ -185,7 +185,7 @@ def transform_weights(state: dict[str, torch.Tensor], shape: Qwen2Shape, tp_size
 def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: str = "qwen2",
                 weights_file: str = "", with_argmax: bool = True, fused_glu: bool = True,
                 logits_dtype: str | None = "float32",
-                residual_dtype: str | None = "float32") -> dict[str, Any]:
+                residual_dtype: str | None = "float32", fused_exchange: bool = True) -> dict[str, Any]:
     """dli.graph.v1 dict for one rank. Inputs: input_ids [B,S] int64, positions [B]
     int64, rotary_cos/rotary_sin, and the weights of transform_weights() (made
     with the same `fused_glu`: one linear_silu_mul node instead of linear +
@@ -196,7 +196,10 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
     stream (embedding output + every block's output) in fp32: a cast after the
     embedding starts it and each add_rms_norm adds the block's bf16 output to it
     unrounded, so a 16-bit model does not round its running sum once per layer
-    (None keeps the residual in the weights' dtype)."""
+    (None keeps the residual in the weights' dtype). With tensor parallelism,
+    `fused_exchange` makes each row-split projection and the all-reduce + add +
+    RMSNorm after it one `linear_all_reduce_add_rms_norm` node, whose decode
+    GEMM pushes its partial rows into the group's exchange buffers itself."""
     hq, hkv, d = shape.q_heads // tp_size, shape.kv_heads // tp_size, shape.head_dim
     nodes: list[dict[str, Any]] = []
 
@@ -207,18 +210,28 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
     # residual add + RMSNorm after a row-split projection; with tensor parallelism
     # the projection's output is a partial sum, all-reduced by the same node
     add_norm = "all_reduce_add_rms_norm" if tp_size > 1 else "add_rms_norm"
+    fuse = fused_exchange and tp_size > 1
+
+    def project_add_norm(name, resid_in, x_in, w_in, ln, outs, proj_name, part):
+        """row-split projection + (all-reduce) + residual add + RMSNorm"""
+        if fuse:
+            node(name, "linear_all_reduce_add_rms_norm", [resid_in, x_in, w_in, ln], outs, {"eps": eps})
+        else:
+            node(proj_name, "linear", [x_in, w_in], [part])
+            node(name, add_norm, [resid_in, part, ln], outs, {"eps": eps})
+
     node("embed_tokens", "embedding", ["input_ids", "embed"], ["h0"])
-    resid, delta = "h0", None
+    resid, pending = "h0", None  # pending: the previous layer's (down input, down weight, name)
     if residual_dtype:
         node("residual_stream", "cast", ["h0"], ["h0_res"], {"dtype": residual_dtype})
         resid = "h0_res"
     for i in range(shape.layers):
         L = f"layers.{i}"
-        if delta is None:
+        if pending is None:
             node(f"{L}.input_layernorm", "rms_norm", ["h0", f"{L}.ln_in"], [f"{L}.x"], {"eps": eps})
         else:
-            node(f"{L}.input_layernorm", add_norm, [resid, delta, f"{L}.ln_in"],
-                 [f"{L}.x", f"{L}.h_in"], {"eps": eps})
+            project_add_norm(f"{L}.input_layernorm", resid, pending[0], pending[1], f"{L}.ln_in",
+                             [f"{L}.x", f"{L}.h_in"], pending[2], pending[3])
             resid = f"{L}.h_in"
         node(f"{L}.qkv_proj", "linear", [f"{L}.x", f"{L}.wqkv", f"{L}.bqkv"], [f"{L}.qkv"])
         node(f"{L}.rotary_cache", "qkv_rotary_cache",
@@ -227,9 +240,8 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
               "kv_cache": f"layer_{i}"})
         node(f"{L}.attention", "attention_kvcache", [f"{L}.q", "positions"], [f"{L}.attn"],
              {"kv_cache": f"layer_{i}"})
-        node(f"{L}.o_proj", "linear", [f"{L}.attn", f"{L}.wo"], [f"{L}.o_part"])
-        node(f"{L}.post_attention_layernorm", add_norm, [resid, f"{L}.o_part", f"{L}.ln_post"],
-             [f"{L}.x2", f"{L}.h_mid"], {"eps": eps})
+        project_add_norm(f"{L}.post_attention_layernorm", resid, f"{L}.attn", f"{L}.wo", f"{L}.ln_post",
+                         [f"{L}.x2", f"{L}.h_mid"], f"{L}.o_proj", f"{L}.o_part")
         resid = f"{L}.h_mid"
         if fused_glu:
             node(f"{L}.gate_up_proj", "linear_silu_mul", [f"{L}.x2", f"{L}.wgu"], [f"{L}.act"],
@@ -237,9 +249,8 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
         else:
             node(f"{L}.gate_up_proj", "linear", [f"{L}.x2", f"{L}.wgu"], [f"{L}.gu"])
             node(f"{L}.act", "silu_mul", [f"{L}.gu"], [f"{L}.act"])
-        node(f"{L}.down_proj", "linear", [f"{L}.act", f"{L}.wd"], [f"{L}.d_part"])
-        delta = f"{L}.d_part"
-    node("norm", add_norm, [resid, delta, "norm"], ["normed", "h_out"], {"eps": eps})
+        pending = (f"{L}.act", f"{L}.wd", f"{L}.down_proj", f"{L}.d_part")
+    project_add_norm("norm", resid, pending[0], pending[1], "norm", ["normed", "h_out"], pending[2], pending[3])
     node("last_token", "last_token", ["normed"], ["last_hidden"])
     # with a vocab-parallel LM head, `logits` is this rank's slice of the vocabulary
     node("lm_head", "linear", ["last_hidden", "lm_head"], ["logits"],

@@ -75,6 +75,8 @@ SIGNATURES = {
     "dli_sm100_allreduce_add_rms_norm": (N, [P, D, D, D, I, I, P, P, P, P, P, I, I, I, F, I, D, P]),
     "dli_sm100_allreduce_add_rms_norm_ex": (N, [P, D, D, D, I, I, P, P, P, P, P, I, I, I, F, I, D, D, P]),
     "dli_sm100_allgather_argmax": (N, [P, D, D, D, I, I, D, P, I, I, I, P, I, D, P]),
+    "dli_sm100_linear_exchange_push": (N, [P, P, P, I, I, I, D, P, D, D, I, I, P]),
+    "dli_sm100_exchange_add_rms_norm_ex": (N, [P, D, D, D, I, I, P, P, P, P, I, I, I, F, I, D, D, P]),
 }
 
 _lib = None
@@ -270,6 +272,31 @@ class ExchangeGroup:
             _ptr(w), _ptr(normed), _ptr(residual_out), rows * hidden, rows, hidden, eps, timeout_ns,
             _dt(delta), _dt(residual), _stream())
         check(st, "allreduce_add_rms_norm")
+        return normed, residual_out
+
+    def linear_allreduce_add_rms_norm(self, x, w, residual, norm_w, eps=1e-6, timeout_ns=0):
+        """The fused row-split projection: x [tp, rows, k], w [tp, n, k] (each
+        rank's shard), residual [tp, rows, n]. Every rank's GEMM pushes its
+        partial rows into the buffers (dli_sm100_linear_exchange_push, one launch
+        per rank), then one launch over all ranks sums, adds and normalises
+        (dli_sm100_exchange_add_rms_norm_ex). Returns (normed, residual_out), or
+        None when the shape is outside the fused path (DLI_ERR_UNSUPPORTED)."""
+        _contig(x, w, residual, norm_w)
+        tp, rows, k = x.shape
+        n = w.shape[1]
+        L = lib()
+        for r in range(tp):
+            st = L.dli_sm100_linear_exchange_push(_ptr(x[r]), _ptr(w[r]), None, rows, n, k, _dt(x), self._ptrs,
+                                                  self.tp, r, self.max_rows, self.row_elems, _stream())
+            if st == 2 and r == 0:  # DLI_ERR_UNSUPPORTED: nothing was launched on any rank
+                return None
+            check(st, "linear_exchange_push")
+        normed = torch.empty(tp, rows, n, dtype=x.dtype, device=x.device)
+        residual_out = torch.empty_like(residual)
+        st = L.dli_sm100_exchange_add_rms_norm_ex(
+            self._ptrs, self.tp, 0, tp, self.max_rows, self.row_elems, _ptr(residual), _ptr(norm_w), _ptr(normed),
+            _ptr(residual_out), rows * n, rows, n, eps, timeout_ns, _dt(x), _dt(residual), _stream())
+        check(st, "exchange_add_rms_norm")
         return normed, residual_out
 
     def allgather_argmax(self, logits, timeout_ns=0, ranks=None):

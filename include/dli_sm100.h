@@ -351,6 +351,31 @@ dli_status dli_sm100_allgather_argmax(void* const* buffers, int tp, int rank, in
                                       int64_t width, int64_t rank_stride, int64_t* out_ids, int64_t timeout_ns,
                                       dli_dtype dtype, void* stream);
 
+/* A row-split projection and its all-reduce in fewer steps (additive; the
+ * reference has no tensor parallelism): dli_sm100_linear_exchange_push computes
+ * y = x[m,k] . w[n,k]^T (+ bias[n]) for m <= 128 tokens on tcgen05 and, instead
+ * of writing y, stores this rank's partial rows (rounded to dtype) as
+ * epoch-tagged words into every rank's exchange buffer, from the GEMM's own
+ * split-K epilogue; dli_sm100_exchange_add_rms_norm_ex then waits for all
+ * ranks' rows in this rank's buffer, sums them in rank order and applies the
+ * residual add and RMSNorm exactly as dli_sm100_allreduce_add_rms_norm_ex does
+ * with the partial y as delta (bit-identical results). The two calls go
+ * back to back on the stream, once per projection, on every rank of the group.
+ * dli_sm100_linear_exchange_push returns DLI_ERR_UNSUPPORTED, launching
+ * nothing, for shapes it does not serve (m > 128, a plan without split-K); the
+ * decision depends on (m, n, k, dtype) only, so every rank makes the same one
+ * and can fall back to linear + dli_sm100_allreduce_add_rms_norm_ex together.
+ * Misaligned operands are DLI_ERR_INVALID_ARGUMENT. row_elems >= n, a multiple
+ * of 8; max_rows >= m. */
+dli_status dli_sm100_linear_exchange_push(const void* x, const void* w, const void* bias, int64_t m, int64_t n,
+                                          int64_t k, dli_dtype dtype, void* const* buffers, int tp, int rank,
+                                          int64_t max_rows, int64_t row_elems, void* stream);
+dli_status dli_sm100_exchange_add_rms_norm_ex(void* const* buffers, int tp, int rank, int ranks_in_launch,
+                                              int64_t max_rows, int64_t row_elems, const void* residual,
+                                              const void* w, void* normed, void* residual_out, int64_t rank_stride,
+                                              int64_t rows, int64_t hidden, float eps, int64_t timeout_ns,
+                                              dli_dtype dtype, dli_dtype residual_dtype, void* stream);
+
 dli_status dli_sm100_allreduce_add_rms_norm(void* const* buffers, int tp, int rank, int ranks_in_launch,
                                             int64_t max_rows, int64_t row_elems, const void* delta,
                                             const void* residual, const void* w, void* normed,

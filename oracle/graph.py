@@ -69,6 +69,13 @@ class GraphOracle:
             d = x[1] if self.all_reduce is None else self.all_reduce(np.asarray(x[1]))
             n, r = O.add_rms_norm(x[0], d, x[2], a.get("eps", 1e-6))
             return [n, r]
+        if op == "linear_all_reduce_add_rms_norm":
+            # (residual, x, w, norm weight): the row-split projection, its
+            # all-reduce and the residual add + RMSNorm of one Megatron block
+            part = O.linear(x[1], x[2], None)
+            d = part if self.all_reduce is None else self.all_reduce(np.asarray(part))
+            n, r = O.add_rms_norm(x[0], d, x[3], a.get("eps", 1e-6))
+            return [n, r]
         if op == "all_reduce":
             return [x[0] if self.all_reduce is None else self.all_reduce(np.asarray(x[0]))]
         if op == "qkv_rotary_cache":

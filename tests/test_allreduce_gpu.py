@@ -161,3 +161,45 @@ def test_vocab_parallel_argmax_missing_peer_times_out():
     group.allgather_argmax(logits, timeout_ns=50_000_000, ranks=1)
     with pytest.raises(RuntimeError, match="exchange"):
         C.check_device_error()
+
+
+@pytest.mark.parametrize("tp,rows,n,k", [
+    (2, 32, 3584, 1792),    # 7B o_proj at TP 2, the benchmark's 32 sequences
+    (4, 16, 3584, 4736),    # 7B down_proj at TP 4, 16 sequences per data-parallel group
+    (8, 16, 8192, 1024),    # 72B o_proj at TP 8
+    (4, 7, 3584, 896),      # ragged row count
+])
+@pytest.mark.parametrize("res32", [True, False], ids=["res32", "res16"])
+def test_gemm_pushed_exchange_matches_two_kernel_path(tp, rows, n, k, res32):
+    """A row-split projection whose GEMM pushes its partial rows straight into
+    the exchange buffers from its split-K epilogue
+    (dli_sm100_linear_exchange_push), then the sum + residual add + RMSNorm
+    (dli_sm100_exchange_add_rms_norm_ex), against linear + the fused all-reduce
+    of the partial outputs: bit-identical on every rank, over consecutive calls
+    (epochs advance, slots alternate)."""
+    dtype = torch.bfloat16
+    fused = C.ExchangeGroup(tp, max_rows=64, row_elems=8192, dtype=dtype)
+    plain = C.ExchangeGroup(tp, max_rows=64, row_elems=8192, dtype=dtype)
+    g = torch.Generator(device="cuda").manual_seed(tp * 7 + rows + n + k)
+    w = (torch.randn(tp, n, k, device="cuda", generator=g) * 0.02).to(dtype)
+    norm_w = (1 + 0.1 * torch.randn(n, device="cuda", generator=g)).to(dtype)
+    for step in range(3):
+        x = torch.randn(tp, rows, k, device="cuda", generator=g).to(dtype)
+        res = torch.randn(rows, n, device="cuda", generator=g).to(torch.float32 if res32 else dtype)
+        res = res.unsqueeze(0).expand(tp, rows, n).contiguous()
+        got = fused.linear_allreduce_add_rms_norm(x, w, res, norm_w, eps=1e-6)
+        assert got is not None, "shape expected on the fused path"
+        delta = torch.stack([C.linear(x[r], w[r]) for r in range(tp)])
+        ref_n, ref_r = plain.allreduce_add_rms_norm(res, delta, norm_w, eps=1e-6)
+        C.check_device_error()
+        assert torch.equal(got[0], ref_n), step
+        assert torch.equal(got[1], ref_r), step
+
+
+def test_gemm_pushed_exchange_declines_prefill_rows():
+    """More than 128 rows (prefill) is outside the fused path: UNSUPPORTED, nothing launched."""
+    group = C.ExchangeGroup(2, max_rows=512, row_elems=3584, dtype=torch.bfloat16)
+    x = torch.randn(2, 300, 1792, device="cuda").bfloat16()
+    w = (torch.randn(2, 3584, 1792, device="cuda") * 0.02).bfloat16()
+    res = torch.randn(2, 300, 3584, device="cuda")
+    assert group.linear_allreduce_add_rms_norm(x, w, res, torch.ones(3584, device="cuda").bfloat16()) is None

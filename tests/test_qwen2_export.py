@@ -67,12 +67,21 @@ def test_graph_structure_per_layer():
     lm = next(n for n in gf["nodes"] if n["name"] == "lm_head")
     assert lm["attrs"]["out_dtype"] == "float32"
     assert g["inputs"] == ["input_ids", "positions"] and g["outputs"] == ["logits", "next_ids"]
-    g2 = build_graph(TINY, capacity=64, tp_size=2)
+    g2 = build_graph(TINY, capacity=64, tp_size=2, fused_exchange=False)
     ops2 = [n["op"] for n in g2["nodes"]]
     # every add_rms_norm after a row-split projection becomes the all-reduce form
     assert ops2.count("all_reduce_add_rms_norm") == 2 * TINY.layers
     assert "add_rms_norm" not in ops2 and "all_reduce" not in ops2
     assert ops2[-1] == "tp_argmax" and ops[-1] == "argmax"
+    # fused (default): each row-split projection and the all-reduce + add + norm
+    # after it are one node reading the projection's input and weight
+    g3 = build_graph(TINY, capacity=64, tp_size=2)
+    fx = [n for n in g3["nodes"] if n["op"] == "linear_all_reduce_add_rms_norm"]
+    assert len(fx) == 2 * TINY.layers and "all_reduce_add_rms_norm" not in [n["op"] for n in g3["nodes"]]
+    assert fx[0]["inputs"][1:3] == ["layers.0.attn", "layers.0.wo"]
+    assert fx[1]["inputs"][1:3] == ["layers.0.act", "layers.0.wd"]
+    assert fx[-1]["name"] == "norm" and fx[-1]["outputs"] == ["normed", "h_out"]
+    assert len(g3["nodes"]) == len(g2["nodes"]) - 2 * TINY.layers
     rc = next(n for n in g2["nodes"] if n["op"] == "qkv_rotary_cache")
     assert rc["attrs"]["q_heads"] == 2 and rc["attrs"]["kv_heads"] == 1
 
@@ -184,6 +193,12 @@ def _run_tp(oracles, ids, pos, ref):
             # sum the partials (input 1) over the ranks, then the residual add + norm
             total = sum(np.asarray(env[node["inputs"][1]]) for env in envs)
             outs = [o._op("add_rms_norm", [env[node["inputs"][0]], total, env[node["inputs"][2]]], node["attrs"])
+                    for o, env in zip(oracles, envs)]
+        if node["op"] == "linear_all_reduce_add_rms_norm":
+            # each rank's partial projection of (input 1, input 2), summed over the ranks
+            total = sum(O.linear(np.asarray(env[node["inputs"][1]]), np.asarray(env[node["inputs"][2]]), None)
+                        for env in envs)
+            outs = [o._op("add_rms_norm", [env[node["inputs"][0]], total, env[node["inputs"][3]]], node["attrs"])
                     for o, env in zip(oracles, envs)]
         for env, res in zip(envs, outs):
             for name, val in zip(node["outputs"], res):
