@@ -85,6 +85,8 @@ def parse_args():
     ap.add_argument("--prompt", type=int, default=None)
     ap.add_argument("--decode", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-fused-exchange", action="store_true",
+                    help="TP graphs: linear + all_reduce_add_rms_norm nodes instead of the GEMM-epilogue push")
     return ap.parse_args()
 
 
@@ -508,7 +510,8 @@ def main() -> int:
     weights["rotary_cos"], weights["rotary_sin"] = cos.to(dev), sin.to(dev)
     torch.cuda.synchronize()
 
-    runner = Qwen2Runner(shape, weights, capacity, tp_size=tp, tp_rank=tp_rank, communicator=comm or 0)
+    runner = Qwen2Runner(shape, weights, capacity, tp_size=tp, tp_rank=tp_rank, communicator=comm or 0,
+                         fused_exchange=not args.no_fused_exchange)
     gen = torch.Generator(device=dev).manual_seed(100 + group)
     prompts = torch.randint(0, shape.vocab, (b_local, prompt), device=dev, generator=gen)
 
@@ -651,7 +654,8 @@ def main() -> int:
             "config": workload_config(args.model, batch, prompt, dsteps) | {
                        "parallelism": f"tp{tp}" + (f"xdp{dp}" if dp > 1 else ""),
                        "l2": "inputs larger than L2 (weights stream from HBM every step)",
-                       "kv_capacity": capacity},
+                       "kv_capacity": capacity} | ({"tp_exchange": "exchange kernel" if args.no_fused_exchange
+                                                    else "GEMM-epilogue push"} if tp > 1 else {}),
             "prefill": {"value": prefill_tok_s, "unit": "tok/s (prefill)", "ms_per_step": pre_ms / args.steps},
             "decode_ms_per_token_step": step_ms,
             "e2e": {"value": e2e_tok_s, "unit": "tok/s (decode)", "h2d_bytes_per_step": 8 * b_local,

@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(512) allreduce_add_rms_norm_kernel(
   constexpr int V = Vec16<T>::N;
   __shared__ float scratch[32];
   __shared__ uint32_t s_epoch;
-  pdl_wait();  // the partial comes from the previous kernel
+  pdl_wait();  // the partial (or, pushed, the GEMM that stored it) comes from the previous kernel
   pdl_trigger();
   const int rank = p.rank0 + static_cast<int>(blockIdx.y);
   const int64_t r = blockIdx.x;

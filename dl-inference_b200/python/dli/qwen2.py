@@ -19,9 +19,11 @@ from . import PLUGIN_PATH, Engine, Graph
 class Qwen2Runner:
     def __init__(self, shape: Any, weights: dict[str, torch.Tensor], capacity: int,
                  tp_size: int = 1, tp_rank: int = 0, communicator: int = 0,
-                 plugin: str = PLUGIN_PATH, fused_glu: bool = True):
+                 plugin: str = PLUGIN_PATH, fused_glu: bool = True, fused_exchange: bool = True):
         """`weights` come from dli_export.qwen2.transform_weights with the same
-        `fused_glu` (the fused SwiGLU GEMM serves bfloat16/float16 weights)."""
+        `fused_glu` (the fused SwiGLU GEMM serves bfloat16/float16 weights).
+        `fused_exchange`: tensor-parallel projections push their partial rows
+        from the GEMM epilogue (linear_all_reduce_add_rms_norm nodes)."""
         from dli_export.qwen2 import build_graph, rotary_tables
 
         self.shape = shape
@@ -31,7 +33,8 @@ class Qwen2Runner:
         self.engine.load_library(plugin)
         if tp_size > 1:
             self.engine.set_communicator(communicator, tp_rank, tp_size)
-        self.graph = Graph.from_json(json.dumps(build_graph(shape, capacity, tp_size, fused_glu=fused_glu)))
+        self.graph = Graph.from_json(json.dumps(build_graph(shape, capacity, tp_size, fused_glu=fused_glu,
+                                                            fused_exchange=fused_exchange)))
         consts = dict(weights)
         if "rotary_cos" not in consts:
             cos, sin = rotary_tables(shape, capacity)

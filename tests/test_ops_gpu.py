@@ -311,6 +311,30 @@ def test_conv2d_alexnet_shapes(c, h, oc, dtype):
     assert_close(y.float(), ref, dtype, f"conv {c}->{oc} @{h}")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("n,c,h,w,oc,kh,kw,stride,pad", [
+    (4, 64, 20, 20, 96, 1, 1, (1, 1), (0, 0)),     # 1x1: the gather is a plain copy
+    (2, 16, 33, 31, 40, 5, 5, (1, 1), (2, 2)),     # 5x5, odd sizes, K = 400 (two k blocks, zero tail)
+    (2, 3, 64, 64, 64, 7, 7, (2, 2), (3, 3)),      # 7x7 stride 2 stem, K = 147 (weight repacked to 152)
+    (8, 128, 14, 14, 256, 3, 3, (2, 2), (0, 0)),   # stride 2, no padding, split-K plan
+    (1, 32, 9, 40, 48, 3, 1, (1, 2), (1, 0)),      # non-square kernel and strides
+])
+def test_conv2d_implicit_gemm_shapes(n, c, h, w, oc, kh, kw, stride, pad, dtype):
+    """bf16/f16 conv2d on the implicit-GEMM tcgen05 kernel (patches gathered into
+    shared memory: kernel sizes, strides, padding, K tails and repacked weights)
+    against an fp64 convolution of the same rounded inputs."""
+    import dli_sm100 as C
+
+    g = torch.Generator().manual_seed(n + c + h + oc + kh)
+    x = torch.randn(n, c, h, w, generator=g).to(dtype)
+    wt = (torch.randn(oc, c, kh, kw, generator=g) * 0.05).to(dtype)
+    b = (torch.randn(oc, generator=g) * 0.05).to(dtype)
+    y = C.conv2d(x.cuda(), wt.cuda(), b.cuda(), stride, pad)
+    C.check_device_error()
+    ref = torch.nn.functional.conv2d(x.double(), wt.double(), b.double(), stride=stride, padding=pad)
+    assert_close(y.float(), ref, dtype, f"conv {c}->{oc} k{kh}x{kw} s{stride} p{pad}")
+
+
 # ---- attention ----------------------------------------------------------------------
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
