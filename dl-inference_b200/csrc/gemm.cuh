@@ -18,6 +18,12 @@ enum GemmEpilogue : int {
   // the rows, rounded to T, go as epoch-tagged words into every tensor-parallel
   // rank's exchange buffer (row j, feature pairs i, i+1 per word), not to `out`
   kEpiExchange = 5,
+  // swap-AB, split-K push plans only: D row i = feature of the fused q|k|v
+  // projection, column j = token; rounded to T, the q and k rows rotated
+  // (interleaved pairs i, i+1) and written to q_out [tokens, Hq, D] and into
+  // the KV cache rows of each token's position, as dli_sm100_qkv_rotary_cache
+  // does with the projection's output
+  kEpiQkvRotary = 6,
 };
 
 struct GemmPlan {

@@ -65,9 +65,10 @@ struct TcLayout {
 // rows [r*R, (r+1)*R), R = ceil(128/S). kEpiGluT: rank r owns gate rows
 // [r*Rg, (r+1)*Rg) of 0..63, Rg = ceil(64/S), and the matching up rows (+64),
 // stored after its Rg gate rows.
-// kEpiExchange: R = 2*ceil(64/S), even, so each rank owns whole feature pairs.
+// kEpiExchange, kEpiQkvRotary: R = 2*ceil(64/S), even, so each rank owns whole
+// feature pairs.
 __device__ __host__ __forceinline__ int push_rows_per_rank(int epilogue, int S) {
-  return epilogue == kEpiExchange ? 2 * ((64 + S - 1) / S) : (kBM + S - 1) / S;
+  return (epilogue == kEpiExchange || epilogue == kEpiQkvRotary) ? 2 * ((64 + S - 1) / S) : (kBM + S - 1) / S;
 }
 __device__ __forceinline__ void push_owner(int epilogue, int S, int row, int& owner, int& lidx) {
   if (epilogue == kEpiGluT) {
@@ -110,6 +111,15 @@ struct TcParams {
   char* xbuf[kExchangeMaxRanks];
   int xtp, xrank;
   int64_t xmax_rows, xrow_words;
+  // kEpiQkvRotary: tables [table_rows, pairs], positions [B], outputs, geometry
+  const float* rot_cos;
+  const float* rot_sin;
+  const int64_t* rot_pos;
+  void* rot_q;
+  void* rot_k;
+  void* rot_v;
+  int rot_hq, rot_hkv, rot_d, rot_seq;
+  int64_t rot_pairs, rot_rows, rot_cap;
   // stream-K (tcgen05_gemm_streamk_kernel): partial tiles [ctas][2][128][BN] fp32
   // and one arrival counter per tile, zero between calls
   float* sk_part;
@@ -524,6 +534,68 @@ __device__ __forceinline__ void tile_push_reduce(const TcParams& p, uint8_t* sme
             exchange_store_word(exchange_row_words(p.xbuf[dst], p.xmax_rows, p.xrow_words, p.xtp,
                                                    static_cast<int>(e & 1u), p.xrank, t) + f / 2,
                                 h[k] | (other[k] << 16), e);
+        }
+      }
+    }
+    return;
+  }
+  if (p.epilogue == kEpiQkvRotary) {
+    // rows = features of q|k|v, columns = tokens. Each value is rounded to T
+    // first (the projection's output), then the even/odd features of a rotated
+    // pair (lanes q, q ^ 1) combine with the table entry of the token's
+    // position exactly as the separate rotary kernel computes them.
+    const T* bias = static_cast<const T*>(p.bias);
+    const int D = p.rot_d;
+    for (int base = 0; base < quads; base += kThreads) {  // the same trip count in every lane
+      const int q = base + static_cast<int>(threadIdx.x);
+      const bool act = q < quads;
+      const int lr = act ? q % mine : 0, cq = act ? (q / mine) * 4 : 0;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (act) {
+        for (int s2 = 0; s2 < S; ++s2) {
+          const float4 a = *reinterpret_cast<const float4*>(recv + (s2 * slot_rows + lr) * (BN + 4) + cq);
+          v[0] += a.x; v[1] += a.y; v[2] += a.z; v[3] += a.w;
+        }
+      }
+      const int f = ti * kBM + split * slot_rows + lr;  // feature of q|k|v
+      const bool live = act && f < p.rows_a;
+      const float bv = (live && bias) ? to_f32(bias[f]) : 0.f;
+      float x[4], xo[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        x[k] = round_through<T>(v[k] + bv);
+        xo[k] = __shfl_xor_sync(0xffffffffu, x[k], 1);
+      }
+      if (!live) continue;
+      const int head = f / D, d = f - head * D, pair = d >> 1;
+      const bool even = (d & 1) == 0;
+      const bool rotated = head < p.rot_hq + p.rot_hkv && pair < p.rot_pairs;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int t = tj * BN + cq + k;  // token b * S + s
+        if (t >= p.rows_b) break;
+        const int b = t / p.rot_seq, sq = t - b * p.rot_seq;
+        const int64_t pos = p.rot_pos[b] + sq;
+        float y = x[k];
+        if (rotated) {
+          if (pos >= 0 && pos < p.rot_rows) {
+            const float c = p.rot_cos[pos * p.rot_pairs + pair], sn = p.rot_sin[pos * p.rot_pairs + pair];
+            const float a = even ? x[k] : xo[k], bb = even ? xo[k] : x[k];
+            y = even ? a * c - bb * sn : a * sn + bb * c;
+          } else {
+            set_device_error(p.err, kDevErrRotaryPosition);
+          }
+        }
+        const T o = from_f32<T>(y);
+        if (head < p.rot_hq) {
+          static_cast<T*>(p.rot_q)[(static_cast<int64_t>(t) * p.rot_hq + head) * D + d] = o;
+        } else if (pos >= 0 && pos < p.rot_cap) {
+          const bool is_k = head < p.rot_hq + p.rot_hkv;
+          const int kvh = is_k ? head - p.rot_hq : head - p.rot_hq - p.rot_hkv;
+          static_cast<T*>(is_k ? p.rot_k : p.rot_v)[((static_cast<int64_t>(b) * p.rot_hkv + kvh) * p.rot_cap + pos) * D +
+                                                  d] = o;
+        } else {
+          set_device_error(p.err, kDevErrKvCapacity);
         }
       }
     }
@@ -2501,6 +2573,66 @@ extern "C" dli_status dli_sm100_linear_exchange_push(const void* x, const void* 
   p.xrank = rank;
   p.xmax_rows = max_rows;
   p.xrow_words = row_elems * 2 / 4;
+  return bf16 ? launch_tc_bn<__nv_bfloat16>(plan.bn, plan.stages, ma, mb, p, plan.splits, as_stream(stream))
+              : launch_tc_bn<__half>(plan.bn, plan.stages, ma, mb, p, plan.splits, as_stream(stream));
+}
+
+extern "C" dli_status dli_sm100_linear_qkv_rotary_cache(
+    const void* x, const void* wqkv, const void* bqkv, const float* cos_table, const float* sin_table,
+    const int64_t* positions, void* q_out, void* cache_k, void* cache_v, int64_t batch, int64_t seq, int64_t k,
+    int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t pairs, int64_t table_rows, int64_t capacity,
+    dli_dtype dtype, void* stream) {
+  const std::string name = "linear_qkv_rotary_cache";
+  if (batch < 0 || seq < 0 || k <= 0 || q_heads <= 0 || kv_heads <= 0 || head_dim <= 0 || head_dim % 2 != 0 ||
+      pairs < 0 || pairs > head_dim / 2 || table_rows <= 0 || capacity <= 0)
+    return fail(DLI_ERR_INVALID_ARGUMENT, name + ": bad sizes");
+  if (dtype != DLI_DTYPE_BF16 && dtype != DLI_DTYPE_F16)
+    return fail(DLI_ERR_UNSUPPORTED, name + ": bfloat16/float16 only");
+  const int64_t m = batch * seq, n = (q_heads + 2 * kv_heads) * head_dim;
+  if (m == 0) return ok();
+  if (!x || !wqkv || !cos_table || !sin_table || !positions || !q_out || !cache_k || !cache_v)
+    return fail(DLI_ERR_INVALID_ARGUMENT, name + ": null pointer");
+  // decode-sized calls whose K is split over a cluster (push reduction); others
+  // take linear + dli_sm100_qkv_rotary_cache
+  if (m > kSwapRows || k % 8 != 0 || n > (1 << 30))
+    return fail(DLI_ERR_UNSUPPORTED, name + ": shape outside the fused path");
+  const GemmPlan plan = plan_tn_gemm(n, m, k, dtype, true);
+  if (!plan.tcgen05 || plan.bn > 64 || plan.splits < 2)
+    return fail(DLI_ERR_UNSUPPORTED, name + ": plan without a split-K push reduction");
+  if (!aligned(x, 16) || !aligned(wqkv, 16))
+    return fail(DLI_ERR_UNSUPPORTED, name + ": 16-byte aligned operands expected");
+  const bool bf16 = dtype == DLI_DTYPE_BF16;
+  CUtensorMap ma, mb;
+  dli_status st = make_kmajor_map(&ma, wqkv, n, k, k, kBM, bf16);
+  if (st != DLI_OK) return st;
+  st = make_kmajor_map(&mb, x, m, k, k, plan.bn, bf16);
+  if (st != DLI_OK) return st;
+  TcParams p{};
+  p.rows_a = static_cast<int>(n);
+  p.rows_b = static_cast<int>(m);
+  p.tiles_i = plan.tiles_i;
+  p.tiles_j = plan.tiles_j;
+  p.kblocks = plan.kblocks;
+  p.splits = plan.splits;
+  p.epilogue = kEpiQkvRotary;
+  p.ohw = 1;
+  p.bias = bqkv;
+  p.out = nullptr;
+  p.err = device_error_word();
+  p.const_a = 1;
+  p.rot_cos = cos_table;
+  p.rot_sin = sin_table;
+  p.rot_pos = positions;
+  p.rot_q = q_out;
+  p.rot_k = cache_k;
+  p.rot_v = cache_v;
+  p.rot_hq = static_cast<int>(q_heads);
+  p.rot_hkv = static_cast<int>(kv_heads);
+  p.rot_d = static_cast<int>(head_dim);
+  p.rot_seq = static_cast<int>(seq);
+  p.rot_pairs = pairs;
+  p.rot_rows = table_rows;
+  p.rot_cap = capacity;
   return bf16 ? launch_tc_bn<__nv_bfloat16>(plan.bn, plan.stages, ma, mb, p, plan.splits, as_stream(stream))
               : launch_tc_bn<__half>(plan.bn, plan.stages, ma, mb, p, plan.splits, as_stream(stream));
 }

@@ -566,6 +566,61 @@ class QkvRotaryCacheOp final : public dli::Operator {
   }
 };
 
+// linear_qkv_rotary_cache: (x [B,S,H], wqkv, bqkv, cos, sin, positions) -> q
+// [B,S,Hq,D]: the fused q|k|v projection followed by qkv_rotary_cache, as one
+// node. Decode-sized calls run one GEMM whose split-K epilogue rotates and
+// scatters (the qkv tensor is never written); others run linear, then
+// qkv_rotary_cache. Both forms give the same bits. Attributes as qkv_rotary_cache.
+class LinearQkvRotaryCacheOp final : public dli::Operator {
+ public:
+  std::string type() const override { return "linear_qkv_rotary_cache"; }
+  void compute(const Inputs& in, const Outputs& out, const Attributes& attrs, ExecutionContext& ctx) const override {
+    arity(in, out, 6, 6, 1, type());
+    dli::requireCudaInputs(in, type());
+    const Tensor& x = *in[0];
+    const Tensor& w = *in[1];
+    const Tensor& bias = *in[2];
+    const Tensor& cos = *in[3];
+    const Tensor& sin = *in[4];
+    const Tensor& pos = *in[5];
+    dli::requireFloat(x, type());
+    dli::requireSameDtype(x, w, type());
+    dli::requireSameDtype(x, bias, type());
+    if (cos.dtype() != DType::Float32 || sin.dtype() != DType::Float32 || cos.shape() != sin.shape() || cos.rank() != 2)
+      throw std::invalid_argument(type() + " expects float32 cos/sin [max_pos, pairs]");
+    if (pos.dtype() != DType::Int64) throw std::invalid_argument(type() + " positions must be int64");
+    const std::int64_t hq = requireIntAttr(attrs, "q_heads", type());
+    const std::int64_t hkv = requireIntAttr(attrs, "kv_heads", type());
+    const std::int64_t d = requireIntAttr(attrs, "head_dim", type());
+    const std::int64_t cap = requireIntAttr(attrs, "capacity", type());
+    const std::string& name = attrs.require<std::string>("kv_cache");
+    if (x.rank() != 3 || w.rank() != 2 || w.dim(0) != (hq + 2 * hkv) * d || w.dim(1) != x.dim(2) ||
+        static_cast<std::int64_t>(bias.numel()) != w.dim(0))
+      throw std::invalid_argument(type() + " expects x [B,S,H], wqkv [(Hq+2Hkv)*D, H], bqkv [(Hq+2Hkv)*D]");
+    const std::int64_t b = x.dim(0), s = x.dim(1), k = x.dim(2);
+    if (static_cast<std::int64_t>(pos.numel()) != b) throw std::invalid_argument(type() + " positions must be [B]");
+    if (ctx.kv_cache == nullptr) throw std::invalid_argument(type() + " missing KV cache");
+    if (x.dtype() == DType::BFloat16 || x.dtype() == DType::Float16) {
+      dli::KVCacheEntry& e = ctx.kv_cache->reserve(name, b, hkv, cap, d, x.dtype(), x.deviceId());
+      *out[0] = Tensor::cuda(x.dtype(), {b, s, hq, d}, x.deviceId());
+      const dli_status st = dli_sm100_linear_qkv_rotary_cache(
+          dli::ptr(x), dli::ptr(w), dli::ptr(bias), static_cast<const float*>(dli::ptr(cos)),
+          static_cast<const float*>(dli::ptr(sin)), static_cast<const std::int64_t*>(dli::ptr(pos)),
+          out[0]->deviceData(), e.key.deviceData(), e.value.deviceData(), b, s, k, hq, hkv, d, cos.dim(1),
+          cos.dim(0), e.capacity(), cdt(x.dtype()), ctx.cuda_stream);
+      if (st == DLI_OK) return;
+      if (st != DLI_ERR_UNSUPPORTED) check(st, type());
+    }
+    // two-step form: the projection, then rotary + cache write
+    Tensor qkv;
+    const Tensor* lin_in[3] = {&x, &w, &bias};
+    Tensor* lin_out[1] = {&qkv};
+    LinearOp().compute(Inputs(lin_in, lin_in + 3), Outputs(lin_out, lin_out + 1), Attributes{}, ctx);
+    const Tensor* rc_in[4] = {&qkv, &cos, &sin, &pos};
+    QkvRotaryCacheOp().compute(Inputs(rc_in, rc_in + 4), out, attrs, ctx);
+  }
+};
+
 // attention_kvcache: (q [B,S,Hq,D], positions[B]) -> out [B,S,Hq*D] over the
 // kv_cache entry's rows [0, positions[b] + S), bottom-right causal.
 class AttentionKvCacheOp final : public dli::Operator {
@@ -893,6 +948,7 @@ extern "C" bool dli_register_operators(dli::OperatorRegistry* registry) {
   reg<AllReduceOp>(registry, "all_reduce");
   reg<AllReduceAddRmsNormOp>(registry, "all_reduce_add_rms_norm");
   reg<LinearAllReduceAddRmsNormOp>(registry, "linear_all_reduce_add_rms_norm");
+  reg<LinearQkvRotaryCacheOp>(registry, "linear_qkv_rotary_cache");
   reg<TpArgmaxOp>(registry, "tp_argmax");
   return true;
 }

@@ -185,7 +185,8 @@ def transform_weights(state: dict[str, torch.Tensor], shape: Qwen2Shape, tp_size
 def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: str = "qwen2",
                 weights_file: str = "", with_argmax: bool = True, fused_glu: bool = True,
                 logits_dtype: str | None = "float32",
-                residual_dtype: str | None = "float32", fused_exchange: bool = True) -> dict[str, Any]:
+                residual_dtype: str | None = "float32", fused_exchange: bool = True,
+                fused_qkv_rotary: bool = True) -> dict[str, Any]:
     """dli.graph.v1 dict for one rank. Inputs: input_ids [B,S] int64, positions [B]
     int64, rotary_cos/rotary_sin, and the weights of transform_weights() (made
     with the same `fused_glu`: one linear_silu_mul node instead of linear +
@@ -199,7 +200,10 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
     (None keeps the residual in the weights' dtype). With tensor parallelism,
     `fused_exchange` makes each row-split projection and the all-reduce + add +
     RMSNorm after it one `linear_all_reduce_add_rms_norm` node, whose decode
-    GEMM pushes its partial rows into the group's exchange buffers itself."""
+    GEMM pushes its partial rows into the group's exchange buffers itself.
+    `fused_qkv_rotary` makes the q|k|v projection and its rotary + KV-cache
+    write one `linear_qkv_rotary_cache` node (decode GEMMs rotate and scatter
+    in their epilogue)."""
     hq, hkv, d = shape.q_heads // tp_size, shape.kv_heads // tp_size, shape.head_dim
     nodes: list[dict[str, Any]] = []
 
@@ -233,11 +237,16 @@ def build_graph(shape: Qwen2Shape, capacity: int, tp_size: int = 1, model_type: 
             project_add_norm(f"{L}.input_layernorm", resid, pending[0], pending[1], f"{L}.ln_in",
                              [f"{L}.x", f"{L}.h_in"], pending[2], pending[3])
             resid = f"{L}.h_in"
-        node(f"{L}.qkv_proj", "linear", [f"{L}.x", f"{L}.wqkv", f"{L}.bqkv"], [f"{L}.qkv"])
-        node(f"{L}.rotary_cache", "qkv_rotary_cache",
-             [f"{L}.qkv", "rotary_cos", "rotary_sin", "positions"], [f"{L}.q"],
-             {"q_heads": hq, "kv_heads": hkv, "head_dim": d, "capacity": int(capacity),
-              "kv_cache": f"layer_{i}"})
+        rot_attrs = {"q_heads": hq, "kv_heads": hkv, "head_dim": d, "capacity": int(capacity),
+                     "kv_cache": f"layer_{i}"}
+        if fused_qkv_rotary:
+            node(f"{L}.qkv_proj", "linear_qkv_rotary_cache",
+                 [f"{L}.x", f"{L}.wqkv", f"{L}.bqkv", "rotary_cos", "rotary_sin", "positions"], [f"{L}.q"],
+                 rot_attrs)
+        else:
+            node(f"{L}.qkv_proj", "linear", [f"{L}.x", f"{L}.wqkv", f"{L}.bqkv"], [f"{L}.qkv"])
+            node(f"{L}.rotary_cache", "qkv_rotary_cache",
+                 [f"{L}.qkv", "rotary_cos", "rotary_sin", "positions"], [f"{L}.q"], rot_attrs)
         node(f"{L}.attention", "attention_kvcache", [f"{L}.q", "positions"], [f"{L}.attn"],
              {"kv_cache": f"layer_{i}"})
         project_add_norm(f"{L}.post_attention_layernorm", resid, f"{L}.attn", f"{L}.wo", f"{L}.ln_post",

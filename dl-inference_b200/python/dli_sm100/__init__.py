@@ -77,6 +77,7 @@ SIGNATURES = {
     "dli_sm100_allgather_argmax": (N, [P, D, D, D, I, I, D, P, I, I, I, P, I, D, P]),
     "dli_sm100_linear_exchange_push": (N, [P, P, P, I, I, I, D, P, D, D, I, I, P]),
     "dli_sm100_exchange_add_rms_norm_ex": (N, [P, D, D, D, I, I, P, P, P, P, I, I, I, F, I, D, D, P]),
+    "dli_sm100_linear_qkv_rotary_cache": (N, [P] * 9 + [I] * 9 + [D, P]),
 }
 
 _lib = None
@@ -380,6 +381,23 @@ def qkv_rotary_cache(qkv, cos, sin, positions, cache_k, cache_v, batch, seq, q_h
                                            q_heads, kv_heads, head_dim, cos.shape[1], cos.shape[0],
                                            cache_k.shape[2], _dt(qkv), _stream()),
           "qkv_rotary_cache")
+    return q_out
+
+
+def linear_qkv_rotary_cache(x, wqkv, bqkv, cos, sin, positions, cache_k, cache_v, batch, seq, q_heads, kv_heads,
+                            head_dim, q_out=None):
+    """The q|k|v projection with rotary + KV-cache write in its GEMM epilogue.
+    Returns q_out, or None when the shape is outside the fused path
+    (DLI_ERR_UNSUPPORTED: nothing launched)."""
+    _contig(x, wqkv, bqkv, cos, sin, positions, cache_k, cache_v)
+    q_out = q_out if q_out is not None else torch.empty(batch, seq, q_heads, head_dim, dtype=x.dtype, device=x.device)
+    st = lib().dli_sm100_linear_qkv_rotary_cache(
+        _ptr(x), _ptr(wqkv), _ptr(bqkv), _ptr(cos), _ptr(sin), _ptr(positions), _ptr(q_out), _ptr(cache_k),
+        _ptr(cache_v), batch, seq, x.shape[-1], q_heads, kv_heads, head_dim, cos.shape[1], cos.shape[0],
+        cache_k.shape[2], _dt(x), _stream())
+    if st == 2:  # DLI_ERR_UNSUPPORTED
+        return None
+    check(st, "linear_qkv_rotary_cache")
     return q_out
 
 

@@ -217,6 +217,21 @@ dli_status dli_sm100_qkv_rotary_cache(const void* qkv, const float* cos_table,
                                       int64_t head_dim, int64_t pairs, int64_t table_rows,
                                       int64_t capacity, dli_dtype dtype, void* stream);
 
+/* The q|k|v projection and dli_sm100_qkv_rotary_cache in one kernel (additive):
+ * qkv = x[B*S, k] . wqkv[(Hq+2Hkv)*D, k]^T + bqkv, rounded to dtype, then q
+ * rotated into q_out [B,S,Hq,D] and rotated k / raw v written into the cache
+ * rows positions[b] + s, bit-identical to linear followed by
+ * dli_sm100_qkv_rotary_cache (same tables, same error words for positions
+ * outside the table or the capacity). The qkv tensor is never written: the
+ * GEMM's split-K epilogue rotates and scatters. Serves decode-sized calls
+ * (B*S <= 128 on a split-K plan); other shapes return DLI_ERR_UNSUPPORTED
+ * without launching, and callers run the two-step form. */
+dli_status dli_sm100_linear_qkv_rotary_cache(const void* x, const void* wqkv, const void* bqkv, const float* cos_table,
+                                             const float* sin_table, const int64_t* positions, void* q_out,
+                                             void* cache_k, void* cache_v, int64_t batch, int64_t seq, int64_t k,
+                                             int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t pairs,
+                                             int64_t table_rows, int64_t capacity, dli_dtype dtype, void* stream);
+
 /* Attention over a KV cache with per-sequence lengths (additive). q/out are
  * [B,S,Hq,D] (token-major, the layout a linear emits); cache_k/v are
  * [B,Hkv,capacity,D]; sequence b sees keys [0, positions[b] + S) with the

@@ -80,6 +80,9 @@ class GraphOracle:
             return [x[0] if self.all_reduce is None else self.all_reduce(np.asarray(x[0]))]
         if op == "qkv_rotary_cache":
             return [self._qkv_rotary_cache(x, a)]
+        if op == "linear_qkv_rotary_cache":
+            # (x, wqkv, bqkv, cos, sin, positions): the projection, then rotary + cache write
+            return [self._qkv_rotary_cache([O.linear(x[0], x[1], x[2])] + list(x[3:]), a)]
         if op == "attention_kvcache":
             return [self._attention_kvcache(x, a)]
         if op in ("add", "mul", "silu", "relu", "softmax"):

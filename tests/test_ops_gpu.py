@@ -457,6 +457,53 @@ def test_qkv_rotary_cache_matches_oracle():
     assert ck[0, :, :3].abs().sum().item() == 0 and ck[0, :, 8:].abs().sum().item() == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("b,s,hq,hkv,d,k,pairs", [
+    (32, 1, 28, 4, 128, 3584, 64),   # 7B decode
+    (32, 1, 7, 1, 128, 3584, 64),    # 7B decode, TP 4 shard
+    (8, 1, 14, 2, 64, 896, 32),      # 0.5B decode (a 128-row tile spans two heads)
+    (64, 1, 8, 1, 128, 8192, 64),    # 72B decode, TP 8 shard
+    (16, 2, 28, 4, 128, 3584, 48),   # two tokens per sequence, partial rotary (48 of 64 pairs)
+])
+def test_linear_qkv_rotary_cache_matches_two_step(b, s, hq, hkv, d, k, pairs, dtype):
+    """The q|k|v projection with rotary + cache write in its GEMM epilogue against
+    linear followed by qkv_rotary_cache: q, and the cache rows of every
+    token, bit-identical; every other cache row untouched."""
+    import dli_sm100 as C
+
+    cap = 96
+    g = torch.Generator(device="cuda").manual_seed(b + s + hq + k)
+    x = torch.randn(b * s, k, device="cuda", generator=g).to(dtype)
+    w = (torch.randn((hq + 2 * hkv) * d, k, device="cuda", generator=g) * 0.02).to(dtype)
+    bias = (torch.randn((hq + 2 * hkv) * d, device="cuda", generator=g) * 0.02).to(dtype)
+    ang = torch.randn(cap, pairs, device="cuda", generator=g)
+    cos, sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()
+    positions = torch.randint(0, cap - s + 1, (b,), device="cuda", generator=g)
+    fill = torch.randn(b, hkv, cap, d, device="cuda", generator=g).to(dtype)
+    ck1, cv1, ck2, cv2 = fill.clone(), (fill * 2).clone(), fill.clone(), (fill * 2).clone()
+    q1 = C.linear_qkv_rotary_cache(x, w, bias, cos, sin, positions, ck1, cv1, b, s, hq, hkv, d)
+    assert q1 is not None, "decode shape expected on the fused path"
+    qkv = C.linear(x, w, bias)
+    q2 = C.qkv_rotary_cache(qkv, cos, sin, positions, ck2, cv2, b, s, hq, hkv, d)
+    C.check_device_error()
+    assert torch.equal(q1, q2)
+    assert torch.equal(ck1, ck2) and torch.equal(cv1, cv2)
+    assert not torch.equal(ck1, fill)  # the token rows were written
+
+
+def test_linear_qkv_rotary_cache_declines_prefill():
+    import dli_sm100 as C
+
+    b, s, hq, hkv, d, k, cap = 2, 300, 4, 2, 64, 256, 512
+    x = torch.randn(b * s, k, device="cuda").bfloat16()
+    w = (torch.randn((hq + 2 * hkv) * d, k, device="cuda") * 0.02).bfloat16()
+    bias = torch.zeros((hq + 2 * hkv) * d, device="cuda").bfloat16()
+    cos = torch.ones(cap, d // 2, device="cuda")
+    ck = torch.zeros(b, hkv, cap, d, device="cuda").bfloat16()
+    assert C.linear_qkv_rotary_cache(x, w, bias, cos, cos, torch.zeros(b, dtype=torch.int64, device="cuda"),
+                                     ck, ck.clone(), b, s, hq, hkv, d) is None
+
+
 def test_kv_append_is_a_sequence_concat():
     import dli_sm100 as C
 

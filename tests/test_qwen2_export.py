@@ -43,7 +43,7 @@ def test_interleaved_rotary_on_permuted_rows_equals_rotate_half():
 
 
 def test_graph_structure_per_layer():
-    g = build_graph(TINY, capacity=64, tp_size=1, fused_glu=False, residual_dtype=None)
+    g = build_graph(TINY, capacity=64, tp_size=1, fused_glu=False, residual_dtype=None, fused_qkv_rotary=False)
     ops = [n["op"] for n in g["nodes"]]
     assert ops[0] == "embedding"
     layer0 = ["rms_norm", "linear", "qkv_rotary_cache", "attention_kvcache", "linear", "add_rms_norm",
@@ -82,8 +82,13 @@ def test_graph_structure_per_layer():
     assert fx[1]["inputs"][1:3] == ["layers.0.act", "layers.0.wd"]
     assert fx[-1]["name"] == "norm" and fx[-1]["outputs"] == ["normed", "h_out"]
     assert len(g3["nodes"]) == len(g2["nodes"]) - 2 * TINY.layers
-    rc = next(n for n in g2["nodes"] if n["op"] == "qkv_rotary_cache")
+    rc = next(n for n in g2["nodes"] if n["op"] == "linear_qkv_rotary_cache")
     assert rc["attrs"]["q_heads"] == 2 and rc["attrs"]["kv_heads"] == 1
+    # fused q|k|v projection + rotary + cache write (default): one node per layer
+    qr = [n for n in gf["nodes"] if n["op"] == "linear_qkv_rotary_cache"]
+    assert len(qr) == TINY.layers and "qkv_rotary_cache" not in [n["op"] for n in gf["nodes"]]
+    assert qr[0]["inputs"] == ["layers.0.x", "layers.0.wqkv", "layers.0.bqkv", "rotary_cos", "rotary_sin",
+                               "positions"] and qr[0]["outputs"] == ["layers.0.q"]
 
 
 def test_tensor_parallel_shards_recompose():
