@@ -32,6 +32,12 @@ bool fmha_supported(const FmhaArgs& a, dli_dtype dtype);
 // is an error instead of a launch of the mma.sync kernel.
 bool fmha_required();
 
+// 4-D bf16/f16 tensor map: dims[0] innermost (contiguous), byte strides of
+// dims 1..3, 128-byte swizzle, elements outside the dims read as zero. Returns
+// DLI_ERR_UNSUPPORTED when the encoder rejects the layout.
+dli_status make_map_4d(CUtensorMap* map, const void* base, bool bf16, const uint64_t (&dims)[4],
+                       const uint64_t (&strides)[3], const uint32_t (&box)[4]);
+
 // Launches the kernel on `stream` (fmha_supported() must hold). Returns
 // DLI_ERR_UNSUPPORTED, launching nothing, when a tensor map cannot be encoded.
 dli_status run_fmha_prefill(const FmhaArgs& a, dli_dtype dtype, cudaStream_t stream);

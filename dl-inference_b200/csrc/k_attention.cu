@@ -27,6 +27,7 @@
 //    graphs (the reference dtype) and head dims the MMA kernels do not cover.
 #include <algorithm>
 #include <cfloat>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -60,6 +61,7 @@ struct AttnArgs {
   int splits;
   float* part_o;    // [B, Hkv, splits, 16, D]
   float* part_ml;   // [B, Hkv, splits, 16, 2]
+  unsigned* err;    // device error word (bounded waits, cache capacity)
 };
 
 __device__ __forceinline__ int kv_len_of(const AttnArgs& a, int b) {
@@ -549,24 +551,46 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
 }
 __device__ __forceinline__ void ldsm_x4_a(uint32_t (&r)[4], uint32_t addr) { ldsm_x4(r, addr); }
 
-template <typename T, int D, int STAGES>
+// TMA: K/V blocks arrive by tensor-map copies (one elected thread, per-stage
+// full/empty mbarriers, no CTA barrier inside the key loop) into D/64 boxes of
+// [64 keys][64 elements] with the 128-byte swizzle; otherwise every thread
+// issues 16-byte cp.async into row-major swizzled tiles.
+template <typename T, int D, int STAGES, bool TMA>
 struct DecodeClusterSmem {
   static constexpr int kRing = 2 * STAGES * 64 * D * 2;     // K and V stages
   static constexpr int kQ = 8 * D * 2;                      // swizzled Q rows
   static constexpr int kWarpO = 4 * 8 * D * 4;              // per-warp scaled O^T (aliases the ring)
   static constexpr int kState = 8 * D * 4 + 2 * 8 * 4;      // merged O [8][D], m[8], l[8]
   static constexpr int kWarpML = 2 * 4 * 8 * 4;             // per-warp m, l
-  static constexpr int kBytes = kRing + kQ + kState + kWarpML;
+  static constexpr int kBarOff = kRing + kQ + kState + kWarpML;
+  static constexpr int kBars = TMA ? 2 * STAGES * 8 : 0;   // full[STAGES], empty[STAGES]
+  static constexpr int kSlack = TMA ? 1024 : 0;             // ring base rounded up to 1 KiB
+  static constexpr int kBytes = kBarOff + kBars + kSlack;
   static_assert(kWarpO <= kRing, "warp partials alias the K/V ring");
+  static_assert(kBarOff % 8 == 0, "mbarrier alignment");
 };
 
-template <typename T, int D, int STAGES>
+// Element offset of (key row, column) in one K or V stage.
+template <int D, bool TMA>
+__device__ __forceinline__ int kv_swz(int row, int col) {
+  if constexpr (TMA)
+    return (col >> 6) * (64 * 64) + row * 64 + ((((col >> 3) & 7) ^ (row & 7)) << 3) + (col & 7);
+  else
+    return swz<D>(row, col);
+}
+
+template <typename T, int D, int STAGES, bool TMA>
 __global__ void __launch_bounds__(128)
-    attn_decode_cluster_kernel(const AttnArgs a) {
+    attn_decode_cluster_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap tk,
+                               const __grid_constant__ CUtensorMap tv) {
   DLI_PDL_ENTRY();
-  using L = DecodeClusterSmem<T, D, STAGES>;
+  using L = DecodeClusterSmem<T, D, STAGES, TMA>;
   constexpr int BN = 64;
-  extern __shared__ __align__(16) uint8_t smem_raw[];
+  extern __shared__ __align__(16) uint8_t smem_base[];
+  // the same offset in every CTA of the launch, so DSMEM addresses still map rank to rank
+  uint8_t* smem_raw = TMA ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_base) + 1023) &
+                                                       ~static_cast<uintptr_t>(1023))
+                          : smem_base;
   T* sk = reinterpret_cast<T*>(smem_raw);                       // [STAGES][BN*D]
   T* sv = sk + STAGES * BN * D;                                  // [STAGES][BN*D]
   T* sq = reinterpret_cast<T*>(smem_raw + L::kRing);            // [8][D] swizzled
@@ -581,7 +605,14 @@ __global__ void __launch_bounds__(128)
   const int nsplit = gridDim.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int kv_len = kv_len_of(a, b);
+  int kv_len = kv_len_of(a, b);
+  if constexpr (TMA) {
+    const int64_t cap = a.k_sh / D;  // cache rows per head (the tensor maps' row extent)
+    if (kv_len > cap) {
+      if (threadIdx.x == 0) set_device_error(a.err, kDevErrKvCapacity);
+      kv_len = static_cast<int>(cap);
+    }
+  }
   const int off = kv_len - a.seq_q;
   const int rows = a.group * a.seq_q;  // <= 8
   const int total_blocks = (kv_len + BN - 1) / BN;
@@ -591,6 +622,31 @@ __global__ void __launch_bounds__(128)
 
   const T* kbase = static_cast<const T*>(a.k) + b * a.k_sb + kvh * a.k_sh;
   const T* vbase = static_cast<const T*>(a.v) + b * a.k_sb + kvh * a.k_sh;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + L::kBarOff);  // TMA only
+  uint64_t* empty = full + STAGES;
+  // K and V of block j (of this split) into stage st, completing on full[st]
+  auto issue_kv = [&](int j, int st) {
+    mbar_arrive_expect_tx(&full[st], 2 * BN * D * 2);
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c) {
+      tma_load_4d(sk + st * BN * D + c * 64 * 64, &tk, c * 64, (blk0 + j) * BN, kvh, b, &full[st]);
+      tma_load_4d(sv + st * BN * D + c * 64 * 64, &tv, c * 64, (blk0 + j) * BN, kvh, b, &full[st]);
+    }
+  };
+  int issued = 0;      // thread 0: K/V blocks issued by TMA
+  bool refill = true;  // thread 0: cleared when a stage was never released
+  if constexpr (TMA) {
+    if (threadIdx.x == 0) {
+      for (int st = 0; st < STAGES; ++st) {
+        mbar_init(&full[st], 1);
+        mbar_init(&empty[st], 4);  // one arrival per warp
+      }
+      mbar_fence_init();
+      tma_prefetch_desc(&tk);
+      tma_prefetch_desc(&tv);
+      for (; issued < STAGES && issued < nblocks; ++issued) issue_kv(issued, issued);
+    }
+  }
 
   // Q rows r -> (token s = r / group, head kvh*group + r % group); rows >= `rows` zero
   {
@@ -603,13 +659,19 @@ __global__ void __launch_bounds__(128)
       cp_async16(s0 + swz<D>(r, ch * 8) * 2, qb + hh * a.q_sh + qs * a.q_ss + ch * 8, valid);
     }
   }
+  if constexpr (TMA) {
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();  // Q and the initialised barriers are visible to every warp
+  } else {
 #pragma unroll
-  for (int st = 0; st < STAGES - 1; ++st) {
-    if (st < nblocks) {
-      load_tile<T, D, BN, 128>(sk + st * BN * D, kbase, (blk0 + st) * BN, kv_len);
-      load_tile<T, D, BN, 128>(sv + st * BN * D, vbase, (blk0 + st) * BN, kv_len);
+    for (int st = 0; st < STAGES - 1; ++st) {
+      if (st < nblocks) {
+        load_tile<T, D, BN, 128>(sk + st * BN * D, kbase, (blk0 + st) * BN, kv_len);
+        load_tile<T, D, BN, 128>(sv + st * BN * D, vbase, (blk0 + st) * BN, kv_len);
+      }
+      cp_async_commit();  // the first group also carries Q
     }
-    cp_async_commit();  // the first group also carries Q
   }
 
   // query token of the thread's two score columns (rows 2t, 2t+1), for the causal mask
@@ -624,15 +686,24 @@ __global__ void __launch_bounds__(128)
   const int kw = warp * 16;  // this warp's 16 keys of every block
 
   for (int it = 0; it < nblocks; ++it) {
-    const int pre = it + STAGES - 1;
-    if (pre < nblocks) {
-      const int st = pre % STAGES;
-      load_tile<T, D, BN, 128>(sk + st * BN * D, kbase, (blk0 + pre) * BN, kv_len);
-      load_tile<T, D, BN, 128>(sv + st * BN * D, vbase, (blk0 + pre) * BN, kv_len);
+    if constexpr (TMA) {
+      // every lane observes the phase, then the warp agrees (uniform exit)
+      const bool got = mbar_wait(&full[it % STAGES], (it / STAGES) & 1);
+      if (!__all_sync(0xffffffffu, got)) {
+        if (lane == 0) set_device_error(a.err, kDevErrAttentionTimeout);
+        break;
+      }
+    } else {
+      const int pre = it + STAGES - 1;
+      if (pre < nblocks) {
+        const int st = pre % STAGES;
+        load_tile<T, D, BN, 128>(sk + st * BN * D, kbase, (blk0 + pre) * BN, kv_len);
+        load_tile<T, D, BN, 128>(sv + st * BN * D, vbase, (blk0 + pre) * BN, kv_len);
+      }
+      cp_async_commit();
+      cp_async_wait<STAGES - 1>();
+      __syncthreads();
     }
-    cp_async_commit();
-    cp_async_wait<STAGES - 1>();
-    __syncthreads();
     if (it == 0) {
       // Q^T B fragments: ldmatrix of the [8 rows][16 dims] slices
       const uint32_t qa = static_cast<uint32_t>(__cvta_generic_to_shared(sq));
@@ -655,7 +726,7 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       uint32_t af[4];
-      ldsm_x4_a(af, ks + swz<D>(kw + (lane & 7) + ((lane >> 3) & 1) * 8, kk * 16 + (lane >> 4) * 8) * 2);
+      ldsm_x4_a(af, ks + kv_swz<D, TMA>(kw + (lane & 7) + ((lane >> 3) & 1) * 8, kk * 16 + (lane >> 4) * 8) * 2);
       mma16816<T>(sc, af, qf[kk][0], qf[kk][1]);
     }
     const int key0 = (blk0 + it) * BN + kw + g, key1 = key0 + 8;
@@ -694,15 +765,53 @@ __global__ void __launch_bounds__(128)
     // P^T as the B operand: transpose the two 8x8 accumulator blocks
     const uint32_t pb0 = movmatrix_t(pack2<T>(p00, p01));
     const uint32_t pb1 = movmatrix_t(pack2<T>(p10, p11));
+    if constexpr (TMA) {
+      // V rows of keys >= kv_len hold whatever the cache had there (the copy
+      // is not clipped to the sequence): zero this warp's rows so a stale
+      // non-finite value cannot reach O through a zero weight
+      const int kfirst = (blk0 + it) * BN + kw;
+      if (kfirst + 16 > kv_len) {
+        T* vt = sv + (it % STAGES) * BN * D;
+        for (int c = lane; c < 16 * (D / 8); c += 32) {
+          const int r = c / (D / 8), ch = c - r * (D / 8);
+          if (kfirst + r >= kv_len)
+            *reinterpret_cast<uint4*>(vt + kv_swz<D, TMA>(kw + r, ch * 8)) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        __syncwarp();
+      }
+    }
 #pragma unroll
     for (int mt = 0; mt < D / 16; ++mt) {
       uint32_t va[4];
-      ldsm_x4_t(va, vs + swz<D>(kw + (lane & 7) + (lane >> 4) * 8, mt * 16 + ((lane >> 3) & 1) * 8) * 2);
+      ldsm_x4_t(va, vs + kv_swz<D, TMA>(kw + (lane & 7) + (lane >> 4) * 8, mt * 16 + ((lane >> 3) & 1) * 8) * 2);
       mma16816<T>(o[mt], va, pb0, pb1);
     }
-    __syncthreads();
+    if constexpr (TMA) {
+      const int st = it % STAGES;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
+      if (threadIdx.x == 0 && refill && issued < nblocks) {
+        // refill the stage once all four warps have released it
+        if (mbar_wait(&empty[st], (it / STAGES) & 1)) {
+          issue_kv(issued, st);
+          ++issued;
+        } else {
+          set_device_error(a.err, kDevErrAttentionTimeout);
+          refill = false;
+        }
+      }
+      __syncwarp();
+    } else {
+      __syncthreads();
+    }
   }
-  cp_async_wait<0>();
+  if constexpr (TMA) {
+    // no copy may still be writing the ring when it becomes the partial area
+    if (threadIdx.x == 0)
+      for (int j = max(0, issued - STAGES); j < issued; ++j) mbar_wait(&full[j % STAGES], (j / STAGES) & 1);
+  } else {
+    cp_async_wait<0>();
+  }
   __syncthreads();  // the ring becomes the warp-partial area
 
   // merge the 4 warps (fixed order)
@@ -1460,10 +1569,16 @@ struct DecodePlan {
 // K/V stages of the cluster decode kernel: 3 (two CTAs per SM at D = 128) or 2.
 static const int kClusterStages = tuning_knob("ATTN_CLUSTER_STAGES", 3) == 2 ? 2 : 3;
 
+// DLI_SM100_ATTN_DECODE_TMA: 1 K/V blocks of the cluster decode kernel by TMA
+// with mbarrier stages; 0 (default) by cp.async with a CTA barrier per block.
+// Measured at the Qwen2-7B decode shape (B 32, context 2304): 31.2 us by TMA
+// against 30.2 us by cp.async, so the barrier per block is not what bounds it.
+static const bool kDecodeTma = tuning_knob("ATTN_DECODE_TMA", 0) != 0;
+
 template <int D, int STAGES>
 int cluster_decode_occupancy(int cluster) {
-  using L = DecodeClusterSmem<__nv_bfloat16, D, STAGES>;
-  auto kern = attn_decode_cluster_kernel<__nv_bfloat16, D, STAGES>;
+  using L = DecodeClusterSmem<__nv_bfloat16, D, STAGES, true>;  // the larger of the two layouts
+  auto kern = attn_decode_cluster_kernel<__nv_bfloat16, D, STAGES, true>;
   if (ensure_smem(reinterpret_cast<const void*>(kern), L::kBytes, "attention decode") != DLI_OK) return 0;
   int n = 0;
   if (cluster <= 1) {
@@ -1559,17 +1674,42 @@ dli_status launch_decode(const AttnArgs& args, const DecodePlan& plan, cudaStrea
   return DLI_OK;
 }
 
+// The K/V tensor maps of the TMA decode kernel: 4-D [batch, Hkv, cache rows, D]
+// with 64-key x 64-element boxes. False (and the cp.async kernel serves the
+// call) when the layout is outside what a map can describe.
+template <int D>
+bool decode_kv_maps(const AttnArgs& a, bool bf16, CUtensorMap* tk, CUtensorMap* tv) {
+  if (a.k_sh % D != 0 || a.k_sh % 8 != 0 || a.k_sb % 8 != 0 || a.k_sb < a.k_sh) return false;
+  const int64_t rows = a.k_sh / D;
+  if (rows < 1 || rows > (1ll << 30)) return false;
+  const uint64_t dims[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(rows), static_cast<uint64_t>(a.hkv),
+                            static_cast<uint64_t>(a.batch)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(D * 2), static_cast<uint64_t>(a.k_sh * 2),
+                               static_cast<uint64_t>(a.k_sb * 2)};
+  const uint32_t box[4] = {64u, 64u, 1u, 1u};
+  if (make_map_4d(tk, a.k, bf16, dims, strides, box) != DLI_OK) return false;
+  if (make_map_4d(tv, a.v, bf16, dims, strides, box) != DLI_OK) return false;
+  return true;
+}
+
 template <typename T, int D, int STAGES>
 dli_status launch_decode_cluster(const AttnArgs& args, const DecodePlan& plan, cudaStream_t stream) {
-  using L = DecodeClusterSmem<T, D, STAGES>;
-  auto kern = attn_decode_cluster_kernel<T, D, STAGES>;
-  const dli_status st = ensure_smem(reinterpret_cast<const void*>(kern), L::kBytes, "attention decode");
+  CUtensorMap tk, tv;
+  const bool tma = kDecodeTma && decode_kv_maps<D>(args, std::is_same<T, __nv_bfloat16>::value, &tk, &tv);
+  if (!tma) {
+    std::memset(&tk, 0, sizeof(tk));
+    std::memset(&tv, 0, sizeof(tv));
+  }
+  const unsigned smem =
+      tma ? DecodeClusterSmem<T, D, STAGES, true>::kBytes : DecodeClusterSmem<T, D, STAGES, false>::kBytes;
+  auto kern = tma ? attn_decode_cluster_kernel<T, D, STAGES, true> : attn_decode_cluster_kernel<T, D, STAGES, false>;
+  const dli_status st = ensure_smem(reinterpret_cast<const void*>(kern), smem, "attention decode");
   if (st != DLI_OK) return st;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(plan.splits), static_cast<unsigned>(args.hkv),
                      static_cast<unsigned>(args.batch));
   cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   unsigned n = 0;
@@ -1587,7 +1727,7 @@ dli_status launch_decode_cluster(const AttnArgs& args, const DecodePlan& plan, c
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  cudaLaunchKernelEx(&cfg, kern, args);
+  cudaLaunchKernelEx(&cfg, kern, args, tk, tv);
   return check_launch("attention decode");
 }
 
@@ -1663,6 +1803,7 @@ dli_status run_attention(AttnArgs& args, dli_dtype dtype, int64_t max_kv, void* 
       args.part_ml = args.part_o + static_cast<int64_t>(args.batch) * args.hkv * plan.splits * 16 * args.head_dim;
     }
     args.splits = plan.splits;
+    args.err = device_error_word();
     if (dtype == DLI_DTYPE_BF16)
       return args.head_dim == 64 ? launch_tc_attention<__nv_bfloat16, 64>(args, plan, stream)
                                  : launch_tc_attention<__nv_bfloat16, 128>(args, plan, stream);

@@ -19,9 +19,11 @@
 //              on the tensor pipe while the softmax warps work on the current one;
 //   warps 2-5  softmax, one thread per query row (its TMEM lane): read the S row
 //              (tcgen05.ld), mask, online max/sum in fp32, write P = exp2(S*scale
-//              - m) as bf16/f16 into a 128-byte-swizzled shared tile (the A
-//              operand of O += P V), and at the end read O, divide by the row
-//              sum and store it.
+//              - m) as bf16/f16 (the A operand of O += P V) back over the first
+//              half of the same S buffer with tcgen05.st (or, with the P-in-shared
+//              variant, into a 128-byte-swizzled shared tile), and at the end
+//              read O, divide by the row sum, write it over the Q tile in
+//              shared memory and store the tile with TMA.
 // The running maximum is only moved when a block raises it by more than 8
 // (log2 units): until then P values up to 2^8 are accumulated against the old
 // maximum, which is exact in fp32 and in the bf16/f16 range, so O in TMEM is
@@ -31,9 +33,11 @@
 // Synchronisation (all mbarriers, every wait bounded; a timeout sets the device
 // error word and winds the CTA down): q_full; k_full/k_empty and v_full/v_empty
 // per ring stage; s_full (MMA commit) and s_empty (4 softmax warps) per S
-// buffer; p_full (4 softmax warps) for the single P tile; o_done (MMA commit
-// after each P V): the softmax warps wait for it before they rewrite the P tile
-// or rescale O, so P V_{j-1} has consumed the tile before P_j overwrites it.
+// buffer; p_full (4 softmax warps) per P; o_done (MMA commit after each P V):
+// the softmax warps wait for it before they rescale O (and, with P in shared
+// memory, before they rewrite the single P tile). A P in tensor memory needs
+// no such wait: P_j sits in S_j's buffer, and S_{j+2}, the next write there,
+// is issued after P_j V_j, which the tensor pipe executes first.
 //
 // Keys at or past a sequence's length are masked; V rows past the length that
 // exist in memory (stale cache rows) are zeroed in shared memory before the
@@ -55,17 +59,20 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 2^8 before O is r
 // per block 128: one CTA per SM (230 KB, all 512 TMEM columns). Keys per block
 // 64: two CTAs per SM (<= 113 KB and 256 TMEM columns each), so one CTA's
 // prologue, epilogue and softmax latency overlap the other's MMAs.
-template <int D, int BN_>
+// PT: P goes to tensor memory over the S buffer it was computed from (the A
+// operand of O += P V read from TMEM), which frees the shared P tile for a
+// third K stage (64-key blocks) or V stage (128-key blocks).
+template <int D, int BN_, bool PT>
 struct FmhaLayout {
   static constexpr int BM = 128;  // query rows per CTA (tcgen05 M)
   static constexpr int BN = BN_;  // keys per block
   static constexpr int kCtasPerSm = BN_ == 64 ? 2 : 1;
-  static constexpr int KST = BN_ == 128 ? 3 : (D == 128 ? 2 : 3);
-  static constexpr int VST = BN_ == 128 ? (D == 128 ? 2 : 3) : 2;
+  static constexpr int KST = BN_ == 128 ? 3 : ((D == 128 && !PT) ? 2 : 3);
+  static constexpr int VST = BN_ == 128 ? ((D == 128 && !PT) ? 2 : 3) : 2;
   static constexpr int kBox = 128 * 128;                   // one 128-row x 64-element box
   static constexpr int kQBytes = (D / 64) * kBox;
   static constexpr int kKVBytes = (D / 64) * BN * 128;     // one K or V block
-  static constexpr int kPBytes = (BN / 64) * kBox;
+  static constexpr int kPBytes = PT ? 0 : (BN / 64) * kBox;
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQBytes;
   static constexpr int kVOff = kKOff + KST * kKVBytes;
@@ -90,7 +97,7 @@ struct FmhaLayout {
 struct FmhaParams {
   void* out;
   int64_t o_sb, o_sh, o_ss;
-  int seq_q, kv_rows, dense_kv, group, causal, q_s_inner;
+  int seq_q, kv_rows, dense_kv, group, causal, q_s_inner, o_s_inner;
   const int64_t* positions;
   float scale_log2;
   unsigned* err;
@@ -126,11 +133,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, done && *abort_flag == 0);
 }
 
-template <typename T, int D, int BNK>
-__global__ void __launch_bounds__(kFmhaThreads, FmhaLayout<D, BNK>::kCtasPerSm)
+template <typename T, int D, int BNK, bool PT>
+__global__ void __launch_bounds__(kFmhaThreads, FmhaLayout<D, BNK, PT>::kCtasPerSm)
     fmha_prefill_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                        const __grid_constant__ CUtensorMap tv, const FmhaParams p) {
-  using L = FmhaLayout<D, BNK>;
+                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
+                        const FmhaParams p) {
+  using L = FmhaLayout<D, BNK, PT>;
   constexpr int BM = L::BM, BN = L::BN, KST = L::KST, VST = L::VST;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
@@ -183,6 +191,7 @@ __global__ void __launch_bounds__(kFmhaThreads, FmhaLayout<D, BNK>::kCtasPerSm)
     tma_prefetch_desc(&tq);
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
+    tma_prefetch_desc(&to);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, L::kTmemCols);
@@ -280,9 +289,16 @@ __global__ void __launch_bounds__(kFmhaThreads, FmhaLayout<D, BNK>::kCtasPerSm)
         const uint32_t v_addr = smem_u32(smem + L::kVOff + s * L::kKVBytes);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t ad = umma_desc_sw128(p_addr + (kk / 4) * L::kBox) + 2 * (kk % 4);
           const uint64_t bd = umma_desc_mn_sw128(v_addr + kk * 16 * 128, BN * 128, 1024);
-          umma_f16(tmem + L::kOCol, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          if constexpr (PT) {
+            // P_j over S_j's columns; the MMAs run in issue order, so S_{j+2}
+            // (issued after this) cannot overwrite it before it is read
+            umma_f16_ts(tmem + L::kOCol, tmem + static_cast<uint32_t>((j & 1) * BN + kk * 8), bd, idesc_o,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+          } else {
+            const uint64_t ad = umma_desc_sw128(p_addr + (kk / 4) * L::kBox) + 2 * (kk % 4);
+            umma_f16(tmem + L::kOCol, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         umma_commit(&v_empty[s]);
         umma_commit(o_done);
@@ -390,8 +406,9 @@ __global__ void __launch_bounds__(kFmhaThreads, FmhaLayout<D, BNK>::kCtasPerSm)
         pk[i / 2] = pack_pair<T>(p0, p1);
       }
       l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
-      // P V_{j-1} must have consumed the P tile before it is rewritten
-      if (j > 0 && !waited) {
+      // P V_{j-1} must have consumed the shared P tile before it is rewritten
+      // (a TMEM P goes over S_j, which no MMA reads)
+      if (!PT && j > 0 && !waited) {
         if (!warp_wait(o_done, (j - 1) & 1, abort_flag)) {
           ok = false;
           break;
@@ -414,8 +431,16 @@ __global__ void __launch_bounds__(kFmhaThreads, FmhaLayout<D, BNK>::kCtasPerSm)
           }
         }
       }
-      // P row into the 128-byte-swizzled K-major tile (two 64-key boxes)
-      {
+      if constexpr (PT) {
+        // P row into this lane's S_j columns: BN 16-bit values in BN / 2 columns
+#pragma unroll
+        for (int c = 0; c < BN / 64; ++c)
+          tmem_st_32x32b_x32(lane_base + static_cast<uint32_t>(sb * BN + c * 32),
+                             *reinterpret_cast<const uint32_t(*)[32]>(&pk[c * 32]));
+        tmem_st_wait();
+        if (j == nblocks - 1) fence_proxy_async_smem();  // the zeroed V rows
+      } else {
+        // P row into the 128-byte-swizzled K-major tile (two 64-key boxes)
         uint8_t* prow = p_tile + row * 128;
         const int r7 = row & 7;
 #pragma unroll
@@ -424,47 +449,61 @@ __global__ void __launch_bounds__(kFmhaThreads, FmhaLayout<D, BNK>::kCtasPerSm)
           *reinterpret_cast<uint4*>(prow + box * L::kBox + ((cc ^ r7) << 4)) =
               make_uint4(pk[c * 4], pk[c * 4 + 1], pk[c * 4 + 2], pk[c * 4 + 3]);
         }
+        fence_proxy_async_smem();
       }
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (!ok) {
-      if (lane == 0) {
-        set_device_error(p.err, kDevErrAttentionTimeout);
-        *abort_flag = 1;
-      }
-    } else {
-      if (nblocks > 0 && !warp_wait(o_done, (nblocks - 1) & 1, abort_flag)) {
-        if (lane == 0) set_device_error(p.err, kDevErrAttentionTimeout);
-      } else {
-        tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        T* dst = static_cast<T*>(p.out) + b * p.o_sb + h * p.o_sh + static_cast<int64_t>(qrow) * p.o_ss;
+    if (!ok && lane == 0) {
+      set_device_error(p.err, kDevErrAttentionTimeout);
+      *abort_flag = 1;
+    }
+    // O / l as T into the Q tile's shared memory (the last Q K^T has completed),
+    // in the same 128-byte-swizzled boxes, then one thread stores the tile by
+    // TMA (rows past the sequence are outside the map and are not written).
+    // Every softmax warp takes this path, abort or not, so the named barrier
+    // below always completes.
+    bool have_o = ok && nblocks > 0;
+    if (have_o && !warp_wait(o_done, (nblocks - 1) & 1, abort_flag)) {
+      if (lane == 0) set_device_error(p.err, kDevErrAttentionTimeout);
+      have_o = false;
+    }
+    tc_fence_after();
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    uint8_t* orow = smem + L::kQOff + row * 128;
+    const int r7 = row & 7;
 #pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
-          uint32_t r[32];
-          if (nblocks > 0) {
-            tmem_ld_32x32b_x32(lane_base + L::kOCol + c, r);
-            tmem_ld_wait();
-          } else {
+    for (int c = 0; c < D; c += 32) {
+      uint32_t r[32];
+      if (have_o) {
+        tmem_ld_32x32b_x32(lane_base + L::kOCol + c, r);
+        tmem_ld_wait();
+      } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = 0u;
-          }
-          if (qrow < p.seq_q) {
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              uint4 v;
-              v.x = pack_pair<T>(__uint_as_float(r[q4 * 8 + 0]) * inv, __uint_as_float(r[q4 * 8 + 1]) * inv);
-              v.y = pack_pair<T>(__uint_as_float(r[q4 * 8 + 2]) * inv, __uint_as_float(r[q4 * 8 + 3]) * inv);
-              v.z = pack_pair<T>(__uint_as_float(r[q4 * 8 + 4]) * inv, __uint_as_float(r[q4 * 8 + 5]) * inv);
-              v.w = pack_pair<T>(__uint_as_float(r[q4 * 8 + 6]) * inv, __uint_as_float(r[q4 * 8 + 7]) * inv);
-              *reinterpret_cast<uint4*>(dst + c + q4 * 8) = v;
-            }
-          }
-        }
+        for (int i = 0; i < 32; ++i) r[i] = 0u;
       }
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint4 v;
+        v.x = pack_pair<T>(__uint_as_float(r[q4 * 8 + 0]) * inv, __uint_as_float(r[q4 * 8 + 1]) * inv);
+        v.y = pack_pair<T>(__uint_as_float(r[q4 * 8 + 2]) * inv, __uint_as_float(r[q4 * 8 + 3]) * inv);
+        v.z = pack_pair<T>(__uint_as_float(r[q4 * 8 + 4]) * inv, __uint_as_float(r[q4 * 8 + 5]) * inv);
+        v.w = pack_pair<T>(__uint_as_float(r[q4 * 8 + 6]) * inv, __uint_as_float(r[q4 * 8 + 7]) * inv);
+        const int ch = ((c & 63) >> 3) + q4;  // 16-byte chunk of the 128-byte box row
+        *reinterpret_cast<uint4*>(orow + (c >> 6) * L::kBox + ((ch ^ r7) << 4)) = v;
+      }
+    }
+    fence_proxy_async_smem();
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four softmax warps
+    if (warp == 2 && lane == 0) {
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        if (p.o_s_inner) tma_store_4d(&to, smem + L::kQOff + c * L::kBox, c * 64, m0, h, b);
+        else tma_store_4d(&to, smem + L::kQOff + c * L::kBox, c * 64, h, m0, b);
+      }
+      bulk_commit();
+      bulk_wait_read();  // the tile stays in shared memory until the copy has read it
     }
   }
   tc_fence_before();
@@ -496,6 +535,8 @@ EncodeTiledFn encode_tiled() {
   return fn;
 }
 
+}  // namespace
+
 // 4-D map, dims[0] innermost (contiguous), strides in bytes for dims 1..3,
 // 128-byte swizzle, out-of-range elements read as zero.
 dli_status make_map_4d(CUtensorMap* map, const void* base, bool bf16, const uint64_t (&dims)[4],
@@ -516,11 +557,13 @@ dli_status make_map_4d(CUtensorMap* map, const void* base, bool bf16, const uint
   return DLI_OK;
 }
 
-template <typename T, int D, int BNK>
+namespace {
+
+template <typename T, int D, int BNK, bool PT>
 dli_status launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
-  using L = FmhaLayout<D, BNK>;
+  using L = FmhaLayout<D, BNK, PT>;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   const bool s_inner = a.q_ss <= a.q_sh;
   const uint64_t qd[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(s_inner ? a.seq_q : a.hq),
                           static_cast<uint64_t>(s_inner ? a.hq : a.seq_q), static_cast<uint64_t>(a.batch)};
@@ -550,15 +593,26 @@ dli_status launch_fmha(const FmhaArgs& a, cudaStream_t stream) {
   p.group = a.hq / a.hkv;
   p.causal = a.causal;
   p.q_s_inner = s_inner ? 1 : 0;
+  // the output tile goes out through its own map (the output may be laid out
+  // differently from q)
+  const bool o_inner = a.o_ss <= a.o_sh;
+  const uint64_t od[4] = {static_cast<uint64_t>(D), static_cast<uint64_t>(o_inner ? a.seq_q : a.hq),
+                          static_cast<uint64_t>(o_inner ? a.hq : a.seq_q), static_cast<uint64_t>(a.batch)};
+  const uint64_t os[3] = {static_cast<uint64_t>((o_inner ? a.o_ss : a.o_sh) * 2),
+                          static_cast<uint64_t>((o_inner ? a.o_sh : a.o_ss) * 2), static_cast<uint64_t>(a.o_sb * 2)};
+  const uint32_t ob[4] = {64u, o_inner ? 128u : 1u, o_inner ? 1u : 128u, 1u};
+  st = make_map_4d(&to, a.out, kBf16, od, os, ob);
+  if (st != DLI_OK) return st;
+  p.o_s_inner = o_inner ? 1 : 0;
   p.positions = a.positions;
   p.scale_log2 = a.scale_log2;
   p.err = device_error_word();
-  auto kern = fmha_prefill_kernel<T, D, BNK>;
+  auto kern = fmha_prefill_kernel<T, D, BNK, PT>;
   st = ensure_smem(reinterpret_cast<const void*>(kern), L::kBytes, "attention prefill (tcgen05)");
   if (st != DLI_OK) return st;
   dim3 grid(static_cast<unsigned>(ceil_div(a.seq_q, L::BM)), static_cast<unsigned>(a.hq),
             static_cast<unsigned>(a.batch));
-  launch_pdl(kern, grid, dim3(kFmhaThreads), L::kBytes, stream, tq, tk, tv, p);
+  launch_pdl(kern, grid, dim3(kFmhaThreads), L::kBytes, stream, tq, tk, tv, to, p);
   return check_launch("attention prefill (tcgen05)");
 }
 
@@ -587,8 +641,9 @@ bool fmha_supported(const FmhaArgs& a, dli_dtype dtype) {
     if (s <= 0 || s % 8 != 0) return false;
   if (a.k_sh % a.head_dim != 0) return false;
   // the batch stride is the outermost (4-D maps list dims by increasing stride)
-  if (a.q_sb < std::max(a.q_sh, a.q_ss) || a.k_sb < a.k_sh) return false;
-  if (std::min(a.q_sh, a.q_ss) < a.head_dim || a.k_sh / a.head_dim < 1) return false;
+  if (a.q_sb < std::max(a.q_sh, a.q_ss) || a.o_sb < std::max(a.o_sh, a.o_ss) || a.k_sb < a.k_sh) return false;
+  if (std::min(a.q_sh, a.q_ss) < a.head_dim || std::min(a.o_sh, a.o_ss) < a.head_dim || a.k_sh / a.head_dim < 1)
+    return false;
   if (a.k_sh / a.head_dim > (1ll << 30)) return false;
   return true;
 }
@@ -601,16 +656,26 @@ static int fmha_block_keys() {
   return bn;
 }
 
-template <int BNK>
+// DLI_SM100_ATTN_FMHA_P: where P = exp2(S * scale - m) is staged for O += P V:
+// 1 (default) tensor memory, over the S buffer; 0 a swizzled shared-memory tile.
+static bool fmha_p_in_tmem() {
+  static const bool tm = tuning_knob("ATTN_FMHA_P", 1) != 0;
+  return tm;
+}
+
+template <int BNK, bool PT>
 dli_status run_fmha_bn(const FmhaArgs& a, dli_dtype dtype, cudaStream_t stream) {
   if (dtype == DLI_DTYPE_BF16)
-    return a.head_dim == 64 ? launch_fmha<__nv_bfloat16, 64, BNK>(a, stream)
-                            : launch_fmha<__nv_bfloat16, 128, BNK>(a, stream);
-  return a.head_dim == 64 ? launch_fmha<__half, 64, BNK>(a, stream) : launch_fmha<__half, 128, BNK>(a, stream);
+    return a.head_dim == 64 ? launch_fmha<__nv_bfloat16, 64, BNK, PT>(a, stream)
+                            : launch_fmha<__nv_bfloat16, 128, BNK, PT>(a, stream);
+  return a.head_dim == 64 ? launch_fmha<__half, 64, BNK, PT>(a, stream)
+                          : launch_fmha<__half, 128, BNK, PT>(a, stream);
 }
 
 dli_status run_fmha_prefill(const FmhaArgs& a, dli_dtype dtype, cudaStream_t stream) {
-  return fmha_block_keys() == 64 ? run_fmha_bn<64>(a, dtype, stream) : run_fmha_bn<128>(a, dtype, stream);
+  if (fmha_p_in_tmem())
+    return fmha_block_keys() == 64 ? run_fmha_bn<64, true>(a, dtype, stream) : run_fmha_bn<128, true>(a, dtype, stream);
+  return fmha_block_keys() == 64 ? run_fmha_bn<64, false>(a, dtype, stream) : run_fmha_bn<128, false>(a, dtype, stream);
 }
 
 }  // namespace dli_sm100

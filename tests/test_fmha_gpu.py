@@ -1,5 +1,6 @@
 """GPU parity of the tcgen05 prefill attention kernel (k_fmha.cu): S = Q K^T and
-O in tensor memory, K/V tiles by TMA, P through shared memory.
+O in tensor memory, K/V tiles by TMA, P written back over S in tensor memory
+(default) or through a shared-memory tile (DLI_SM100_ATTN_FMHA_P=0).
 
 Every bf16/f16 prefill with head_dim 64/128 and TMA-compatible strides runs it
 (dense `attention` and `attention_kvcache` with several query rows per KV head).
@@ -132,13 +133,16 @@ print("fmha strict ok")
 """
 
 
-@pytest.mark.parametrize("block_keys", ["128", "64"])
-def test_prefill_runs_on_tcgen05_kernel(block_keys):
+@pytest.mark.parametrize("block_keys,p_tmem", [("128", "1"), ("64", "1"), ("128", "0"), ("64", "0")],
+                         ids=["bn128-ptmem", "bn64-ptmem", "bn128-psmem", "bn64-psmem"])
+def test_prefill_runs_on_tcgen05_kernel(block_keys, p_tmem):
     """DLI_SM100_ATTN_FMHA=2 turns a fallback to the mma.sync kernel into an
     error, so these shapes provably ran on the tcgen05 kernel, with 128-key
-    blocks (one CTA per SM) and with 64-key blocks (two CTAs per SM); knobs are
-    read once per process, so each runs in a child."""
-    env = dict(os.environ, DLI_SM100_ATTN_FMHA="2", DLI_SM100_ATTN_FMHA_BN=block_keys)
+    blocks (one CTA per SM) and with 64-key blocks (two CTAs per SM), P in
+    tensor memory and in shared memory; knobs are read once per process, so
+    each runs in a child."""
+    env = dict(os.environ, DLI_SM100_ATTN_FMHA="2", DLI_SM100_ATTN_FMHA_BN=block_keys,
+               DLI_SM100_ATTN_FMHA_P=p_tmem)
     here = Path(__file__).resolve().parent
     env["PYTHONPATH"] = os.pathsep.join([str(here), str(here.parent), str(Path(C.__file__).resolve().parents[1]),
                                          env.get("PYTHONPATH", "")])

@@ -430,6 +430,62 @@ def test_attention_kvcache(b, s, hq, hkv, d, cap, positions, dtype):
     assert_close(out.float(), ref, dtype, "attention_kvcache")
 
 
+_DECODE_CHILD = r"""
+import sys, torch
+import dli_sm100 as C
+cases = [(32, 1, 28, 4, 128, 2560, [(i * 997) % 2559 for i in range(32)]),
+         (32, 1, 7, 1, 128, 2560, [(i * 997) % 2559 for i in range(32)]),
+         (16, 1, 64, 8, 128, 4608, [(i * 1237) % 4607 for i in range(16)]),
+         (3, 1, 12, 2, 64, 256, [0, 1, 254]), (4, 2, 16, 4, 128, 512, [0, 63, 64, 509]),
+         (2, 1, 8, 1, 128, 200, [130, 5])]  # capacity not a multiple of the 64-key block
+outs = []
+for dtype in (torch.bfloat16, torch.float16):
+    for (b, s, hq, hkv, d, cap, positions) in cases:
+        g = torch.Generator(device="cuda").manual_seed(b * s + cap)
+        q = torch.randn(b, s, hq, d, device="cuda", generator=g).to(dtype)
+        ck = torch.randn(b, hkv, cap, d, device="cuda", generator=g).to(dtype)
+        cv = torch.randn(b, hkv, cap, d, device="cuda", generator=g).to(dtype)
+        for i, p in enumerate(positions):  # rows past each sequence: NaN
+            ck[i, :, p + s:] = float("nan")
+            cv[i, :, p + s:] = float("nan")
+        out = C.attention_kvcache(q, ck, cv, torch.tensor(positions, dtype=torch.int64, device="cuda"))
+        assert torch.isfinite(out.float()).all()
+        outs.append(out.cpu())
+C.check_device_error()
+torch.save(outs, sys.argv[1])
+print("decode child ok")
+"""
+
+
+def test_decode_cluster_tma_matches_cp_async(tmp_path):
+    """The cluster decode kernel with K/V by TMA and mbarrier stages
+    (DLI_SM100_ATTN_DECODE_TMA=1) against the cp.async form (=0, the default):
+    the same arithmetic in the same order, so the outputs are bit-identical,
+    with NaN in every cache row past a sequence (the TMA copy is not clipped to
+    the sequence; the kernel zeroes those V rows). Knobs are read once per
+    process, so each form runs in a child."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    import dli_sm100 as C
+
+    here = Path(__file__).resolve().parent
+    res = {}
+    for tma in ("1", "0"):
+        env = dict(os.environ, DLI_SM100_ATTN_DECODE_TMA=tma)
+        env["PYTHONPATH"] = os.pathsep.join([str(here), str(here.parent), str(Path(C.__file__).resolve().parents[1]),
+                                             env.get("PYTHONPATH", "")])
+        out = tmp_path / f"tma{tma}.pt"
+        r = subprocess.run([sys.executable, "-c", _DECODE_CHILD, str(out)], env=env, capture_output=True, text=True,
+                           timeout=600)
+        assert r.returncode == 0 and "decode child ok" in r.stdout, (r.stdout[-2000:], r.stderr[-3000:])
+        res[tma] = torch.load(out)
+    for a, b in zip(res["1"], res["0"]):
+        assert torch.equal(a, b)
+
+
 def test_qkv_rotary_cache_matches_oracle():
     import dli_sm100 as C
 
