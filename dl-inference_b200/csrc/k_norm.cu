@@ -4,7 +4,9 @@
 // loads and reduces sum(x^2) with warp shuffles + one smem exchange; pass 2
 // re-reads the row (an L1/L2 hit: a row is at most a few tens of KB) and writes
 // the normalised values. HBM traffic is therefore one read of x (plus delta for
-// the fused form) and one write per output, the algorithmic minimum.
+// the fused form) and one write per output, the algorithmic minimum. The
+// fp32-residual form keeps the row in registers instead (one 8-element vector
+// per thread, rows up to 8192 wide), so nothing is read twice.
 //
 // Rounding follows the reference formula (python/dli_ops/aot/rms_norm/kernel.py:11-13)
 // for fp32; for 16-bit types the normalised value is rounded to T before the
@@ -133,6 +135,49 @@ __global__ void add_rms_norm_res32_kernel(const float* residual /* may alias res
   }
 }
 
+// The same with one 8-element vector per thread (blockDim >= hidden / 8): the
+// row stays in registers between the sum of squares and the normalisation, so
+// residual, delta and weight are read once, in a single round trip, and the
+// second pass over the stored residual is gone. Same formula as above; the
+// squares are summed over another thread partition.
+template <typename T>
+__global__ void add_rms_norm_res32_reg_kernel(const float* residual /* may alias residual_out */,
+                                              const T* __restrict__ delta, const T* __restrict__ w,
+                                              T* __restrict__ out, float* residual_out, int64_t rows,
+                                              int64_t hidden, float eps) {
+  DLI_PDL_ENTRY();
+  __shared__ float scratch[32];
+  const int64_t c = static_cast<int64_t>(threadIdx.x) * 8;
+  const bool act = c < hidden;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    Vec16<T> g;
+    float ss = 0.f;
+    if (act) {
+      const Vec16<T> d = load16(delta + r * hidden + c);
+      const float4 a0 = *reinterpret_cast<const float4*>(residual + r * hidden + c);
+      const float4 a1 = *reinterpret_cast<const float4*>(residual + r * hidden + c + 4);
+      g = load16(w + c);
+      a[0] = a0.x + to_f32(d.e[0]); a[1] = a0.y + to_f32(d.e[1]); a[2] = a0.z + to_f32(d.e[2]);
+      a[3] = a0.w + to_f32(d.e[3]); a[4] = a1.x + to_f32(d.e[4]); a[5] = a1.y + to_f32(d.e[5]);
+      a[6] = a1.z + to_f32(d.e[6]); a[7] = a1.w + to_f32(d.e[7]);
+      *reinterpret_cast<float4*>(residual_out + r * hidden + c) = make_float4(a[0], a[1], a[2], a[3]);
+      *reinterpret_cast<float4*>(residual_out + r * hidden + c + 4) = make_float4(a[4], a[5], a[6], a[7]);
+      ss = a[0] * a[0] + a[1] * a[1] + a[2] * a[2] + a[3] * a[3];
+      ss += a[4] * a[4] + a[5] * a[5] + a[6] * a[6] + a[7] * a[7];
+    }
+    const float total = block_sum(ss, scratch);
+    const float inv = rsqrtf(total / static_cast<float>(hidden) + eps);
+    if (act) {
+      Vec16<T> o;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o.e[j] = from_f32<T>(round_through<T>(a[j] * inv) * to_f32(g.e[j]));
+      store16(out + r * hidden + c, o);
+    }
+    __syncthreads();  // scratch reuse by the next row
+  }
+}
+
 template <bool kFused>
 dli_status launch(const void* x, const void* delta, const void* w, void* out, void* residual_out,
                   int64_t rows, int64_t hidden, float eps, dli_dtype dtype, void* stream,
@@ -191,6 +236,20 @@ extern "C" dli_status dli_sm100_add_rms_norm_ex(const void* residual, const void
   const bool vec = hidden % 8 == 0 && aligned(residual, 32) && aligned(residual_out, 32) && aligned(delta, 16) &&
                    aligned(w, 16) && aligned(normed, 16);
   const int64_t lanes = vec ? hidden / 8 : hidden;
+  if (vec && lanes <= 1024) {  // the whole row in registers, one vector per thread
+    const int threads = static_cast<int>((lanes + 31) / 32 * 32);
+    if (dtype == DLI_DTYPE_BF16)
+      launch_pdl(add_rms_norm_res32_reg_kernel<__nv_bfloat16>, grid, threads, 0, as_stream(stream),
+                 static_cast<const float*>(residual), static_cast<const __nv_bfloat16*>(delta),
+                 static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(normed),
+                 static_cast<float*>(residual_out), rows, hidden, eps);
+    else
+      launch_pdl(add_rms_norm_res32_reg_kernel<__half>, grid, threads, 0, as_stream(stream),
+                 static_cast<const float*>(residual), static_cast<const __half*>(delta),
+                 static_cast<const __half*>(w), static_cast<__half*>(normed), static_cast<float*>(residual_out),
+                 rows, hidden, eps);
+    return check_launch(name);
+  }
   const int threads = lanes >= 512 ? 512 : (lanes >= 256 ? 256 : (lanes >= 128 ? 128 : 32));
   if (dtype == DLI_DTYPE_BF16)
     launch_pdl(add_rms_norm_res32_kernel<__nv_bfloat16>, grid, threads, 0, as_stream(stream),

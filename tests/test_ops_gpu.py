@@ -602,11 +602,13 @@ def test_rms_norm_and_fused_residual(rows, hidden, dtype):
 
 def test_add_rms_norm_fp32_residual():
     """Residual stream in float32 around bf16 tensors: residual_out = residual +
-    delta exactly in fp32; normed (bf16) against the float64 oracle."""
+    delta exactly in fp32; normed (bf16) against the float64 oracle. Rows of
+    <= 8192 (multiples of 8) run the register-resident kernel, the others the
+    two-pass one."""
     import dli_sm100 as C
 
     g = torch.Generator(device="cuda").manual_seed(9)
-    for rows, hidden in ((5, 896), (33, 3584), (3, 100)):
+    for rows, hidden in ((5, 896), (33, 3584), (3, 100), (2, 8192), (2, 8200)):
         r = torch.randn(rows, hidden, device="cuda", generator=g) * 3
         dlt = torch.randn(rows, hidden, device="cuda", generator=g).to(torch.bfloat16)
         w = (1 + 0.1 * torch.randn(hidden, device="cuda", generator=g)).to(torch.bfloat16)
