@@ -7,6 +7,7 @@
 #include <cfloat>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace dli_sm100 {
 namespace {
@@ -277,70 +278,126 @@ __global__ void softmax_kernel(const T* __restrict__ x, T* __restrict__ out, int
 }
 
 // ---- argmax -------------------------------------------------------------------------
+// (best, best_i) over columns [begin, end) of a row, indices absolute; ties keep
+// the lowest index. 16-byte loads, 4 in flight per thread, when the range
+// starts 16-byte aligned; the scalar loop takes the tail.
 template <typename T>
-__global__ void argmax_kernel(const T* __restrict__ x, int64_t* __restrict__ out, int64_t rows,
-                              int64_t width) {
-  DLI_PDL_ENTRY();
-  __shared__ float sval[32];
-  __shared__ int64_t sidx[32];
+__device__ __forceinline__ void argmax_scan(const T* row, int64_t begin, int64_t end, float& best,
+                                            int64_t& best_i) {
   constexpr int V = Vec16<T>::N;
-  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    const T* row = x + r * width;
-    float best = -INFINITY;
-    int64_t best_i = width;  // sentinel larger than any index
-    // 16-byte loads, 4 in flight per thread; the scalar loop takes the tail and
-    // rows whose start is not 16-byte aligned.
-    const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
-    const int64_t nvec = vec ? width / V : 0;
-    int64_t v0 = threadIdx.x;
-    for (; v0 + 3 * (int64_t)blockDim.x < nvec; v0 += 4 * (int64_t)blockDim.x) {
-      Vec16<T> pk[4];
+  const T* base = row + begin;
+  const int64_t len = end - begin;
+  const bool vec = (reinterpret_cast<uintptr_t>(base) & 15) == 0;
+  const int64_t nvec = vec ? len / V : 0;
+  int64_t v0 = threadIdx.x;
+  for (; v0 + 3 * (int64_t)blockDim.x < nvec; v0 += 4 * (int64_t)blockDim.x) {
+    Vec16<T> pk[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) pk[u] = load16(row + (v0 + u * (int64_t)blockDim.x) * V);
+    for (int u = 0; u < 4; ++u) pk[u] = load16(base + (v0 + u * (int64_t)blockDim.x) * V);
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-#pragma unroll
-        for (int j = 0; j < V; ++j) {
-          const float v = to_f32(pk[u].e[j]);
-          const int64_t c = (v0 + u * (int64_t)blockDim.x) * V + j;
-          if (v > best || (v == best && c < best_i)) { best = v; best_i = c; }
-        }
-    }
-    for (; v0 < nvec; v0 += blockDim.x) {
-      const Vec16<T> pk = load16(row + v0 * V);
+    for (int u = 0; u < 4; ++u)
 #pragma unroll
       for (int j = 0; j < V; ++j) {
-        const float v = to_f32(pk.e[j]);
-        const int64_t c = v0 * V + j;
+        const float v = to_f32(pk[u].e[j]);
+        const int64_t c = begin + (v0 + u * (int64_t)blockDim.x) * V + j;
         if (v > best || (v == best && c < best_i)) { best = v; best_i = c; }
       }
-    }
-    for (int64_t c = nvec * V + threadIdx.x; c < width; c += blockDim.x) {
-      const float v = to_f32(row[c]);
+  }
+  for (; v0 < nvec; v0 += blockDim.x) {
+    const Vec16<T> pk = load16(base + v0 * V);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      const float v = to_f32(pk.e[j]);
+      const int64_t c = begin + v0 * V + j;
       if (v > best || (v == best && c < best_i)) { best = v; best_i = c; }
     }
+  }
+  for (int64_t c = begin + nvec * V + threadIdx.x; c < end; c += blockDim.x) {
+    const float v = to_f32(row[c]);
+    if (v > best || (v == best && c < best_i)) { best = v; best_i = c; }
+  }
+}
+
+// Block-wide (max, lowest index); the result is valid in thread 0.
+__device__ __forceinline__ void block_argmax(float& best, int64_t& best_i, float* sval, int64_t* sidx,
+                                             int64_t sentinel) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+    if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) { sval[warp] = best; sidx[warp] = best_i; }
+  __syncthreads();
+  if (warp == 0) {
+    best = lane < nw ? sval[lane] : -INFINITY;
+    best_i = lane < nw ? sidx[lane] : sentinel;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, best, o);
       const int64_t oi = __shfl_xor_sync(0xffffffffu, best_i, o);
       if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
     }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    __syncthreads();
-    if (lane == 0) { sval[warp] = best; sidx[warp] = best_i; }
-    __syncthreads();
-    if (warp == 0) {
-      best = lane < nw ? sval[lane] : -INFINITY;
-      best_i = lane < nw ? sidx[lane] : width;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int64_t oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-        if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
-      }
-      if (lane == 0) out[r] = best_i < width ? best_i : 0;
-    }
   }
+}
+
+template <typename T>
+__global__ void argmax_kernel(const T* __restrict__ x, int64_t* __restrict__ out, int64_t rows,
+                              int64_t width) {
+  DLI_PDL_ENTRY();
+  __shared__ float sval[32];
+  __shared__ int64_t sidx[32];
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    float best = -INFINITY;
+    int64_t best_i = width;  // sentinel larger than any index
+    argmax_scan(x + r * width, 0, width, best, best_i);
+    block_argmax(best, best_i, sval, sidx, width);
+    if (threadIdx.x == 0) out[r] = best_i < width ? best_i : 0;
+  }
+}
+
+// Few long rows (greedy decoding over a vocabulary): the kArgmaxSplit CTAs of a
+// cluster scan consecutive chunks of one row (chunk lengths a multiple of 8
+// elements, so every chunk of an aligned row starts 16-byte aligned), then rank
+// 0 combines the chunks' (max, index) in rank order through distributed shared
+// memory. Chunks are in index order, so ties keep the lowest index, as above.
+constexpr int kArgmaxSplit = 8;
+
+template <typename T>
+__global__ void __launch_bounds__(512) argmax_cluster_kernel(const T* __restrict__ x, int64_t* __restrict__ out,
+                                                             int64_t width, int64_t chunk) {
+  DLI_PDL_ENTRY();
+  __shared__ float sval[32];
+  __shared__ int64_t sidx[32];
+  __shared__ float cand_v;
+  __shared__ int64_t cand_i;
+  const int64_t r = blockIdx.x;
+  const int rank = static_cast<int>(blockIdx.y);  // cluster rank (clusters span y)
+  const int64_t begin = min(width, rank * chunk), end = min(width, begin + chunk);
+  float best = -INFINITY;
+  int64_t best_i = width;
+  argmax_scan(x + r * width, begin, end, best, best_i);
+  block_argmax(best, best_i, sval, sidx, width);
+  if (threadIdx.x == 0) {
+    cand_v = best;
+    cand_i = best_i;
+  }
+  cluster_sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    const uint32_t va = smem_u32(&cand_v), ia = smem_u32(&cand_i);
+    for (int s2 = 1; s2 < kArgmaxSplit; ++s2) {
+      float v;
+      uint64_t i;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(mapa_shared(va, s2)) : "memory");
+      asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(i) : "r"(mapa_shared(ia, s2)) : "memory");
+      const int64_t ii = static_cast<int64_t>(i);
+      if (v > best || (v == best && ii < best_i)) { best = v; best_i = ii; }
+    }
+    out[r] = best_i < width ? best_i : 0;
+  }
+  cluster_sync();  // every rank's candidate stays readable until rank 0 is done
 }
 
 // ---- token select ---------------------------------------------------------------------
@@ -525,6 +582,17 @@ extern "C" dli_status dli_sm100_argmax(const void* x, int64_t* out_ids, int64_t 
                                        dli_dtype dtype, void* stream) {
   if (rows < 0 || width <= 0) return fail(DLI_ERR_INVALID_ARGUMENT, "argmax: bad sizes");
   if (rows == 0) return ok();
+  // few long rows: a cluster of CTAs per row while the clusters fit one wave
+  if (width >= 16 * 1024 && rows * kArgmaxSplit <= 2ll * sm_count() && rows <= 65535) {
+    const int64_t chunk = ceil_div(ceil_div(width, kArgmaxSplit), 8) * 8;
+    dli_status st = dispatch_float(dtype, "argmax", [&](auto tag) {
+      using T = decltype(tag);
+      launch_pdl_cluster(argmax_cluster_kernel<T>, dim3(static_cast<unsigned>(rows), kArgmaxSplit), dim3(512), 0,
+                         as_stream(stream), kArgmaxSplit, (const T*)x, out_ids, width, chunk);
+    });
+    if (st != DLI_OK) return st;
+    return check_launch("argmax");
+  }
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, sm_count() * 16));
   dli_status st = dispatch_float(dtype, "argmax", [&](auto tag) {
     using T = decltype(tag);

@@ -662,6 +662,10 @@ class LastTokenOp final : public dli::Operator {
     const Tensor& x = *in[0];
     if (x.rank() != 3) throw std::invalid_argument("last_token expects [B,S,W]");
     const std::int64_t index = attrs.value_or<std::int64_t>("index", x.dim(1) - 1);
+    if (x.dim(1) == 1 && index == 0) {  // one token per sequence (decode): a view, no copy
+      *out[0] = x.withShape({x.dim(0), x.dim(2)});
+      return;
+    }
     *out[0] = Tensor::cuda(x.dtype(), {x.dim(0), x.dim(2)}, x.deviceId());
     check(dli_sm100_select_token(dli::ptr(x), out[0]->deviceData(), x.dim(0), x.dim(1), x.dim(2), index,
                                  cdt(x.dtype()), ctx.cuda_stream),

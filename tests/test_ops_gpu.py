@@ -622,6 +622,26 @@ def test_add_rms_norm_fp32_residual():
         assert torch.equal(normed2, normed) and torch.equal(r2, resid)
 
 
+@pytest.mark.parametrize("rows,width,dtype", [(32, 152064, torch.float32), (3, 50001, torch.bfloat16),
+                                              (37, 16384, torch.float32), (40, 20000, torch.float32)])
+def test_argmax_long_rows(rows, width, dtype):
+    """Greedy-decoding argmax over a vocabulary: few long rows split over a
+    cluster of CTAs per row (the first three shapes; 40 rows take the one-CTA
+    form), against torch.argmax, with the row maximum planted twice (the lowest
+    index wins) on both sides of a chunk boundary and at the last column."""
+    import dli_sm100 as C
+
+    g = torch.Generator(device="cuda").manual_seed(rows + width)
+    x = torch.randn(rows, width, device="cuda", generator=g).to(dtype)
+    chunk = -(-(-(-width // 8)) // 8) * 8
+    x[0, chunk - 1] = 100.0
+    x[0, chunk + 5] = 100.0
+    x[1, width - 1] = 50.0
+    x[2, 3] = 7.0
+    x[2, width - 2] = 7.0
+    assert torch.equal(C.argmax(x), torch.argmax(x.float(), -1))
+
+
 def test_silu_mul_embedding_argmax_select_cast():
     import dli_sm100 as C
 
