@@ -1034,27 +1034,53 @@ __global__ void attn_fallback_kernel(const AttnArgs a) {
 }
 
 // ---- fp32 tiles on CUDA cores (the reference's dtype) -------------------------------------
-// CTA = 16 query rows of one (sequence, query head) x one split of the keys;
-// 4 warps of 4 rows each. 32-key K/V blocks are double-buffered in shared memory
-// with cp.async; lane j scores key j against the warp's 4 rows (float4 reads of
-// the padded K rows, conflict-free), the online softmax runs per row across the
-// warp (shuffle max/sum, exp2), and for O += P V each lane owns D/32 output
-// columns while the 32 probabilities are broadcast by shuffles. When the rows
-// alone cannot fill the GPU (decode), the keys are split over up to 8 CTAs of
-// a thread-block cluster whose (m, l, O) are merged through distributed shared
-// memory in rank order: exact fp32, deterministic, no workspace. Rows past a
-// sequence's keys are never loaded (cp.async zero-fills them).
-constexpr int kF32Rows = 16, kF32Keys = 32;
+// CTA = W·RW query rows of one (sequence, query head) x one split of the keys;
+// W warps of RW rows each (RW = 8 by default, 4 with DLI_SM100_ATTN_F32_RW=4;
+// W = 8 by default, 4 with DLI_SM100_ATTN_F32_WARPS=4). Eight warps give 16
+// warps per SM (two 110 KB CTAs); the kernel is bound by instruction latency, and
+// at B·H = 896, 128 x 128 causal tiles, D = 128 it takes 216 us against 249 us
+// with four warps and 319 us with four warps of four rows.
+// 32-key K/V blocks are double-buffered in shared memory with cp.async.
+//  * S = Q K^T: lane j scores key j against the warp's RW rows. Per 4-wide d step
+//    a lane reads its key's K chunk (float4; the padded rows make the 8 lanes of
+//    a phase hit distinct banks) and each row's Q chunk (a broadcast float4), so
+//    one shared-memory wavefront feeds 4·RW / (4 + RW) FMA instructions.
+//  * The online softmax runs per row across the warp (shuffle max/sum, exp2).
+//  * O += P V: each lane owns D/32 output columns. The warp's probabilities go
+//    through a small per-warp tile in shared memory ([32 keys][RW], written as
+//    float4s on conflict-free padded rows) and come back as broadcast float4s:
+//    per key one V read and RW/4 broadcasts feed RW·D/32 FMAs per lane, where a
+//    shuffle per (row, key) would bound the loop on the shuffle unit.
+//  * A warp whose rows cannot see any key of a block (causal) skips it: the
+//    skipped update would have been exact (alpha = 1, p = 0).
+// When the rows alone cannot fill the GPU (decode), the keys are split over up to
+// 8 CTAs of a thread-block cluster whose (m, l, O) are merged through distributed
+// shared memory in rank order, in the freed K/V stages: exact fp32, deterministic,
+// no workspace. Rows past a sequence's keys are never loaded (cp.async zero-fills
+// them). The row-by-key update order is the same for every W and RW, so without a
+// key split they change the launch shape, not the result bits.
+constexpr int kF32Keys = 32;
 
-template <int D>
+template <int D, int RW, int W>
 struct F32AttnSmem {
+  static_assert(RW == 4 || RW == 8, "4 or 8 query rows per warp");
+  static_assert(W == 4 || W == 8, "4 or 8 warps");
+  static constexpr int kThreads = 32 * W;
+  static constexpr int kRows = W * RW;                 // query rows per CTA
   static constexpr int kRow = D + 4;                   // padded K/V row (floats)
-  static constexpr int kQ = kF32Rows * D;              // [16][D]
+  static constexpr int kPRow = RW == 8 ? 12 : 4;       // padded P row of one key (floats)
+  static constexpr int kQ = kRows * D;                 // [kRows][D]
   static constexpr int kKV = 2 * 2 * kF32Keys * kRow;  // 2 stages x (K, V) x [32][D+4]
-  static constexpr int kState = kF32Rows * (D + 2);    // merge: O [16][D] + m, l per row
-  static constexpr int kFloats = kQ + kKV + kState;
+  static constexpr int kP = W * kF32Keys * kPRow;      // per warp [32 keys][kPRow]
+  static constexpr int kState = kRows * (D + 2);       // merge: O [kRows][D] + m, l per row
+  static_assert(kState <= kKV, "the merge state reuses the K/V stages");
+  static constexpr int kFloats = kQ + kKV + kP;
   static constexpr int kBytes = kFloats * 4;
 };
+
+// Query rows per warp and warps per CTA of the fp32 tile kernel.
+static const int kF32RowsPerWarp = tuning_knob("ATTN_F32_RW", 8) == 4 ? 4 : 8;
+static const int kF32Warps = tuning_knob("ATTN_F32_WARPS", 8) == 4 ? 4 : 8;
 
 // A lane's DL consecutive fp32 columns (DL = D/32: 2 at D=64, 4 at D=128) as
 // one 8- or 16-byte access: the address is aligned to the access width.
@@ -1078,18 +1104,20 @@ __device__ __forceinline__ void store_cols(float* p, const float* v, float scale
   }
 }
 
-template <int D>
-__global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
+template <int D, int RW, int W>
+__global__ void __launch_bounds__(32 * W, W == 8 ? 2 : 1) attn_f32_kernel(const AttnArgs a) {
   DLI_PDL_ENTRY();
-  using L = F32AttnSmem<D>;
+  using L = F32AttnSmem<D, RW, W>;
+  constexpr int kThreads = L::kThreads;
   constexpr int DL = D / 32;  // output columns per lane
+  constexpr int kRows = L::kRows;
   extern __shared__ __align__(16) float f32s[];
   float* sq = f32s;
   float* skv = f32s + L::kQ;
-  float* st = skv + L::kKV;  // [16][D] O, then m[16], l[16]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* sp = skv + L::kKV + warp * kF32Keys * L::kPRow;  // this warp's P tile
   const int split = blockIdx.x, splits = gridDim.x;
-  const int m0 = blockIdx.y * kF32Rows;
+  const int m0 = blockIdx.y * kRows;
   const int bh = blockIdx.z;
   const int h = bh % a.hq, b = bh / a.hq;
   const int kvh = h / a.group;
@@ -1100,14 +1128,14 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
   const float* vbase = static_cast<const float*>(a.v) + b * a.k_sb + kvh * a.k_sh;
 
   // Q rows (zero past the sequence)
-  for (int c = threadIdx.x; c < kF32Rows * D / 4; c += 128) {
+  for (int c = threadIdx.x; c < kRows * D / 4; c += kThreads) {
     const int r = c / (D / 4), d4 = (c % (D / 4)) * 4;
     const int qs = m0 + r;
     const float4 v = qs < a.seq_q ? *reinterpret_cast<const float4*>(qbase + static_cast<int64_t>(qs) * a.q_ss + d4)
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
     *reinterpret_cast<float4*>(sq + r * D + d4) = v;
   }
-  int n_end = a.causal ? min(kv_len, m0 + kF32Rows + off) : kv_len;
+  int n_end = a.causal ? min(kv_len, m0 + kRows + off) : kv_len;
   n_end = max(n_end, 0);
   const int nblocks = (n_end + kF32Keys - 1) / kF32Keys;
   const int b0 = static_cast<int>(static_cast<int64_t>(split) * nblocks / splits);
@@ -1118,7 +1146,7 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
     float* vt = kt + kF32Keys * L::kRow;
     const uint32_t ks = static_cast<uint32_t>(__cvta_generic_to_shared(kt));
     const uint32_t vs = static_cast<uint32_t>(__cvta_generic_to_shared(vt));
-    for (int c = threadIdx.x; c < kF32Keys * D / 4; c += 128) {
+    for (int c = threadIdx.x; c < kF32Keys * D / 4; c += kThreads) {
       const int r = c / (D / 4), d4 = (c % (D / 4)) * 4;
       const int key = blk * kF32Keys + r;
       const bool valid = key < n_end;
@@ -1129,17 +1157,19 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
     cp_async_commit();
   };
 
-  float o[4][DL];
-  float m_row[4], l_row[4];
+  float o[RW][DL];
+  float m_row[RW], l_row[RW];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < RW; ++i) {
     m_row[i] = -INFINITY;
     l_row[i] = 0.f;
 #pragma unroll
     for (int c = 0; c < DL; ++c) o[i][c] = 0.f;
   }
-  const int r_base = warp * 4;
+  const int r_base = warp * RW;
   const bool warp_rows = m0 + r_base < a.seq_q;  // the warp has at least one live row
+  // last key the warp's last row may see (causal); blocks past it are skipped
+  const int warp_key_end = m0 + r_base + RW + off;
   if (b0 < b1) load_block(b0, 0);
   for (int blk = b0; blk < b1; ++blk) {
     const int stage = (blk - b0) & 1;
@@ -1152,14 +1182,16 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
     __syncthreads();
     const float* kt = skv + stage * 2 * kF32Keys * L::kRow;
     const float* vt = kt + kF32Keys * L::kRow;
-    if (warp_rows) {
-      // scores of key (blk*32 + lane) for the warp's 4 rows
-      float sc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
+    if (warp_rows && (!a.causal || blk * kF32Keys < warp_key_end)) {
+      // scores of key (blk*32 + lane) for the warp's RW rows
+      float sc[RW];
+#pragma unroll
+      for (int i = 0; i < RW; ++i) sc[i] = 0.f;
+#pragma unroll 4
       for (int d = 0; d < D; d += 4) {
         const float4 kv = *reinterpret_cast<const float4*>(kt + lane * L::kRow + d);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < RW; ++i) {
           const float4 qv = *reinterpret_cast<const float4*>(sq + (r_base + i) * D + d);
           sc[i] = fmaf(qv.x, kv.x, sc[i]);
           sc[i] = fmaf(qv.y, kv.y, sc[i]);
@@ -1168,9 +1200,9 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
         }
       }
       const int key = blk * kF32Keys + lane;
-      float pr[4];
+      float pr[RW];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < RW; ++i) {
         const int qs = m0 + r_base + i;
         const int lim = a.causal ? min(kv_len, qs + off + 1) : kv_len;
         const float v = key < lim ? sc[i] * a.scale_log2 : -INFINITY;
@@ -1182,20 +1214,28 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
 #pragma unroll
         for (int c = 0; c < DL; ++c) o[i][c] *= alpha;
       }
+      // the lane's key row of P: [key][row], float4 stores
+#pragma unroll
+      for (int i = 0; i < RW; i += 4)
+        *reinterpret_cast<float4*>(sp + lane * L::kPRow + i) = make_float4(pr[i], pr[i + 1], pr[i + 2], pr[i + 3]);
+      __syncwarp();
       // O += P V: lane owns columns lane*DL .. lane*DL+DL-1
 #pragma unroll 4
       for (int j = 0; j < kF32Keys; ++j) {
         float vv[DL];
         load_cols<DL>(vt + j * L::kRow + lane * DL, vv);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float pj = __shfl_sync(0xffffffffu, pr[i], j);
+        for (int i4 = 0; i4 < RW; i4 += 4) {
+          const float4 p4 = *reinterpret_cast<const float4*>(sp + j * L::kPRow + i4);
+          const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
-          for (int c = 0; c < DL; ++c) o[i][c] = fmaf(pj, vv[c], o[i][c]);
+          for (int ii = 0; ii < 4; ++ii)
+#pragma unroll
+            for (int c = 0; c < DL; ++c) o[i4 + ii][c] = fmaf(pj[ii], vv[c], o[i4 + ii][c]);
         }
       }
     }
-    __syncthreads();  // the stage is refilled next iteration
+    __syncthreads();  // the stage (and the P tile) is rewritten next iteration
   }
 
   auto store_row = [&](int r, const float* vals, float inv) {
@@ -1206,15 +1246,18 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
   };
   if (splits == 1) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) store_row(r_base + i, o[i], l_row[i] > 0.f ? 1.f / l_row[i] : 0.f);
+    for (int i = 0; i < RW; ++i) store_row(r_base + i, o[i], l_row[i] > 0.f ? 1.f / l_row[i] : 0.f);
     return;
   }
-  // split-KV: publish (m, l, O) and merge across the cluster in rank order
+  // split-KV: publish (m, l, O) in the freed K/V stages (every warp passed the
+  // loop's last __syncthreads and no cp.async is in flight) and merge across the
+  // cluster in rank order
+  float* st = skv;
   float* so = st;
-  float* sm = st + kF32Rows * D;
-  float* sl = sm + kF32Rows;
+  float* sm = st + kRows * D;
+  float* sl = sm + kRows;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < RW; ++i) {
     store_cols<DL>(so + (r_base + i) * D + lane * DL, o[i], 1.f);
     if (lane == 0) {
       sm[r_base + i] = m_row[i];
@@ -1223,14 +1266,14 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
   }
   cluster_sync();
   const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(st));
-  const int rows_per = (kF32Rows + splits - 1) / splits;
-  for (int r = split * rows_per + warp; r < min(kF32Rows, (split + 1) * rows_per); r += 4) {
+  const int rows_per = (kRows + splits - 1) / splits;
+  for (int r = split * rows_per + warp; r < min(kRows, (split + 1) * rows_per); r += W) {
     float mm = -INFINITY;
     for (int s = 0; s < splits; ++s) {
       float v;
       asm volatile("ld.shared::cluster.f32 %0, [%1];"
                    : "=f"(v)
-                   : "r"(mapa_shared(base + static_cast<uint32_t>((kF32Rows * D + r) * 4), s))
+                   : "r"(mapa_shared(base + static_cast<uint32_t>((kRows * D + r) * 4), s))
                    : "memory");
       mm = fmaxf(mm, v);
     }
@@ -1241,11 +1284,11 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
       float ms, ls;
       asm volatile("ld.shared::cluster.f32 %0, [%1];"
                    : "=f"(ms)
-                   : "r"(mapa_shared(base + static_cast<uint32_t>((kF32Rows * D + r) * 4), s))
+                   : "r"(mapa_shared(base + static_cast<uint32_t>((kRows * D + r) * 4), s))
                    : "memory");
       asm volatile("ld.shared::cluster.f32 %0, [%1];"
                    : "=f"(ls)
-                   : "r"(mapa_shared(base + static_cast<uint32_t>((kF32Rows * D + kF32Rows + r) * 4), s))
+                   : "r"(mapa_shared(base + static_cast<uint32_t>((kRows * D + kRows + r) * 4), s))
                    : "memory");
       const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - mm);
       ll += ls * w;
@@ -1264,13 +1307,13 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(const AttnArgs a) {
   cluster_sync();  // every rank's shared memory stays alive until all reads are done
 }
 
-template <int D>
-dli_status launch_attn_f32(const AttnArgs& args, cudaStream_t stream) {
-  using L = F32AttnSmem<D>;
-  auto kern = attn_f32_kernel<D>;
+template <int D, int RW, int W>
+dli_status launch_attn_f32_rw(const AttnArgs& args, cudaStream_t stream) {
+  using L = F32AttnSmem<D, RW, W>;
+  auto kern = attn_f32_kernel<D, RW, W>;
   const dli_status st = ensure_smem(reinterpret_cast<const void*>(kern), L::kBytes, "attention fp32");
   if (st != DLI_OK) return st;
-  const int64_t tiles = ceil_div(args.seq_q, kF32Rows);
+  const int64_t tiles = ceil_div(args.seq_q, L::kRows);
   const int64_t rows = tiles * args.batch * args.hq;
   const int64_t blocks = ceil_div(args.seq_k, kF32Keys);
   // split the keys when the row tiles alone leave SMs idle (two CTAs per SM)
@@ -1279,7 +1322,7 @@ dli_status launch_attn_f32(const AttnArgs& args, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(splits), static_cast<unsigned>(tiles),
                      static_cast<unsigned>(static_cast<int64_t>(args.batch) * args.hq));
-  cfg.blockDim = dim3(128);
+  cfg.blockDim = dim3(L::kThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -1300,6 +1343,13 @@ dli_status launch_attn_f32(const AttnArgs& args, cudaStream_t stream) {
   cfg.numAttrs = n;
   cudaLaunchKernelEx(&cfg, kern, args);
   return check_launch("attention fp32");
+}
+
+template <int D>
+dli_status launch_attn_f32(const AttnArgs& args, cudaStream_t stream) {
+  if (kF32Warps == 8)
+    return kF32RowsPerWarp == 4 ? launch_attn_f32_rw<D, 4, 8>(args, stream) : launch_attn_f32_rw<D, 8, 8>(args, stream);
+  return kF32RowsPerWarp == 4 ? launch_attn_f32_rw<D, 4, 4>(args, stream) : launch_attn_f32_rw<D, 8, 4>(args, stream);
 }
 
 // ---- fp32 decode: few query rows per KV head ---------------------------------------
@@ -1550,7 +1600,7 @@ dli_status run_attn_f32_decode(const AttnArgs& a, cudaStream_t stream) {
 bool f32_attention_ok(const AttnArgs& a) {
   static const bool on = tuning_knob("ATTN_F32", 1) != 0;
   if (!on || (a.head_dim != 64 && a.head_dim != 128)) return false;
-  if (static_cast<int64_t>(a.batch) * a.hq > 65535 || ceil_div(a.seq_q, kF32Rows) > 65535) return false;
+  if (static_cast<int64_t>(a.batch) * a.hq > 65535 || ceil_div(a.seq_q, 4 * kF32RowsPerWarp) > 65535) return false;
   for (const void* ptr : {a.q, a.k, a.v, static_cast<const void*>(a.out)})
     if (!aligned(ptr, 16)) return false;
   for (int64_t s : {a.q_sb, a.q_sh, a.q_ss, a.o_sb, a.o_sh, a.o_ss, a.k_sb, a.k_sh})

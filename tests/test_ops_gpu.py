@@ -356,9 +356,10 @@ def test_attention_dense(b, hq, hkv, sq, sk, d, causal, dtype):
 
 @pytest.mark.parametrize("b,hq,hkv,sq,sk,d,causal", [
     (1, 1, 1, 1, 2048, 128, True), (1, 1, 1, 1, 517, 64, True), (2, 4, 4, 128, 128, 128, True),
-    (1, 6, 2, 77, 300, 64, False), (3, 8, 1, 33, 33, 128, True), (2, 2, 2, 5, 1000, 128, True)])
+    (1, 6, 2, 77, 300, 64, False), (3, 8, 1, 33, 33, 128, True), (2, 2, 2, 5, 1000, 128, True),
+    (1, 4, 2, 200, 260, 128, True), (2, 3, 1, 150, 150, 64, True)])
 def test_attention_fp32_tiles(b, hq, hkv, sq, sk, d, causal):
-    """The fp32 attention kernel (16-row tiles, split-KV merged in a cluster for
+    """The fp32 attention kernel (64-row tiles, split-KV merged in a cluster for
     decode-sized rows) at the reference's dtype: rel-err <= 1e-4 against the oracle."""
     import dli_sm100 as C
 
