@@ -207,6 +207,55 @@ def cpu_baseline(shape, batch: int, prompt: int, seconds: float = 20.0) -> dict:
             "ms_per_step": step_s * 1e3}
 
 
+def cpu_prefill(shape, prompt: int, seconds: float = 5.0) -> dict:
+    """Times the prefill half of the reference's CPU path: transformers' Qwen2
+    (eager, bf16) runs ONE decoder layer of the named shape over one full
+    `prompt`-token sequence with the causal mask, repeated within `seconds`
+    (at least once, after a short warm-up), plus the LM head on the last token; scaled to the full
+    model. The host cores are busy with one sequence already, so a batch of B
+    sequences takes B times as long and the rate is tokens per second either way."""
+    import torch
+    from transformers import Qwen2Config
+    from transformers.models.qwen2.modeling_qwen2 import Qwen2DecoderLayer, Qwen2RotaryEmbedding
+
+    threads = torch.get_num_threads()
+    cfg = Qwen2Config(vocab_size=shape.vocab, hidden_size=shape.hidden,
+                      intermediate_size=shape.intermediate, num_hidden_layers=1,
+                      num_attention_heads=shape.q_heads, num_key_value_heads=shape.kv_heads,
+                      max_position_embeddings=prompt + 64, rms_norm_eps=shape.rms_eps,
+                      rope_theta=shape.rope_theta, attn_implementation="eager")
+    torch.manual_seed(1)
+    with torch.no_grad():
+        layer = Qwen2DecoderLayer(cfg, 0).to(torch.bfloat16).eval()
+        for p in layer.parameters():
+            p.normal_(0, 0.02)
+        rot = Qwen2RotaryEmbedding(cfg)
+        lm = torch.randn(shape.vocab, shape.hidden, dtype=torch.bfloat16) * 0.02
+        x = torch.randn(1, prompt, shape.hidden, dtype=torch.bfloat16)
+        pos = torch.arange(prompt, dtype=torch.int64)[None]
+        emb = rot(x, pos)
+        mask = torch.full((prompt, prompt), float("-inf")).triu(1)[None, None].to(torch.bfloat16)
+        n0 = min(prompt, 64)  # untimed warm-up on a short prefix
+        layer(x[:, :n0], attention_mask=mask[..., :n0, :n0], position_ids=pos[:, :n0],
+              position_embeddings=tuple(e[:, :n0] for e in emb))
+        reps, t_layer = 0, 0.0
+        start = time.perf_counter()
+        while reps < 1 or time.perf_counter() - start < seconds:
+            t0 = time.perf_counter()
+            layer(x, attention_mask=mask, position_ids=pos, position_embeddings=emb)
+            t_layer += time.perf_counter() - t0
+            reps += 1
+        t0 = time.perf_counter()
+        torch.nn.functional.linear(x[:, -1], lm)
+        t_head = time.perf_counter() - t0
+    seq_s = shape.layers * (t_layer / reps) + t_head
+    return {"value": prompt / seq_s, "unit": "tok/s (prefill)", "cores": threads, "kind": "reference",
+            "ms_per_sequence": seq_s * 1e3,
+            "sample": (f"transformers Qwen2 eager bf16 on {threads} host threads: {reps} causal forwards of "
+                       f"1 of {shape.layers} decoder layers over one {prompt}-token sequence + LM head of the "
+                       f"last token, scaled x{shape.layers} layers")}
+
+
 def workload_config(model: str, batch: int, prompt: int, dsteps: int) -> dict:
     """The `config` keys both arms report for the same workload."""
     return {"workload": f"qwen2-{model}: prefill {batch}x{prompt} + {dsteps} greedy decode steps",
@@ -425,6 +474,7 @@ def run_reference_arm(args, world: int, rank: int):
         if i >= args.warmup:
             vals.append(r)
     value = statistics.median(v["value"] for v in vals)
+    pre = cpu_prefill(shape, prompt)  # once per run: the decode steps above carry the timing contract
     line = {"metric": METRIC, "impl": "reference", "value": value, "unit": "tok/s (decode)",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": statistics.median(v["ms_per_step"] for v in vals),
@@ -433,6 +483,8 @@ def run_reference_arm(args, world: int, rank: int):
             "config": workload_config(args.model, batch, prompt, dsteps) | {
                 "parallelism": "none (host cores)",
                 "reference_sample": f"decode at a {prompt}-token context, one decoder layer timed and scaled"},
+            "prefill": {"value": pre["value"], "unit": pre["unit"], "ms_per_sequence": pre["ms_per_sequence"],
+                        "sample": pre["sample"]},
             "cpu_baseline": {k: vals[-1][k] for k in ("kind", "cores", "sample")} | {"value": value,
                                                                                      "unit": "tok/s (decode)"},
             "e2e": {"value": value, "unit": "tok/s (decode)", "h2d_bytes_per_step": 0,
@@ -640,6 +692,7 @@ def main() -> int:
         try:
             cpu = cpu_baseline(shape, total_seqs, prompt, seconds=20.0)
             cpu.pop("ms_per_step", None)
+            cpu["prefill"] = cpu_prefill(shape, prompt)
         except Exception as exc:  # report, do not fail the GPU measurement
             cpu = {"value": None, "unit": "tok/s (decode)", "cores": os.cpu_count(), "kind": "reference",
                    "sample": f"failed: {exc!r}"[:200]}
