@@ -1041,11 +1041,17 @@ __global__ void attn_fallback_kernel(const AttnArgs a) {
 // at B·H = 896, 128 x 128 causal tiles, D = 128 it takes 216 us against 249 us
 // with four warps and 319 us with four warps of four rows.
 // 32-key K/V blocks are double-buffered in shared memory with cp.async.
-//  * S = Q K^T: lane j scores key j against the warp's RW rows. Per 4-wide d step
-//    a lane reads its key's K chunk (float4; the padded rows make the 8 lanes of
-//    a phase hit distinct banks) and each row's Q chunk (a broadcast float4), so
-//    one shared-memory wavefront feeds 4·RW / (4 + RW) FMA instructions.
-//  * The online softmax runs per row across the warp (shuffle max/sum, exp2).
+//  * S = Q K^T, RW = 8: lane (g, c) = (lane / 8, lane % 8) scores rows 2g, 2g+1 of
+//    the warp against keys c, c+8, c+16, c+24 of the block. Per 4-wide d step a
+//    lane reads 2 Q and 4 K float4s for 32 FMAs; Q and K rows are padded by 4
+//    floats, so each half-warp's reads hit distinct banks and every read takes 2
+//    wavefronts: 12 per 32 FMAs, where one key per lane against 8 broadcast rows
+//    took 20 (a broadcast float4 also costs 2). The row max and sum reduce over
+//    the 8 lanes of a group and reach the other lanes by shuffles.
+//    RW = 4: lane j scores key j against the warp's 4 rows, max and sum reduce
+//    over the warp.
+//  * The online softmax state (m, l) of every row of the warp is held by every
+//    lane.
 //  * O += P V: each lane owns D/32 output columns. The warp's probabilities go
 //    through a small per-warp tile in shared memory ([32 keys][RW], written as
 //    float4s on conflict-free padded rows) and come back as broadcast float4s:
@@ -1057,8 +1063,8 @@ __global__ void attn_fallback_kernel(const AttnArgs a) {
 // 8 CTAs of a thread-block cluster whose (m, l, O) are merged through distributed
 // shared memory in rank order, in the freed K/V stages: exact fp32, deterministic,
 // no workspace. Rows past a sequence's keys are never loaded (cp.async zero-fills
-// them). The row-by-key update order is the same for every W and RW, so without a
-// key split they change the launch shape, not the result bits.
+// them). The launch shape (W, RW) changes where rows are split and the order in
+// which a block's probabilities are summed, both within fp32 rounding.
 constexpr int kF32Keys = 32;
 
 template <int D, int RW, int W>
@@ -1069,7 +1075,8 @@ struct F32AttnSmem {
   static constexpr int kRows = W * RW;                 // query rows per CTA
   static constexpr int kRow = D + 4;                   // padded K/V row (floats)
   static constexpr int kPRow = RW == 8 ? 12 : 4;       // padded P row of one key (floats)
-  static constexpr int kQ = kRows * D;                 // [kRows][D]
+  static constexpr int kQRow = D + 4;                  // padded Q row (floats)
+  static constexpr int kQ = kRows * kQRow;             // [kRows][D+4]
   static constexpr int kKV = 2 * 2 * kF32Keys * kRow;  // 2 stages x (K, V) x [32][D+4]
   static constexpr int kP = W * kF32Keys * kPRow;      // per warp [32 keys][kPRow]
   static constexpr int kState = kRows * (D + 2);       // merge: O [kRows][D] + m, l per row
@@ -1133,7 +1140,7 @@ __global__ void __launch_bounds__(32 * W, W == 8 ? 2 : 1) attn_f32_kernel(const 
     const int qs = m0 + r;
     const float4 v = qs < a.seq_q ? *reinterpret_cast<const float4*>(qbase + static_cast<int64_t>(qs) * a.q_ss + d4)
                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-    *reinterpret_cast<float4*>(sq + r * D + d4) = v;
+    *reinterpret_cast<float4*>(sq + r * L::kQRow + d4) = v;
   }
   int n_end = a.causal ? min(kv_len, m0 + kRows + off) : kv_len;
   n_end = max(n_end, 0);
@@ -1183,41 +1190,121 @@ __global__ void __launch_bounds__(32 * W, W == 8 ? 2 : 1) attn_f32_kernel(const 
     const float* kt = skv + stage * 2 * kF32Keys * L::kRow;
     const float* vt = kt + kF32Keys * L::kRow;
     if (warp_rows && (!a.causal || blk * kF32Keys < warp_key_end)) {
-      // scores of key (blk*32 + lane) for the warp's RW rows
-      float sc[RW];
+      if constexpr (RW == 8) {
+        // S for rows 2g, 2g+1 x keys c + 8j of the block
+        const int g = lane >> 3, c = lane & 7;
+        float sc[2][4];
 #pragma unroll
-      for (int i = 0; i < RW; ++i) sc[i] = 0.f;
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) sc[t][j] = 0.f;
+        const float* q0 = sq + (r_base + 2 * g) * L::kQRow;
 #pragma unroll 4
-      for (int d = 0; d < D; d += 4) {
-        const float4 kv = *reinterpret_cast<const float4*>(kt + lane * L::kRow + d);
+        for (int d = 0; d < D; d += 4) {
+          const float4 qa = *reinterpret_cast<const float4*>(q0 + d);
+          const float4 qb = *reinterpret_cast<const float4*>(q0 + L::kQRow + d);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 kv = *reinterpret_cast<const float4*>(kt + (c + 8 * j) * L::kRow + d);
+            sc[0][j] = fmaf(qa.x, kv.x, sc[0][j]);
+            sc[0][j] = fmaf(qa.y, kv.y, sc[0][j]);
+            sc[0][j] = fmaf(qa.z, kv.z, sc[0][j]);
+            sc[0][j] = fmaf(qa.w, kv.w, sc[0][j]);
+            sc[1][j] = fmaf(qb.x, kv.x, sc[1][j]);
+            sc[1][j] = fmaf(qb.y, kv.y, sc[1][j]);
+            sc[1][j] = fmaf(qb.z, kv.z, sc[1][j]);
+            sc[1][j] = fmaf(qb.w, kv.w, sc[1][j]);
+          }
+        }
+        // masked, scaled scores and each row's block maximum over its 8-lane group
+        float gmax[2];
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int qs = m0 + r_base + 2 * g + t;
+          const int lim = a.causal ? min(kv_len, qs + off + 1) : kv_len;
+          gmax[t] = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int key = blk * kF32Keys + c + 8 * j;
+            sc[t][j] = key < lim ? sc[t][j] * a.scale_log2 : -INFINITY;
+            gmax[t] = fmaxf(gmax[t], sc[t][j]);
+          }
+#pragma unroll
+          for (int x = 1; x < 8; x <<= 1) gmax[t] = fmaxf(gmax[t], __shfl_xor_sync(0xffffffffu, gmax[t], x));
+        }
+        // every lane: new maxima and rescale factors of all 8 rows
+        float mown[2];
 #pragma unroll
         for (int i = 0; i < RW; ++i) {
-          const float4 qv = *reinterpret_cast<const float4*>(sq + (r_base + i) * D + d);
-          sc[i] = fmaf(qv.x, kv.x, sc[i]);
-          sc[i] = fmaf(qv.y, kv.y, sc[i]);
-          sc[i] = fmaf(qv.z, kv.z, sc[i]);
-          sc[i] = fmaf(qv.w, kv.w, sc[i]);
+          const float bm = __shfl_sync(0xffffffffu, gmax[i & 1], (i >> 1) * 8);
+          const float mnew = fmaxf(m_row[i], bm);
+          const float alpha = mnew == -INFINITY ? 1.f : exp2f(m_row[i] - mnew);
+          l_row[i] *= alpha;
+          m_row[i] = mnew;
+#pragma unroll
+          for (int cc = 0; cc < DL; ++cc) o[i][cc] *= alpha;
         }
+        // the lane's own rows' maxima (the same values as m_row[2g + t])
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          float mt = m_row[t];
+#pragma unroll
+          for (int gg = 1; gg < 4; ++gg) mt = g == gg ? m_row[2 * gg + t] : mt;
+          mown[t] = mt;
+        }
+        // probabilities, written as [key][row] pairs, and each row's block sum
+        float gsum[2] = {0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float p0 = mown[0] == -INFINITY ? 0.f : exp2f(sc[0][j] - mown[0]);
+          const float p1 = mown[1] == -INFINITY ? 0.f : exp2f(sc[1][j] - mown[1]);
+          gsum[0] += p0;
+          gsum[1] += p1;
+          *reinterpret_cast<float2*>(sp + (c + 8 * j) * L::kPRow + 2 * g) = make_float2(p0, p1);
+        }
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+          for (int x = 1; x < 8; x <<= 1) gsum[t] += __shfl_xor_sync(0xffffffffu, gsum[t], x);
+#pragma unroll
+        for (int i = 0; i < RW; ++i) l_row[i] += __shfl_sync(0xffffffffu, gsum[i & 1], (i >> 1) * 8);
+      } else {
+        // scores of key (blk*32 + lane) for the warp's RW rows
+        float sc[RW];
+#pragma unroll
+        for (int i = 0; i < RW; ++i) sc[i] = 0.f;
+#pragma unroll 4
+        for (int d = 0; d < D; d += 4) {
+          const float4 kv = *reinterpret_cast<const float4*>(kt + lane * L::kRow + d);
+#pragma unroll
+          for (int i = 0; i < RW; ++i) {
+            const float4 qv = *reinterpret_cast<const float4*>(sq + (r_base + i) * L::kQRow + d);
+            sc[i] = fmaf(qv.x, kv.x, sc[i]);
+            sc[i] = fmaf(qv.y, kv.y, sc[i]);
+            sc[i] = fmaf(qv.z, kv.z, sc[i]);
+            sc[i] = fmaf(qv.w, kv.w, sc[i]);
+          }
+        }
+        const int key = blk * kF32Keys + lane;
+        float pr[RW];
+#pragma unroll
+        for (int i = 0; i < RW; ++i) {
+          const int qs = m0 + r_base + i;
+          const int lim = a.causal ? min(kv_len, qs + off + 1) : kv_len;
+          const float v = key < lim ? sc[i] * a.scale_log2 : -INFINITY;
+          const float mnew = fmaxf(m_row[i], warp_max(v));
+          const float alpha = mnew == -INFINITY ? 1.f : exp2f(m_row[i] - mnew);
+          pr[i] = mnew == -INFINITY ? 0.f : exp2f(v - mnew);
+          l_row[i] = l_row[i] * alpha + warp_sum(pr[i]);
+          m_row[i] = mnew;
+#pragma unroll
+          for (int cc = 0; cc < DL; ++cc) o[i][cc] *= alpha;
+        }
+        // the lane's key row of P: [key][row], float4 stores
+#pragma unroll
+        for (int i = 0; i < RW; i += 4)
+          *reinterpret_cast<float4*>(sp + lane * L::kPRow + i) = make_float4(pr[i], pr[i + 1], pr[i + 2], pr[i + 3]);
       }
-      const int key = blk * kF32Keys + lane;
-      float pr[RW];
-#pragma unroll
-      for (int i = 0; i < RW; ++i) {
-        const int qs = m0 + r_base + i;
-        const int lim = a.causal ? min(kv_len, qs + off + 1) : kv_len;
-        const float v = key < lim ? sc[i] * a.scale_log2 : -INFINITY;
-        const float mnew = fmaxf(m_row[i], warp_max(v));
-        const float alpha = mnew == -INFINITY ? 1.f : exp2f(m_row[i] - mnew);
-        pr[i] = mnew == -INFINITY ? 0.f : exp2f(v - mnew);
-        l_row[i] = l_row[i] * alpha + warp_sum(pr[i]);
-        m_row[i] = mnew;
-#pragma unroll
-        for (int c = 0; c < DL; ++c) o[i][c] *= alpha;
-      }
-      // the lane's key row of P: [key][row], float4 stores
-#pragma unroll
-      for (int i = 0; i < RW; i += 4)
-        *reinterpret_cast<float4*>(sp + lane * L::kPRow + i) = make_float4(pr[i], pr[i + 1], pr[i + 2], pr[i + 3]);
       __syncwarp();
       // O += P V: lane owns columns lane*DL .. lane*DL+DL-1
 #pragma unroll 4
