@@ -62,12 +62,13 @@ def _attn_prefill(b=2, hq=28, hkv=4, d=128, s=2048):
     return (lambda: C.attention_kvcache(q, ck, cv, pos)), 2 * b * s * d * 2 * (hq + 2 * hkv), flops
 
 
-def _attn_f32(bh=896, s=128, d=128):
-    # the reference attention kernel's multi-row shape in its own dtype (fp32, causal)
-    q = torch.randn(1, bh, s, d, device="cuda")
-    k = torch.randn(1, bh, s, d, device="cuda")
-    v = torch.randn(1, bh, s, d, device="cuda")
-    return (lambda: C.attention(q, k, v, causal=True)), 4 * 4 * bh * s * d, 2.0 * bh * d * s * (s + 1)
+def _attn_f32(bh=896, sq=128, sk=128, d=128):
+    # the reference attention kernel's shapes in its own dtype (fp32, bottom-right causal)
+    q = torch.randn(1, bh, sq, d, device="cuda")
+    k = torch.randn(1, bh, sk, d, device="cuda")
+    v = torch.randn(1, bh, sk, d, device="cuda")
+    visible = sq * (sk - sq) + sq * (sq + 1) // 2  # keys seen, summed over the query rows
+    return (lambda: C.attention(q, k, v, causal=True)), 4 * bh * d * (2 * sq + 2 * sk), 4.0 * bh * d * visible
 
 
 CASES = {
@@ -88,6 +89,7 @@ CASES = {
     "attn_prefill_b32": lambda: _attn_prefill(b=32, s=2048),          # the benchmark's prefill launch
     "attn_prefill_0_5b": lambda: _attn_prefill(b=8, hq=14, hkv=2, d=64, s=512),
     "attn_f32_tiles": _attn_f32,
+    "attn_f32_decode": lambda: _attn_f32(sq=1, sk=2048),   # one query row per head: HBM-bound
 }
 
 
