@@ -2080,6 +2080,16 @@ int query_occupancy(int smem_bytes, int cluster) {
   return n;
 }
 
+// Rings of the fp32 split kernel at tile width 32: two raw and two converted
+// stages (default), so the converter warps split K block k+1 while the MMAs of
+// block k still read theirs; DLI_SM100_GEMM_F32X3_CS=1 keeps three raw stages
+// and one converted stage, where each block's conversion waited for the
+// previous block's MMAs. Wider tiles fit only one converted stage.
+bool f32x3_two_cv_stages() {
+  static const bool two = tuning_knob("GEMM_F32X3_CS", 2) != 1;
+  return two;
+}
+
 int layout_bytes(int bn, int stages) {
   switch (bn * 100 + stages) {
     case 3204: return TcLayout<32, 4>::kBytes;
@@ -2089,7 +2099,7 @@ int layout_bytes(int bn, int stages) {
     case 12806: return TcLayout<128, 6>::kBytes;
     case 25604: return TcLayout<256, 4>::kBytes;
     // stages 0: the fp32 split-bf16 kernel's rings at that tile width
-    case 3200: return F32x3Layout<32, 3, 1>::kBytes;
+    case 3200: return f32x3_two_cv_stages() ? F32x3Layout<32, 2, 2>::kBytes : F32x3Layout<32, 3, 1>::kBytes;
     case 6400: return F32x3Layout<64, 3, 1>::kBytes;
     case 12800: return F32x3Layout<128, 2, 1>::kBytes;
     default: return 0;
@@ -2393,7 +2403,10 @@ bool try_gemm_f32x3(const void* a, const void* b, const void* bias, void* out, i
   p.bias_f32 = 1;
   p.b_mn = b_mn ? 1 : 0;
   switch (bn) {
-    case 32: *status = launch_f32x3<32, 3, 1>(ma, mb, p, plan.splits, stream); break;
+    case 32:
+      *status = f32x3_two_cv_stages() ? launch_f32x3<32, 2, 2>(ma, mb, p, plan.splits, stream)
+                                      : launch_f32x3<32, 3, 1>(ma, mb, p, plan.splits, stream);
+      break;
     case 64: *status = launch_f32x3<64, 3, 1>(ma, mb, p, plan.splits, stream); break;
     default: *status = launch_f32x3<128, 2, 1>(ma, mb, p, plan.splits, stream); break;
   }
