@@ -37,7 +37,11 @@
 // the softmax warps wait for it before they rescale O (and, with P in shared
 // memory, before they rewrite the single P tile). A P in tensor memory needs
 // no such wait: P_j sits in S_j's buffer, and S_{j+2}, the next write there,
-// is issued after P_j V_j, which the tensor pipe executes first.
+// is issued after P_j V_j, which the tensor pipe executes first. A rescale at
+// block j may wait on o_done's parity because S_j's commit already covered
+// P V_{j-2}, so o_done is at most one phase behind; before the final read of
+// O it may be two behind, so that read waits on mma_done, committed once after
+// the last MMA.
 //
 // Keys at or past a sequence's length are masked; V rows past the length that
 // exist in memory (stale cache rows) are zeroed in shared memory before the
@@ -464,8 +468,13 @@ __global__ void __launch_bounds__(kFmhaThreads, FmhaLayout<D, BNK, PT>::kCtasPer
     // TMA (rows past the sequence are outside the map and are not written).
     // Every softmax warp takes this path, abort or not, so the named barrier
     // below always completes.
+    // Every MMA must have finished before O is read. The wait is on mma_done (one
+    // phase, committed by the MMA thread after its last issue, abort included),
+    // not on o_done: with P in tensor memory nothing here has waited for P V of
+    // block nblocks-2, so o_done may still be two phases behind, and a parity
+    // wait for phase nblocks-1 would then pass at once.
     bool have_o = ok && nblocks > 0;
-    if (have_o && !warp_wait(o_done, (nblocks - 1) & 1, abort_flag)) {
+    if (have_o && !warp_wait(mma_done, 0, abort_flag)) {
       if (lane == 0) set_device_error(p.err, kDevErrAttentionTimeout);
       have_o = false;
     }
